@@ -1,0 +1,514 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces the `stablehlo.dot_general` dispatches that Sheaf's `@` lowers to
+// (lowering/stablehlo/dot_ops.rs:12-229) and the two GEMMs of its VJP
+// (autodiff/reverse.rs:585-689: dA = adj @ swapaxes(B), dB = swapaxes(A) @ adj,
+// followed by the batch reduction of maybe_unbroadcast, reverse.rs:360-376).
+// The weight gradient is contracted over all B*T tokens in one GEMM (split-K
+// across CTAs) instead of B per-batch partial products plus a reduce.
+//
+// Kernel structure (one CTA per SM, persistent over output tiles):
+//   warp 0     : TMA producer (one elected lane), STAGES-deep smem ring
+//   warp 1     : TMEM allocator + single-thread UMMA issuer (M=128, N=BN, K=16)
+//   warps 2..5 : epilogue; warp w reads TMEM lanes 32*(w%4)..+31, i.e. one
+//                accumulator row per thread, applies the fused epilogue and
+//                stores to global memory.
+// Accumulators are double-buffered in TMEM (2*BN columns) so the epilogue of
+// tile i overlaps the main loop of tile i+1.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "sb_kernels.h"
+#include "sb_ptx.cuh"
+
+namespace sb {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
+constexpr uint32_t kABytes = kBM * kBK * 2;
+
+struct GemmArgs {
+  int M, N, K;
+  int m_tiles, n_tiles;
+  int splits, kb_per_split, kb_total;
+  int epi;
+  void* out;
+  long ldo;
+  int out_f32;
+  const void* aux;
+  long ldaux;
+  int aux_f32;
+  void* out2;
+  long ldo2;
+  long split_stride;  // elements between split-K partial slices (f32 workspace)
+  int vec_ok;         // 16-byte vector stores are aligned for every full chunk
+  int* err;
+};
+
+__device__ __forceinline__ float gelu_fwd(float x) {
+  // 0.5 * (x * (1 + tanh(0.7978846 * (x + 0.044715 * (x * (x * x))))))   (lib/nn.shf:10-11)
+  float inner = x + 0.044715f * (x * (x * x));
+  return 0.5f * (x * (1.0f + tanhf(0.7978846f * inner)));
+}
+
+__device__ __forceinline__ float gelu_grad(float x) {
+  // d/dx of gelu_fwd by the chain rule of its primitive ops.
+  float x2 = x * x;
+  float t = tanhf(0.7978846f * (x + 0.044715f * (x * x2)));
+  return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * 0.7978846f * (1.0f + 0.134145f * x2);
+}
+
+__device__ __forceinline__ float ld_elem(const void* p, long idx, int is_f32) {
+  if (is_f32) return static_cast<const float*>(p)[idx];
+  return bf16_bits_to_f32(static_cast<const uint16_t*>(p)[idx]);
+}
+
+__device__ __forceinline__ void st_elem(void* p, long idx, int is_f32, float v) {
+  if (is_f32)
+    static_cast<float*>(p)[idx] = v;
+  else
+    static_cast<__nv_bfloat16*>(p)[idx] = __float2bfloat16_rn(v);
+}
+
+// Stores 32 consecutive accumulator columns [col0, col0+32) of one row.
+__device__ __forceinline__ void epilogue_row32(const GemmArgs& a, int row, int col0, const uint32_t (&v)[32],
+                                               int split) {
+  if (row >= a.M) return;
+  float f[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+  const bool full = (col0 + 32 <= a.N) && a.vec_ok;
+
+  if (a.epi == EPI_STORE) {
+    if (a.out_f32) {
+      float* o = static_cast<float*>(a.out) + split * a.split_stride + static_cast<long>(row) * a.ldo + col0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+      } else {
+        for (int j = 0; j < 32 && col0 + j < a.N; ++j) o[j] = f[j];
+      }
+    } else {
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + static_cast<long>(row) * a.ldo + col0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 pk = make_uint4(pack_bf16x2(f[j], f[j + 1]), pack_bf16x2(f[j + 2], f[j + 3]),
+                                pack_bf16x2(f[j + 4], f[j + 5]), pack_bf16x2(f[j + 6], f[j + 7]));
+          *reinterpret_cast<uint4*>(o + j) = pk;
+        }
+      } else {
+        for (int j = 0; j < 32 && col0 + j < a.N; ++j) o[j] = __float2bfloat16_rn(f[j]);
+      }
+    }
+  } else if (a.epi == EPI_ADD) {
+    // f32 residual stream: out = aux + acc (aux may alias out).
+    const float* x = static_cast<const float*>(a.aux) + static_cast<long>(row) * a.ldaux + col0;
+    float* o = static_cast<float*>(a.out) + static_cast<long>(row) * a.ldo + col0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 r = *reinterpret_cast<const float4*>(x + j);
+        *reinterpret_cast<float4*>(o + j) = make_float4(r.x + f[j], r.y + f[j + 1], r.z + f[j + 2], r.w + f[j + 3]);
+      }
+    } else {
+      for (int j = 0; j < 32 && col0 + j < a.N; ++j) o[j] = x[j] + f[j];
+    }
+  } else if (a.epi == EPI_GELU) {
+    __nv_bfloat16* u = static_cast<__nv_bfloat16*>(a.out) + static_cast<long>(row) * a.ldo + col0;
+    __nv_bfloat16* g = static_cast<__nv_bfloat16*>(a.out2) + static_cast<long>(row) * a.ldo2 + col0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        float ur[8], gr[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          ur[t] = __bfloat162float(__float2bfloat16_rn(f[j + t]));
+          gr[t] = gelu_fwd(ur[t]);
+        }
+        *reinterpret_cast<uint4*>(u + j) = make_uint4(pack_bf16x2(ur[0], ur[1]), pack_bf16x2(ur[2], ur[3]),
+                                                      pack_bf16x2(ur[4], ur[5]), pack_bf16x2(ur[6], ur[7]));
+        *reinterpret_cast<uint4*>(g + j) = make_uint4(pack_bf16x2(gr[0], gr[1]), pack_bf16x2(gr[2], gr[3]),
+                                                      pack_bf16x2(gr[4], gr[5]), pack_bf16x2(gr[6], gr[7]));
+      }
+    } else {
+      for (int j = 0; j < 32 && col0 + j < a.N; ++j) {
+        float ur = __bfloat162float(__float2bfloat16_rn(f[j]));
+        u[j] = __float2bfloat16_rn(ur);
+        g[j] = __float2bfloat16_rn(gelu_fwd(ur));
+      }
+    }
+  } else {  // EPI_GELU_BWD: out = acc * gelu'(u), u read from aux (bf16)
+    const __nv_bfloat16* u = static_cast<const __nv_bfloat16*>(a.aux) + static_cast<long>(row) * a.ldaux + col0;
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + static_cast<long>(row) * a.ldo + col0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 ur = *reinterpret_cast<const uint4*>(u + j);
+        const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&ur);
+        float r[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) r[t] = f[j + t] * gelu_grad(__bfloat162float(ub[t]));
+        *reinterpret_cast<uint4*>(o + j) = make_uint4(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]),
+                                                      pack_bf16x2(r[4], r[5]), pack_bf16x2(r[6], r[7]));
+      }
+    } else {
+      for (int j = 0; j < 32 && col0 + j < a.N; ++j)
+        o[j] = __float2bfloat16_rn(f[j] * gelu_grad(__bfloat162float(u[j])));
+    }
+  }
+}
+
+template <int BN>
+__host__ __device__ constexpr uint32_t tmem_cols_for() {
+  return (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+}
+
+template <int BN, int STAGES>
+constexpr size_t smem_bytes_for() {
+  return 1024 /*alignment slack*/ + static_cast<size_t>(STAGES) * (kABytes + BN * kBK * 2) +
+         (2 * STAGES + 4) * sizeof(uint64_t) + 16;
+}
+
+template <int BN, bool A_MN, bool B_MN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs a) {
+  constexpr uint32_t kBBytes = BN * kBK * 2;
+  constexpr uint32_t kTmemCols = tmem_cols_for<BN>();
+  static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16,256]");
+  static_assert(!B_MN || BN % 64 == 0, "MN-major B tiles are loaded in 64-wide chunks");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kBBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&tfull[s], 1);
+      mbar_init(&tempty[s], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles = a.m_tiles * a.n_tiles;
+  const int units = tiles * a.splits;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const int split = u % a.splits;
+        const int tile = u / a.splits;
+        const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
+        const int kb0 = split * a.kb_per_split;
+        const int kb1 = min(a.kb_total, kb0 + a.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, a.err, abort_flag)) goto done;
+          mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+          uint8_t* da = sA + s * kABytes;
+          uint8_t* db = sB + s * kBBytes;
+          if (!A_MN) {
+            tma_load_2d(da, &tmA, &full[s], kb * kBK, mt * kBM);
+          } else {
+            tma_load_2d(da, &tmA, &full[s], mt * kBM, kb * kBK);
+            tma_load_2d(da + 8192, &tmA, &full[s], mt * kBM + 64, kb * kBK);
+          }
+          if (!B_MN) {
+            tma_load_2d(db, &tmB, &full[s], kb * kBK, nt * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(db + j * 8192, &tmB, &full[s], nt * BN + j * 64, kb * kBK);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+      uint32_t it = 0;
+      int local = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+        const int split = u % a.splits;
+        const int kb0 = split * a.kb_per_split;
+        const int kb1 = min(a.kb_total, kb0 + a.kb_per_split);
+        const int as = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[as], aph ^ 1, a.err, abort_flag)) goto done;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + as * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, a.err, abort_flag)) goto done;
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * kABytes);
+          const uint32_t b_addr = smem_u32(sB + s * kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = A_MN ? make_sw128_desc(a_addr + kk * 2048, 8192, 1024)
+                                     : make_sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sw128_desc(b_addr + kk * 2048, 8192, 1024)
+                                     : make_sw128_desc(b_addr + kk * 32, 16, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&tfull[as]);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    int local = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      const int split = u % a.splits;
+      const int tile = u / a.splits;
+      const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
+      const int as = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[as], aph, a.err, abort_flag)) break;
+      tc_fence_after();
+      const int row = mt * kBM + q * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + as * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_row + c * 32, v);
+        tmem_wait_ld();
+        epilogue_row32(a, row, nt * BN + c * 32, v, split);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[as]);
+    }
+  }
+
+done:
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Sums split-K partial slices: out[r, c] = sum_s ws[s][r][c].
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, long slice, int M, int N,
+                                     void* out, long ldo, int out_f32) {
+  const long total = static_cast<long>(M) * N;
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < splits; ++s) acc += ws[s * slice + i];
+    const long r = i / N, c = i % N;
+    if (out_f32)
+      static_cast<float*>(out)[r * ldo + c] = acc;
+    else
+      static_cast<__nv_bfloat16*>(out)[r * ldo + c] = __float2bfloat16_rn(acc);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with row stride
+// `ld` elements; box = {box_cols (inner), box_rows}, 128-byte swizzle,
+// out-of-bounds elements read as zero.
+bool make_map_bf16(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows) {
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || ((ld * 2) & 15) != 0) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, bool A_MN, bool B_MN, int STAGES>
+int launch_tc(const GemmDesc& d, const GemmArgs& args, int grid, cudaStream_t s) {
+  CUtensorMap ta, tb;
+  bool ok;
+  if (!A_MN)
+    ok = make_map_bf16(&ta, d.A, d.M, d.K, d.lda, kBK, kBM);
+  else
+    ok = make_map_bf16(&ta, d.A, d.K, d.M, d.lda, 64, kBK);
+  if (!ok) return 2;
+  if (!B_MN)
+    ok = make_map_bf16(&tb, d.B, d.N, d.K, d.ldb, kBK, BN);
+  else
+    ok = make_map_bf16(&tb, d.B, d.K, d.N, d.ldb, 64, kBK);
+  if (!ok) return 2;
+  constexpr size_t smem = smem_bytes_for<BN, STAGES>();
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(gemm_tc_kernel<BN, A_MN, B_MN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return 3;
+    attr_set = true;
+  }
+  gemm_tc_kernel<BN, A_MN, B_MN, STAGES><<<grid, 192, smem, s>>>(ta, tb, args);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+template <int BN, int STAGES>
+int dispatch_major(const GemmDesc& d, const GemmArgs& args, int grid, cudaStream_t s) {
+  if (!d.a_mn && !d.b_mn) return launch_tc<BN, false, false, STAGES>(d, args, grid, s);
+  if (!d.a_mn && d.b_mn) return launch_tc<BN, false, true, STAGES>(d, args, grid, s);
+  if (d.a_mn && d.b_mn) return launch_tc<BN, true, true, STAGES>(d, args, grid, s);
+  return launch_tc<BN, true, false, STAGES>(d, args, grid, s);
+}
+
+struct Plan {
+  int bn, m_tiles, n_tiles, kb_total, splits, kb_per_split;
+};
+
+Plan plan_for(const GemmDesc& d) {
+  Plan p;
+  p.bn = d.bn;
+  if (p.bn == 0) p.bn = (d.N > 128) ? 256 : 128;
+  if (d.b_mn && p.bn % 64) p.bn = 128;
+  p.m_tiles = (d.M + kBM - 1) / kBM;
+  p.n_tiles = (d.N + p.bn - 1) / p.bn;
+  p.kb_total = (d.K + kBK - 1) / kBK;
+  const int tiles = p.m_tiles * p.n_tiles;
+  int splits = d.splits;
+  if (splits <= 0) {
+    splits = 1;
+    const int sms = num_sms();
+    if (d.epi == EPI_STORE && tiles * 2 <= sms && p.kb_total >= 8) splits = std::min(sms / tiles, p.kb_total / 4);
+  }
+  if (d.epi != EPI_STORE) splits = 1;
+  splits = std::max(1, std::min(splits, p.kb_total));
+  p.kb_per_split = (p.kb_total + splits - 1) / splits;
+  p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
+  return p;
+}
+
+}  // namespace
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+size_t gemm_workspace_bytes(const GemmDesc& d, bool bf16) {
+  if (!bf16) return gemm_f32_workspace_bytes(d);
+  Plan p = plan_for(d);
+  if (p.splits <= 1) return 0;
+  return static_cast<size_t>(p.splits) * d.M * d.N * sizeof(float);
+}
+
+int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* err) {
+  if (d.M <= 0 || d.N <= 0 || d.K <= 0) return 1;
+  Plan p = plan_for(d);
+  GemmArgs a{};
+  a.M = d.M;
+  a.N = d.N;
+  a.K = d.K;
+  a.m_tiles = p.m_tiles;
+  a.n_tiles = p.n_tiles;
+  a.splits = p.splits;
+  a.kb_per_split = p.kb_per_split;
+  a.kb_total = p.kb_total;
+  a.epi = d.epi;
+  a.err = err;
+  const bool split = p.splits > 1;
+  if (split) {
+    const size_t need = static_cast<size_t>(p.splits) * d.M * d.N * sizeof(float);
+    if (!workspace || workspace_bytes < need) return 5;
+    a.out = workspace;
+    a.ldo = d.N;
+    a.out_f32 = 1;
+    a.split_stride = static_cast<long>(d.M) * d.N;
+    a.vec_ok = (d.N % 4 == 0);
+  } else {
+    a.out = d.out;
+    a.ldo = d.ldo;
+    a.out_f32 = d.out_f32;
+    a.aux = d.aux;
+    a.ldaux = d.ldaux;
+    a.aux_f32 = d.aux_f32;
+    a.out2 = d.out2;
+    a.ldo2 = d.ldo2;
+    a.split_stride = 0;
+    auto al = [](const void* ptr, long ld, int esz) {
+      return ptr == nullptr || ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ((ld * esz) & 15) == 0);
+    };
+    a.vec_ok = al(d.out, d.ldo, d.out_f32 ? 4 : 2) && al(d.aux, d.ldaux, d.aux_f32 ? 4 : 2) && al(d.out2, d.ldo2, 2);
+  }
+  const int units = p.m_tiles * p.n_tiles * p.splits;
+  const int grid = std::min(units, num_sms());
+  int rc;
+  switch (p.bn) {
+    case 256: rc = dispatch_major<256, 4>(d, a, grid, s); break;
+    case 128: rc = dispatch_major<128, 6>(d, a, grid, s); break;
+    case 64: rc = dispatch_major<64, 8>(d, a, grid, s); break;
+    default: return 6;
+  }
+  if (rc) return rc;
+  if (split) {
+    const long total = static_cast<long>(d.M) * d.N;
+    const int threads = 256;
+    const int blocks = static_cast<int>(std::min<long>((total + threads - 1) / threads, 4L * num_sms()));
+    splitk_reduce_kernel<<<blocks, threads, 0, s>>>(workspace, p.splits, total, d.M, d.N, d.out, d.ldo, d.out_f32);
+    if (cudaPeekAtLastError() != cudaSuccess) return 4;
+  }
+  return 0;
+}
+
+}  // namespace sb

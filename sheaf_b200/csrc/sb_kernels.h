@@ -1,0 +1,52 @@
+// Host-side launch interface of the kernel library (internal to the shared
+// library; the exported C ABI lives in include/sheaf_b200*.h).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace sb {
+
+// Epilogue applied to each accumulator tile of a GEMM.
+enum EpiKind : int {
+  EPI_STORE = 0,     // out = acc
+  EPI_ADD = 1,       // out = acc + aux            (aux may alias out; f32 only)
+  EPI_GELU = 2,      // out = u = acc; out2 = gelu(u)  (bf16 outputs)
+  EPI_GELU_BWD = 3,  // out = acc * gelu'(aux)     (aux = pre-activation u)
+};
+
+// C[M,N] = A[M,K] * B[N,K]^T with either operand stored K-major (rows of K)
+// or MN-major (stored transposed: [K, M] / [K, N] row-major).
+struct GemmDesc {
+  const void* A = nullptr;
+  long lda = 0;       // row stride (elements) of A as stored
+  bool a_mn = false;  // A stored as [K, M]
+  const void* B = nullptr;
+  long ldb = 0;
+  bool b_mn = false;  // B stored as [K, N]
+  int M = 0, N = 0, K = 0;
+  int epi = EPI_STORE;
+  void* out = nullptr;
+  long ldo = 0;
+  bool out_f32 = false;
+  const void* aux = nullptr;
+  long ldaux = 0;
+  bool aux_f32 = false;
+  void* out2 = nullptr;
+  long ldo2 = 0;
+  int splits = 0;  // 0 = choose; 1 = no split-K (split-K only with EPI_STORE)
+  int bn = 0;      // 0 = choose tile width
+};
+
+// bf16 operands on tcgen05 tensor cores (fp32 accumulation in TMEM).
+// `workspace` (fp32) is used for split-K partial sums; returns 0 on success.
+int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* err);
+// fp32 operands on the CUDA cores (exact fp32 FFMA accumulation).
+int gemm_f32(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* err);
+// Bytes of split-K workspace gemm_* would use for this problem (0 if none).
+size_t gemm_workspace_bytes(const GemmDesc& d, bool bf16);
+size_t gemm_f32_workspace_bytes(const GemmDesc& d);
+
+int num_sms();
+
+}  // namespace sb

@@ -1,0 +1,99 @@
+"""GEMM parity (tcgen05 bf16 and CUDA-core fp32) through the C ABI.
+
+The reference op is `stablehlo.dot_general` as Sheaf emits it for `@`
+(sheaf/src/lowering/stablehlo/dot_ops.rs:32-79) and the transposed operands
+of its VJP (sheaf/src/autodiff/reverse.rs:585-689). Checked against a plain
+fp64 matmul of the same (bf16-rounded) operands.
+"""
+import ctypes as C
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    # M, N, K, trans_a, trans_b, lda_pad, ldc_pad
+    (256, 256, 128, 0, 1, 0, 0),
+    (2048, 1152, 384, 0, 1, 0, 0),
+    (300, 200, 136, 0, 1, 0, 0),
+    (512, 384, 1536, 0, 0, 0, 0),
+    (384, 1536, 4096, 1, 0, 0, 0),
+    (1152, 384, 2048, 1, 0, 0, 0),
+    (65, 384, 2048, 1, 0, 15, 0),
+    (512, 65, 384, 0, 1, 0, 15),
+    (640, 96, 192, 1, 1, 0, 0),
+]
+
+
+def _run(elem, M, N, K, ta, tb, lda_pad, ldc_pad, dev):
+    import torch
+    import sheaf_b200 as sb
+
+    dt = torch.bfloat16 if elem == sb.ELEM_BF16 else torch.float32
+    g = torch.Generator(device="cpu").manual_seed(M * 7 + N * 3 + K)
+    a_log = torch.randn(M, K, generator=g)
+    b_log = torch.randn(K, N, generator=g)
+    a_store = a_log.t().contiguous() if ta else a_log
+    b_store = b_log.t().contiguous() if tb else b_log
+    if lda_pad:
+        pad = torch.zeros(a_store.shape[0], a_store.shape[1] + lda_pad)
+        pad[:, : a_store.shape[1]] = a_store
+        a_store = pad
+    a_dev = a_store.to(dt).to(dev)
+    b_dev = b_store.to(dt).to(dev)
+    ldc = N + ldc_pad
+    c_dev = torch.full((M, ldc), float("nan"), dtype=torch.float32, device=dev)
+    L = sb.lib()
+    ws_bytes = L.sb_op_matmul_workspace_size(elem, ta, tb, M, N, K)
+    ws = torch.empty(max(ws_bytes // 4, 1), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = L.sb_op_matmul(elem, a_dev.data_ptr(), a_dev.stride(0), ta, b_dev.data_ptr(), b_dev.stride(0), tb, M, N, K,
+                        c_dev.data_ptr(), ldc, sb.ELEM_F32, ws.data_ptr(), ws_bytes, stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert L.sb_op_device_error() == 0
+    a_r = a_log.to(dt).double()
+    b_r = b_log.to(dt).double()
+    ref = a_r @ b_r
+    out = c_dev[:, :N].double().cpu()
+    return out, ref
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"{c[0]}x{c[1]}x{c[2]}_t{c[3]}{c[4]}" for c in CASES])
+def test_matmul_bf16(case, cuda):
+    import sheaf_b200 as sb
+
+    out, ref = _run(sb.ELEM_BF16, *case, cuda)
+    assert out.isfinite().all()
+    err = (out - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= 1e-5 * scale + 1e-4, (err, scale)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"{c[0]}x{c[1]}x{c[2]}_t{c[3]}{c[4]}" for c in CASES])
+def test_matmul_f32(case, cuda):
+    import sheaf_b200 as sb
+
+    out, ref = _run(sb.ELEM_F32, *case, cuda)
+    err = (out - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= 1e-5 * scale, (err, scale)
+
+
+def test_matmul_bf16_output(cuda):
+    """bf16 output rounding (RNE) on the tcgen05 epilogue."""
+    import torch
+    import sheaf_b200 as sb
+
+    M, N, K = 512, 256, 256
+    a = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    b = torch.randn(N, K, device=cuda).to(torch.bfloat16)
+    c = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    L = sb.lib()
+    rc = L.sb_op_matmul(sb.ELEM_BF16, a.data_ptr(), K, 0, b.data_ptr(), K, 1, M, N, K, c.data_ptr(), N,
+                        sb.ELEM_BF16, None, 0, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    ref = (a.double() @ b.double().t()).to(torch.bfloat16)
+    diff = (c.double() - ref.double()).abs()
+    # fp32 accumulation then one rounding: at most 1 bf16 ulp from the rounded exact result
+    assert (diff <= ref.double().abs() * 2 ** -7 + 1e-6).all()
