@@ -1,0 +1,380 @@
+#!/usr/bin/env python
+"""nanoGPT fwd+VJP (value_and_grad) tokens/s on B200.
+
+Workload (weak scaling, one process per GPU): every rank runs the
+nanoGPT-char value_and_grad step -- 6 layers, 6 heads, d_model 384, block 256,
+vocab 65, batch 64, pre-LN, GELU MLP 4x, causal attention, cross-entropy --
+on its own batch of 64 x 256 token ids, bf16 parameters (fp32 accumulation),
+through the executor's C ABI (`<module>.value_and_grad`). With N > 1 ranks the
+loss and gradients are averaged over NVLink by NCCL inside the step.
+
+Inputs are synthetic and seeded: parameters N(0, 0.02) (layer-norm gains 1),
+token ids uniform in [0, 65), mirroring init-gpt-params and random-randint.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sheaf_b200|reference]
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "nanoGPT fwd+VJP tokens/sec"
+UNIT = "tokens/s"
+CFG = dict(n_layer=6, n_head=6, n_embd=384, block_size=256, vocab_size=65, batch=64, seq=256)
+BF16 = 0x22000010
+F32 = 0x21000020
+
+
+def model_flops_per_token(c=CFG) -> float:
+    """6*N_mm + 12*L*T*D (matmul params incl. LM head; full T x T attention)."""
+    L, D, V, T = c["n_layer"], c["n_embd"], c["vocab_size"], c["seq"]
+    n_mm = L * 12 * D * D + V * D
+    return 6.0 * n_mm + 12.0 * L * T * D
+
+
+def leaf_shapes(c=CFG):
+    L, D, V, P = c["n_layer"], c["n_embd"], c["vocab_size"], c["block_size"]
+    s = [(V, D)]
+    for _ in range(L):
+        s += [(3 * D, D), (D, D), (D,), (D,), (4 * D, D), (D, 4 * D)]
+    return s + [(D,), (P, D), (V, D)]
+
+
+def synthetic_inputs(seed: int, c=CFG):
+    rng = np.random.default_rng(seed)
+    leaves = []
+    for shp in leaf_shapes(c):
+        leaves.append(np.ones(shp, np.float32) if len(shp) == 1 else
+                      (rng.standard_normal(shp, dtype=np.float32) * np.float32(0.02)))
+    x = rng.integers(0, c["vocab_size"], (c["batch"], c["seq"])).astype(np.float32)
+    y = rng.integers(0, c["vocab_size"], (c["batch"], c["seq"])).astype(np.float32)
+    return leaves, x, y
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    return world, rank, local
+
+
+def allmax(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# --------------------------------------------------------------------------
+# CPU baseline: the oracle (numpy restatement of the reference math)
+# --------------------------------------------------------------------------
+
+def cpu_sample(target_s: float = 12.0, batch: int = 4):
+    """Times the oracle's fp32 fwd+VJP on a bounded sample of the workload
+    (batch `batch` of the 64, same model). Returns (tokens/s, cores, sample)."""
+    from oracle import models
+
+    cfg = models.GPTConfig(batch=batch)
+    leaves, x, y = synthetic_inputs(0, dict(CFG, batch=batch))
+    models.gpt_value_and_grad(leaves, x[:1, :64], y[:1, :64], models.GPTConfig(batch=1, seq=64), dtype=np.float32)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float32)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= target_s or n >= 20:
+            break
+    tok = n * batch * CFG["seq"] / el
+    cores = os.cpu_count() or 1
+    return tok, cores, f"{n} x fp32 numpy fwd+VJP steps of batch {batch} (of 64) x 256 tokens, same 6L/6H/384 model"
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the reference's own math on the host cores (the oracle
+    port; the reference's IREE llvm-cpu path cannot be built here)."""
+    if rank != 0:
+        return
+    import numpy as _np  # noqa: F401
+
+    from oracle import models
+
+    batch = 4
+    cfg = models.GPTConfig(batch=batch)
+    leaves, x, y = synthetic_inputs(0, dict(CFG, batch=batch))
+    for _ in range(args.warmup):
+        models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float32)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float32)
+        times.append(time.perf_counter() - t0)
+    tot = sum(times)
+    v = args.steps * batch * CFG["seq"] / tot
+    cores = os.cpu_count() or 1
+    sample = f"each step: fp32 numpy oracle fwd+VJP of batch {batch} (of 64) x 256 tokens, 6L/6H/384/V65"
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "nanoGPT-char value_and_grad 6L/6H/384 T=256 V=65", "global_batch": batch,
+                       "seq_len": CFG["seq"], "parallelism": "host cores"},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# B200 arm
+# --------------------------------------------------------------------------
+
+def measure_kernel_roofline(session, reps: int = 20):
+    """Times the dominant kernel standalone with CUDA events on the session
+    stream: the fc GEMM of the step (tokens x 384 @ 384 x 1536, bf16 in,
+    tcgen05). Returns (avg_ms, flops_per_launch)."""
+    import torch
+
+    import sheaf_b200 as sb
+
+    L = sb.lib()
+    N, D = CFG["batch"] * CFG["seq"], CFG["n_embd"]
+    dev = torch.device(f"cuda:{session.device}")
+    a = torch.randn(N, D, device=dev).to(torch.bfloat16)
+    w = torch.randn(4 * D, D, device=dev).to(torch.bfloat16)
+    c = torch.empty(N, 4 * D, device=dev, dtype=torch.bfloat16)
+    st = torch.cuda.ExternalStream(session.stream, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    times = []
+    with torch.cuda.stream(st):
+        for i in range(reps + 3):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            rc = L.sb_op_matmul(BF16, a.data_ptr(), D, 0, w.data_ptr(), D, 1, N, 4 * D, D, c.data_ptr(), 4 * D, BF16,
+                                None, 0, session.stream)
+            e1.record(st)
+            assert rc == 0
+            st.synchronize()
+            if i >= 3:
+                times.append(e0.elapsed_time(e1))
+    return sum(times) / len(times), 2.0 * N * D * 4 * D
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="sheaf_b200", choices=["sheaf_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    bench_b200(args, world, rank, local)
+
+
+def bench_b200(args, world, rank, local):
+    import torch
+
+    from sheaf_b200.runtime import Session
+
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    s = Session(local)
+    if world > 1:
+        import torch.distributed as dist
+
+        obj = [Session.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        s.join_group(obj[0], rank, world)
+    s.create_gpt_vag("gpt", **CFG, elem=BF16)
+    leaves, x, y = synthetic_inputs(1234 + rank)
+    inputs = [s.upload(l, BF16) for l in leaves]
+    xb, yb = s.upload(x, F32), s.upload(y, F32)
+    inputs += [xb, yb]
+    st = torch.cuda.ExternalStream(s.stream, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > 126 MB L2
+
+    outs = None
+    for _ in range(max(args.warmup, 3)):
+        outs = s.call("gpt.value_and_grad", inputs)
+    loss0 = float(outs[0].to_host())
+    del outs
+    s.synchronize()
+
+    # ---- device-timed steps: inputs resident, L2 flushed before every step
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    k0 = s.stats()["kernel_launches"]
+    events = []
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(st):
+            for _ in range(args.steps):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                outs = s.call("gpt.value_and_grad", inputs)
+                e1.record(st)
+                events.append((e0, e1))
+                del outs
+            s.synchronize()
+            torch.cuda.synchronize(dev)
+    launches = s.stats()["kernel_launches"] - k0
+    local_ms = sum(a.elapsed_time(b) for a, b in events)
+    total_ms = allmax(local_ms, world)
+    barrier(world)
+    tokens = world * CFG["batch"] * CFG["seq"] * args.steps
+    value = tokens / (total_ms / 1e3)
+    ms_per_step = total_ms / args.steps
+
+    # ---- e2e: host ids -> device (pinned), call, loss -> host, every step
+    pin_x = torch.from_numpy(x).pin_memory()
+    pin_y = torch.from_numpy(y).pin_memory()
+    hx, hy = pin_x.numpy(), pin_y.numpy()
+    barrier(world)
+    s.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        xb.write(hx)
+        yb.write(hy)
+        outs = s.call("gpt.value_and_grad", inputs)
+        _ = outs[0].to_host()
+        del outs
+    e2e_s = allmax(time.perf_counter() - t0, world)
+    e2e_value = tokens / e2e_s
+
+    # ---- roofline of the dominant kernel (tcgen05 GEMM), timed standalone
+    k_ms, k_flops = measure_kernel_roofline(s)
+    hbm, tc_burst, tc_sust, src = peaks()
+    achieved_tf = k_flops / (k_ms / 1e3) / 1e12
+    step_tf = model_flops_per_token() * CFG["batch"] * CFG["seq"] / (ms_per_step / 1e3) / 1e12
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "nanoGPT-char value_and_grad 6L/6H/384 T=256 V=65, batch 64 per GPU",
+                   "global_batch": CFG["batch"] * world, "seq_len": CFG["seq"], "parallelism": f"dp{world}",
+                   "l2": "256 MB buffer written before every timed step (outside the events)",
+                   "step_tflops": step_tf, "step_frac_of_bf16_peak": step_tf * 1e12 / (tc_sust * 1e12),
+                   "model_flop_per_token": model_flops_per_token(), "loss_at_warmup": loss0},
+        "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (fc: 16384x384 @ 384x1536, bf16)",
+                     "achieved": achieved_tf, "peak": tc_burst, "unit": "TFLOP/s", "frac": achieved_tf / tc_burst,
+                     "traffic": None, "peak_source": f"{src} bf16_tflops (burst, kernel timed alone)"},
+        "clocks": clk.summary(),
+        "gpu_launches": int(launches),
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(x.nbytes + y.nbytes),
+                "d2h_bytes_per_step": 2},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_sample()
+        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    s.synchronize()
+    barrier(world)
+    del inputs, xb, yb
+    s.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,144 @@
+/* sheaf_b200 executor C ABI.
+ *
+ * Drop-in replacement for the subset of the IREE runtime C API that Sheaf's
+ * runtime binds (sheaf/src/runtime/iree_ffi.rs:149-297) to run compiled
+ * fwd+VJP (`value_and_grad`) and forward modules. The semantics mirror IREE's
+ * one-to-one so the Rust shim is a rename:
+ *
+ *   iree_runtime_instance_create + try_create_default_device
+ *     + session_create_with_device        -> sb_session_create
+ *   iree-compile + session_append_bytecode_module_from_memory
+ *                                         -> sb_module_load_stablehlo
+ *   iree_runtime_session_call_by_name     -> sb_call
+ *   iree_hal_buffer_view_allocate_buffer_copy -> sb_buffer_alloc_copy
+ *   iree_hal_device_transfer_d2h          -> sb_buffer_d2h
+ *   iree_hal_buffer_view_{retain,release,shape_rank,shape_dim,element_type}
+ *                                         -> sb_buffer_{retain,release,rank,dim,elem_type}
+ *   iree_status_{is_ok,format,free}        -> sb_status_{is_ok,message,free}
+ *
+ * Status: NULL means OK; otherwise an owned object the caller frees.
+ * Buffers are reference counted; a buffer keeps its session alive.
+ * Calls are asynchronous on the session's stream: outputs are ready when
+ * read (sb_buffer_d2h waits, with a bounded timeout).
+ * Element types use IREE HAL codes (sheaf/src/runtime/iree_ffi.rs:32-36).
+ */
+#ifndef SHEAF_B200_H_
+#define SHEAF_B200_H_
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "sheaf_b200_ops.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct sb_status_s* sb_status;
+typedef struct sb_session_s sb_session;
+typedef struct sb_buffer_s sb_buffer;
+typedef struct sb_module_s sb_module;
+
+/* Status codes (mirroring iree_status_code_t values where one exists). */
+#define SB_STATUS_OK 0
+#define SB_STATUS_INVALID_ARGUMENT 3
+#define SB_STATUS_DEADLINE_EXCEEDED 4
+#define SB_STATUS_NOT_FOUND 5
+#define SB_STATUS_RESOURCE_EXHAUSTED 8
+#define SB_STATUS_UNIMPLEMENTED 12
+#define SB_STATUS_INTERNAL 13
+#define SB_STATUS_UNAVAILABLE 14
+
+/* ---- status (replaces iree_status_*, iree_ffi.rs:145-147,281-288) ---- */
+SB_API bool sb_status_is_ok(sb_status status);
+SB_API int sb_status_code(sb_status status);
+SB_API const char* sb_status_message(sb_status status);
+SB_API void sb_status_free(sb_status status);
+
+/* ---- session (replaces IreeSession::new, iree_session.rs:122-231) ---- */
+/* One session per process per GPU. The device must be an sm_100 part. */
+SB_API sb_status sb_session_create(int device_ordinal, sb_session** out_session);
+SB_API void sb_session_retain(sb_session* session);
+SB_API void sb_session_release(sb_session* session);
+/* Waits for all work queued on the session; DEADLINE_EXCEEDED after timeout_ns
+ * (< 0 = no limit). Also reports a kernel-side bounded-wait timeout. */
+SB_API sb_status sb_session_synchronize(sb_session* session, int64_t timeout_ns);
+/* The session's cudaStream_t (for callers that interleave their own work). */
+SB_API void* sb_session_stream(sb_session* session);
+/* Dispatch counters in the spirit of `--jit-profile`
+ * (sheaf/src/runtime/iree_session.rs:250-297). kernel_launches counts every
+ * library kernel the session's calls have launched (kernel nodes of a
+ * replayed CUDA graph included). */
+typedef struct sb_session_stats {
+  uint64_t calls;
+  uint64_t graph_captures;
+  uint64_t graph_replays;
+  uint64_t kernel_launches;
+} sb_session_stats;
+SB_API sb_status sb_session_get_stats(sb_session* session, sb_session_stats* out_stats);
+
+/* ---- data-parallel group (no reference counterpart: roadmap item
+ * "NCCL all-reduce", docs/roadmap.md:61-62) ----
+ * Joins this session to an NCCL group of `world` ranks. Afterwards every
+ * value_and_grad call all-reduces (averages) the loss and the gradients, each
+ * rank having received its own equal batch shard. */
+#define SB_NCCL_ID_BYTES 128
+SB_API sb_status sb_nccl_unique_id(void* out_id, size_t id_bytes);
+SB_API sb_status sb_session_join_group(sb_session* session, const void* nccl_id, size_t id_bytes, int rank, int world);
+
+/* ---- buffers (replaces buffer_convert.rs:14-123, device_buffer.rs:47-134) ---- */
+/* Allocates a device buffer from the session pool and copies `bytes` of host
+ * data into it (bytes must equal the element count times the element size). */
+SB_API sb_status sb_buffer_alloc_copy(sb_session* session, const int64_t* shape, size_t rank, uint32_t elem_type,
+                                      const void* host, size_t bytes, sb_buffer** out_buffer);
+/* Allocates an uninitialised device buffer. */
+SB_API sb_status sb_buffer_alloc(sb_session* session, const int64_t* shape, size_t rank, uint32_t elem_type,
+                                 sb_buffer** out_buffer);
+/* Asynchronous host -> device copy into an existing buffer (pinned host
+ * memory makes it truly asynchronous). */
+SB_API sb_status sb_buffer_h2d(sb_buffer* buffer, const void* host, size_t bytes);
+/* Device -> host copy; waits at most timeout_ns (< 0 = no limit). */
+SB_API sb_status sb_buffer_d2h(sb_buffer* buffer, void* host, size_t bytes, int64_t timeout_ns);
+SB_API void sb_buffer_retain(sb_buffer* buffer);
+SB_API void sb_buffer_release(sb_buffer* buffer);
+SB_API size_t sb_buffer_rank(const sb_buffer* buffer);
+SB_API int64_t sb_buffer_dim(const sb_buffer* buffer, size_t axis);
+SB_API uint32_t sb_buffer_elem_type(const sb_buffer* buffer);
+SB_API size_t sb_buffer_byte_length(const sb_buffer* buffer);
+SB_API void* sb_buffer_device_ptr(const sb_buffer* buffer);
+
+/* ---- modules (replaces iree-compile + load_vmfb, jit/vag.rs:660-726,
+ *      iree_session.rs:307-340) ---- */
+/* Parses a StableHLO module as Sheaf's emitter prints it
+ * (lowering/stablehlo/emit.rs:240-257) and maps it onto the kernel library.
+ * An op the library cannot execute yields UNIMPLEMENTED, which the caller
+ * treats like a failed compile (jit/compile.rs:119-125). The module is
+ * registered in the session under its `module @<name>`. */
+SB_API sb_status sb_module_load_stablehlo(sb_session* session, const char* mlir_text, size_t length,
+                                          const char** out_module_name);
+/* Registers the fused nanoGPT value_and_grad module (the graph of
+ * examples/nanogpt/model.shf + cross-entropy) for a configuration without
+ * going through text. Function "value_and_grad": inputs are the 4*...-leaf
+ * parameter pytree in sorted-key order, then x ids [batch, seq] and y ids
+ * [batch, seq] (f32); outputs are loss then one gradient per leaf. */
+typedef struct sb_gpt_config {
+  int32_t n_layer, n_head, n_embd, block_size, vocab_size, batch, seq;
+  uint32_t elem_type; /* SB_ELEM_BF16 or SB_ELEM_F32 */
+} sb_gpt_config;
+SB_API sb_status sb_module_create_gpt_vag(sb_session* session, const char* module_name, const sb_gpt_config* config);
+
+/* ---- invocation (replaces iree_runtime_session_call_by_name,
+ *      iree_session.rs:576-583) ----
+ * `qualified_name` is "<module>.<function>" (iree_dispatch.rs:95-104,172).
+ * Inputs are borrowed for the call. On success `*out_count` outputs are
+ * written to `outputs` (capacity `out_capacity`), each a new reference owned
+ * by the caller. */
+SB_API sb_status sb_call(sb_session* session, const char* qualified_name, sb_buffer* const* inputs, size_t in_count,
+                         sb_buffer** outputs, size_t out_capacity, size_t* out_count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SHEAF_B200_H_ */

@@ -51,6 +51,59 @@ SB_API int sb_op_matmul(uint32_t elem, const void* a, int64_t lda, int trans_a, 
                  size_t workspace_bytes, void* stream);
 SB_API size_t sb_op_matmul_workspace_size(uint32_t elem, int trans_a, int trans_b, int32_t m, int32_t n, int32_t k);
 
+/* Layer norm without beta over the last dim (examples/nanogpt/model.shf:11-14:
+ * (x - mean) / sqrt(var + 1e-5) * gamma, two-pass population variance as in
+ * sheaf/src/lowering/codegen/reduction_builtins.rs:287-358).
+ *   x f32 [rows, d]; gamma, y of type `elem` (SB_ELEM_BF16 / SB_ELEM_F32);
+ *   mean, rstd f32 [rows] saved for the VJP. d must be a multiple of 4. */
+SB_API int sb_op_layernorm_fwd(uint32_t elem, const void* x, const void* gamma, void* y, void* mean, void* rstd,
+                               int32_t rows, int32_t d, void* stream);
+/* VJP (the `/`, `-`, `sqrt`, `var`, `mean` rules of
+ * sheaf/src/autodiff/reverse.rs:551-583,847-914,961-967, composed):
+ *   dres (f32 [rows, d]) += dx; dgamma (`elem`, [d]) = sum_rows dy * xhat.
+ *   dy is f32. */
+SB_API size_t sb_op_layernorm_bwd_workspace_size(int32_t rows, int32_t d);
+SB_API int sb_op_layernorm_bwd(uint32_t elem, const void* dy, const void* x, const void* mean, const void* rstd,
+                               const void* gamma, void* dres, void* dgamma, void* workspace, size_t workspace_bytes,
+                               int32_t rows, int32_t d, void* stream);
+
+/* cross-entropy-loss fused with its VJP (sheaf/lib/nn.shf:28-30,44-50):
+ *   loss_f32[0] = -mean_r log_softmax(logits[r])[targets[r]];
+ *   dlogits = (softmax(logits) - one_hot(targets)) / rows.
+ * logits / dlogits of type `elem` with row strides ld / ldd; targets are f32
+ * class ids (converted by truncation, as `stablehlo.convert` does). */
+SB_API size_t sb_op_cross_entropy_workspace_size(int32_t rows);
+SB_API int sb_op_cross_entropy(uint32_t elem, const void* logits, int64_t ld, int32_t rows, int32_t v,
+                               const void* targets, void* dlogits, int64_t ldd, void* workspace,
+                               size_t workspace_bytes, void* loss_f32, void* stream);
+
+/* Token + position embedding: x[n] = wte[clamp(ids[n])] + wpe[n % t] (f32 out)
+ * (`stablehlo.convert` + `stablehlo.gather`,
+ * sheaf/src/lowering/stablehlo/indexing_ops.rs:416-484; wpe `slice`). */
+SB_API int sb_op_embedding_fwd(uint32_t elem, const void* ids, const void* wte, const void* wpe, void* x,
+                               int32_t ntok, int32_t t, int32_t v, int32_t d, void* stream);
+/* Embedding VJP as a scatter-add (the reference's one-hot matmul,
+ * sheaf/src/autodiff/reverse.rs:1077-1122) and the wpe slice VJP (pad,
+ * sheaf/src/lowering/codegen/builtins.rs:208-271): dx f32 [b*t, d] ->
+ * dwte [v, d], dwpe [p, d] (rows >= t zero), both of type `elem`. */
+SB_API size_t sb_op_embedding_bwd_workspace_size(int32_t v, int32_t d);
+SB_API int sb_op_embedding_bwd(uint32_t elem, const void* ids, const void* dx, int32_t b, int32_t t, int32_t p,
+                               int32_t v, int32_t d, void* dwte, void* dwpe, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/* Fused causal self-attention over the packed projection qkv [b*t, 3*h*hd]
+ * (q | k | v, head j at columns j*hd), as examples/nanogpt/model.shf:55-70
+ * computes it: softmax(where(tril, q k^T / sqrt(hd), -1e10)) v, heads merged
+ * to o [b*t, h*hd]; lse f32 [b*h*t] (log-sum-exp of the scaled scores) is
+ * saved for the VJP. hd is 32 or 64. */
+SB_API int sb_op_attention_fwd(uint32_t elem, const void* qkv, void* o, void* lse, int32_t b, int32_t t, int32_t h,
+                               int32_t hd, void* stream);
+/* VJP: dqkv [b*t, 3*h*hd] (dq | dk | dv) from qkv, o, do and lse. */
+SB_API size_t sb_op_attention_bwd_workspace_size(uint32_t elem, int32_t b, int32_t t, int32_t h, int32_t hd);
+SB_API int sb_op_attention_bwd(uint32_t elem, const void* qkv, const void* o, const void* dout, const void* lse,
+                               void* dqkv, void* workspace, size_t workspace_bytes, int32_t b, int32_t t, int32_t h,
+                               int32_t hd, void* stream);
+
 /* Reads and clears the device error word that bounded waits inside the
  * kernels set (0 = no error, 1 = a barrier wait timed out). Synchronizes
  * the device. */

@@ -176,15 +176,19 @@ def ids_to_index(ids):
 
 
 def embedding(w, ids):
-    """`get` on a tensor with an index tensor -> gather of rows (indexing_ops.rs:416-484)."""
-    return w[ids_to_index(ids)]
+    """`get` on a tensor with an index tensor -> `stablehlo.gather` of rows
+    (indexing_ops.rs:416-484). Gather clamps start indices into range."""
+    return w[np.clip(ids_to_index(ids), 0, w.shape[0] - 1)]
 
 
 def embedding_vjp(w_shape, ids, g, dtype):
-    """reverse.rs:1077-1122: one_hot(idx, V)^T @ adj, i.e. a scatter-add of rows."""
+    """reverse.rs:1077-1122: one_hot(idx, V)^T @ adj, i.e. a scatter-add of
+    rows; an index outside [0, V) has an all-zero one-hot row and adds nothing."""
     out = np.zeros(w_shape, dtype=dtype)
     idx = ids_to_index(ids).reshape(-1)
-    np.add.at(out, idx, g.reshape(len(idx), -1).reshape((len(idx),) + tuple(w_shape[1:])))
+    rows = g.reshape((len(idx),) + tuple(w_shape[1:]))
+    ok = (idx >= 0) & (idx < w_shape[0])
+    np.add.at(out, idx[ok], rows[ok])
     return out
 
 

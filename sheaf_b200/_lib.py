@@ -18,13 +18,69 @@ ELEM_I32 = 0x10000020
 
 _lib = None
 
+
+class GptConfig(C.Structure):
+    """sb_gpt_config (include/sheaf_b200.h)."""
+    _fields_ = [("n_layer", C.c_int32), ("n_head", C.c_int32), ("n_embd", C.c_int32), ("block_size", C.c_int32),
+                ("vocab_size", C.c_int32), ("batch", C.c_int32), ("seq", C.c_int32), ("elem_type", C.c_uint32)]
+
+
+class SessionStats(C.Structure):
+    """sb_session_stats (include/sheaf_b200.h)."""
+    _fields_ = [("calls", C.c_uint64), ("graph_captures", C.c_uint64), ("graph_replays", C.c_uint64),
+                ("kernel_launches", C.c_uint64)]
+
+
+_P = C.c_void_p
 # name -> (restype, argtypes); every symbol declared in include/*.h.
 SIGNATURES: dict[str, tuple] = {
-    "sb_op_matmul": (C.c_int, [C.c_uint32, C.c_void_p, C.c_int64, C.c_int, C.c_void_p, C.c_int64, C.c_int,
-                               C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int64, C.c_uint32, C.c_void_p,
-                               C.c_size_t, C.c_void_p]),
+    # sheaf_b200_ops.h
+    "sb_op_matmul": (C.c_int, [C.c_uint32, _P, C.c_int64, C.c_int, _P, C.c_int64, C.c_int, C.c_int32, C.c_int32,
+                               C.c_int32, _P, C.c_int64, C.c_uint32, _P, C.c_size_t, _P]),
     "sb_op_matmul_workspace_size": (C.c_size_t, [C.c_uint32, C.c_int, C.c_int, C.c_int32, C.c_int32, C.c_int32]),
+    "sb_op_layernorm_fwd": (C.c_int, [C.c_uint32, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, _P]),
+    "sb_op_layernorm_bwd_workspace_size": (C.c_size_t, [C.c_int32, C.c_int32]),
+    "sb_op_layernorm_bwd": (C.c_int, [C.c_uint32, _P, _P, _P, _P, _P, _P, _P, _P, C.c_size_t, C.c_int32, C.c_int32,
+                                      _P]),
+    "sb_op_cross_entropy_workspace_size": (C.c_size_t, [C.c_int32]),
+    "sb_op_cross_entropy": (C.c_int, [C.c_uint32, _P, C.c_int64, C.c_int32, C.c_int32, _P, _P, C.c_int64, _P,
+                                      C.c_size_t, _P, _P]),
+    "sb_op_embedding_fwd": (C.c_int, [C.c_uint32, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P]),
+    "sb_op_embedding_bwd_workspace_size": (C.c_size_t, [C.c_int32, C.c_int32]),
+    "sb_op_embedding_bwd": (C.c_int, [C.c_uint32, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P,
+                                      _P, _P, C.c_size_t, _P]),
+    "sb_op_attention_fwd": (C.c_int, [C.c_uint32, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P]),
+    "sb_op_attention_bwd_workspace_size": (C.c_size_t, [C.c_uint32, C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
+    "sb_op_attention_bwd": (C.c_int, [C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_size_t, C.c_int32, C.c_int32,
+                                      C.c_int32, C.c_int32, _P]),
     "sb_op_device_error": (C.c_int, []),
+    # sheaf_b200.h
+    "sb_status_is_ok": (C.c_bool, [_P]),
+    "sb_status_code": (C.c_int, [_P]),
+    "sb_status_message": (C.c_char_p, [_P]),
+    "sb_status_free": (None, [_P]),
+    "sb_session_create": (_P, [C.c_int, C.POINTER(_P)]),
+    "sb_session_retain": (None, [_P]),
+    "sb_session_release": (None, [_P]),
+    "sb_session_synchronize": (_P, [_P, C.c_int64]),
+    "sb_session_stream": (_P, [_P]),
+    "sb_session_get_stats": (_P, [_P, C.POINTER(SessionStats)]),
+    "sb_nccl_unique_id": (_P, [_P, C.c_size_t]),
+    "sb_session_join_group": (_P, [_P, _P, C.c_size_t, C.c_int, C.c_int]),
+    "sb_buffer_alloc_copy": (_P, [_P, C.POINTER(C.c_int64), C.c_size_t, C.c_uint32, _P, C.c_size_t, C.POINTER(_P)]),
+    "sb_buffer_alloc": (_P, [_P, C.POINTER(C.c_int64), C.c_size_t, C.c_uint32, C.POINTER(_P)]),
+    "sb_buffer_h2d": (_P, [_P, _P, C.c_size_t]),
+    "sb_buffer_d2h": (_P, [_P, _P, C.c_size_t, C.c_int64]),
+    "sb_buffer_retain": (None, [_P]),
+    "sb_buffer_release": (None, [_P]),
+    "sb_buffer_rank": (C.c_size_t, [_P]),
+    "sb_buffer_dim": (C.c_int64, [_P, C.c_size_t]),
+    "sb_buffer_elem_type": (C.c_uint32, [_P]),
+    "sb_buffer_byte_length": (C.c_size_t, [_P]),
+    "sb_buffer_device_ptr": (_P, [_P]),
+    "sb_module_load_stablehlo": (_P, [_P, C.c_char_p, C.c_size_t, C.POINTER(C.c_char_p)]),
+    "sb_module_create_gpt_vag": (_P, [_P, C.c_char_p, C.POINTER(GptConfig)]),
+    "sb_call": (_P, [_P, C.c_char_p, C.POINTER(_P), C.c_size_t, C.POINTER(_P), C.c_size_t, C.POINTER(C.c_size_t)]),
 }
 
 

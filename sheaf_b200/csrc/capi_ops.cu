@@ -5,6 +5,7 @@
 
 #include "../../include/sheaf_b200_ops.h"
 #include "sb_kernels.h"
+#include "sb_nn.h"
 
 namespace sb {
 
@@ -60,6 +61,80 @@ int sb_op_matmul(uint32_t elem, const void* a, int64_t lda, int trans_a, const v
   if (elem == SB_ELEM_BF16)
     return sb::gemm_bf16(d, static_cast<float*>(workspace), workspace_bytes, s, sb::device_error_word());
   return sb::gemm_f32(d, static_cast<float*>(workspace), workspace_bytes, s, sb::device_error_word());
+}
+
+static bool float_elem(uint32_t e) { return e == SB_ELEM_BF16 || e == SB_ELEM_F32; }
+
+int sb_op_layernorm_fwd(uint32_t elem, const void* x, const void* gamma, void* y, void* mean, void* rstd,
+                        int32_t rows, int32_t d, void* stream) {
+  if (!float_elem(elem) || !x || !gamma || !y || !mean || !rstd) return SB_OPERR_ARGS;
+  const bool f = elem == SB_ELEM_F32;
+  return sb::layernorm_fwd(static_cast<const float*>(x), gamma, f, y, f, static_cast<float*>(mean),
+                           static_cast<float*>(rstd), rows, d, static_cast<cudaStream_t>(stream));
+}
+
+size_t sb_op_layernorm_bwd_workspace_size(int32_t rows, int32_t d) { return sb::layernorm_bwd_workspace_bytes(rows, d); }
+
+int sb_op_layernorm_bwd(uint32_t elem, const void* dy, const void* x, const void* mean, const void* rstd,
+                        const void* gamma, void* dres, void* dgamma, void* workspace, size_t workspace_bytes,
+                        int32_t rows, int32_t d, void* stream) {
+  if (!float_elem(elem) || !dy || !x || !mean || !rstd || !gamma || !dres || !dgamma) return SB_OPERR_ARGS;
+  if (workspace_bytes < sb::layernorm_bwd_workspace_bytes(rows, d) || !workspace) return SB_OPERR_WORKSPACE;
+  const bool f = elem == SB_ELEM_F32;
+  return sb::layernorm_bwd(dy, true, static_cast<const float*>(x), static_cast<const float*>(mean),
+                           static_cast<const float*>(rstd), gamma, f, static_cast<float*>(dres), nullptr, dgamma, f,
+                           static_cast<float*>(workspace), rows, d, static_cast<cudaStream_t>(stream));
+}
+
+size_t sb_op_cross_entropy_workspace_size(int32_t rows) { return sb::cross_entropy_workspace_bytes(rows); }
+
+int sb_op_cross_entropy(uint32_t elem, const void* logits, int64_t ld, int32_t rows, int32_t v, const void* targets,
+                        void* dlogits, int64_t ldd, void* workspace, size_t workspace_bytes, void* loss_f32,
+                        void* stream) {
+  if (!float_elem(elem) || !logits || !targets || !dlogits || !loss_f32) return SB_OPERR_ARGS;
+  if (!workspace || workspace_bytes < sb::cross_entropy_workspace_bytes(rows)) return SB_OPERR_WORKSPACE;
+  return sb::cross_entropy_fwd_bwd(logits, elem == SB_ELEM_F32, ld, rows, v, static_cast<const float*>(targets),
+                                   dlogits, ldd, static_cast<float*>(workspace), static_cast<float*>(loss_f32),
+                                   nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int sb_op_embedding_fwd(uint32_t elem, const void* ids, const void* wte, const void* wpe, void* x, int32_t ntok,
+                        int32_t t, int32_t v, int32_t d, void* stream) {
+  if (!float_elem(elem) || !ids || !wte || !wpe || !x || t <= 0 || v <= 0) return SB_OPERR_ARGS;
+  return sb::embedding_fwd(static_cast<const float*>(ids), wte, wpe, elem == SB_ELEM_F32, static_cast<float*>(x),
+                           ntok, t, v, d, static_cast<cudaStream_t>(stream));
+}
+
+size_t sb_op_embedding_bwd_workspace_size(int32_t v, int32_t d) { return sb::embedding_bwd_workspace_bytes(v, d); }
+
+int sb_op_embedding_bwd(uint32_t elem, const void* ids, const void* dx, int32_t b, int32_t t, int32_t p, int32_t v,
+                        int32_t d, void* dwte, void* dwpe, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!float_elem(elem) || !ids || !dx || !dwte || !dwpe || p < t) return SB_OPERR_ARGS;
+  if (workspace_bytes < sb::embedding_bwd_workspace_bytes(v, d)) return SB_OPERR_WORKSPACE;
+  return sb::embedding_bwd(static_cast<const float*>(ids), static_cast<const float*>(dx), b, t, p, v, d, dwte, dwpe,
+                           elem == SB_ELEM_F32, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream));
+}
+
+int sb_op_attention_fwd(uint32_t elem, const void* qkv, void* o, void* lse, int32_t b, int32_t t, int32_t h,
+                        int32_t hd, void* stream) {
+  if (!float_elem(elem) || !qkv || !o || !lse || b <= 0 || t <= 0 || h <= 0) return SB_OPERR_ARGS;
+  return sb::attention_fwd(qkv, elem == SB_ELEM_F32, o, static_cast<float*>(lse), sb::AttnShape{b, t, h, hd},
+                           static_cast<cudaStream_t>(stream));
+}
+
+size_t sb_op_attention_bwd_workspace_size(uint32_t elem, int32_t b, int32_t t, int32_t h, int32_t hd) {
+  return sb::attention_bwd_workspace_bytes(elem == SB_ELEM_F32, sb::AttnShape{b, t, h, hd});
+}
+
+int sb_op_attention_bwd(uint32_t elem, const void* qkv, const void* o, const void* dout, const void* lse, void* dqkv,
+                        void* workspace, size_t workspace_bytes, int32_t b, int32_t t, int32_t h, int32_t hd,
+                        void* stream) {
+  if (!float_elem(elem) || !qkv || !o || !dout || !lse || !dqkv) return SB_OPERR_ARGS;
+  const sb::AttnShape sh{b, t, h, hd};
+  if (!workspace || workspace_bytes < sb::attention_bwd_workspace_bytes(elem == SB_ELEM_F32, sh))
+    return SB_OPERR_WORKSPACE;
+  return sb::attention_bwd(qkv, o, dout, static_cast<const float*>(lse), elem == SB_ELEM_F32, dqkv,
+                           static_cast<float*>(workspace), sh, static_cast<cudaStream_t>(stream));
 }
 
 int sb_op_device_error(void) {

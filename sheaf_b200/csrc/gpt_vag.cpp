@@ -1,0 +1,499 @@
+// The fused nanoGPT value_and_grad module.
+//
+// Executes the graph Sheaf compiles for
+//   ((value-and-grad (fn [p] (cross-entropy-loss (gpt-forward x p config) y))) params)
+// (examples/nanogpt/train.shf:26-28, model.shf:85-113, lib/nn.shf:44-50) as a
+// fixed schedule of library kernels instead of IREE dispatches:
+//   forward : embedding gather + wpe slice; per layer LN -> QKV GEMM ->
+//             fused causal attention -> proj GEMM (+residual epilogue) -> LN ->
+//             fc GEMM (+GELU epilogue) -> fc2 GEMM (+residual epilogue);
+//             final LN -> head GEMM -> fused cross-entropy fwd+VJP
+//   backward: the `@` VJP GEMMs (dX with K-major / N-major operands, dW
+//             contracted over all tokens with split-K), GELU-VJP fused in the
+//             dX epilogue, LN VJP accumulating into the residual gradient,
+//             fused attention VJP, embedding scatter-add + wpe pad.
+// Inputs follow the module signature Sheaf's compile_vag produces
+// (jit/vag.rs:126-141): the params pytree leaves (sorted keys, buffer_convert.rs
+// :218-246), then the captured x and y token ids (f32). Outputs are
+// (loss, grad leaves...) (jit/vag.rs:565-574).
+//
+// Schedule: parameters are copied into plan-owned slots (one batched-copy
+// launch), the compute sequence is replayed from a CUDA graph, and the
+// gradients + loss are copied into one fresh pool allocation that backs all
+// the output buffers. With a data-parallel group, per-layer gradient buckets
+// are all-reduced on a second stream as soon as the layer's weight gradients
+// are complete, overlapping the rest of the backward pass.
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "runtime.h"
+#include "sb_kernels.h"
+#include "sb_nn.h"
+
+namespace sb {
+
+namespace {
+
+constexpr int kMaxSegs = 48;
+
+struct CopySegs {
+  const char* src[kMaxSegs];
+  char* dst[kMaxSegs];
+  unsigned long long bytes[kMaxSegs];
+  int n;
+};
+
+__global__ void batched_copy_kernel(CopySegs c) {
+  const int seg = blockIdx.y;
+  if (seg >= c.n) return;
+  const char* s = c.src[seg];
+  char* d = c.dst[seg];
+  const size_t n = c.bytes[seg];
+  const size_t tid = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  if (((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d)) & 15) == 0) {
+    const size_t n16 = n / 16;
+    for (size_t i = tid; i < n16; i += stride) reinterpret_cast<uint4*>(d)[i] = reinterpret_cast<const uint4*>(s)[i];
+    for (size_t i = n16 * 16 + tid; i < n; i += stride) d[i] = s[i];
+  } else {
+    for (size_t i = tid; i < n; i += stride) d[i] = s[i];
+  }
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+class GptVagModule : public Module {
+ public:
+  GptShape g{};
+  bool bf = true;
+  size_t es = 2;
+  int L = 0, H = 0, D = 0, V = 0, P = 0, B = 0, T = 0, N = 0, ldl = 0;
+  std::vector<std::vector<int64_t>> shapes;
+  std::vector<size_t> offs;
+  size_t grads_bytes = 0, loss_off = 0, out_bytes = 0;
+
+  std::vector<void*> owned;
+  char* params = nullptr;
+  char* grads = nullptr;  // gradients followed by the loss (output element type)
+  float* ids = nullptr;   // x ids [N] then y ids [N]
+  float* loss_f32 = nullptr;
+  std::vector<float*> xs, xmid, mean1, rstd1, mean2, rstd2, lse;
+  float *meanf = nullptr, *rstdf = nullptr;
+  std::vector<void*> h1, h2, qkv, att, u, gact;
+  void *hf = nullptr, *logits = nullptr, *dlogits = nullptr;
+  float* dres = nullptr;
+  void* dres_bf = nullptr;
+  float* dh = nullptr;
+  void *du = nullptr, *dout = nullptr, *dqkv = nullptr;
+  float* ws = nullptr;
+  size_t ws_bytes = 0;
+
+  cudaGraphExec_t exec = nullptr;
+  uint64_t kernels_per_step = 0;  // kernel nodes of the captured step graph
+  int eager_runs = 0;
+  bool use_graph = true;
+  std::vector<cudaEvent_t> bucket_events;
+  cudaEvent_t comm_done = nullptr;
+
+  ~GptVagModule() override { teardown(); }
+
+  void teardown() override {
+    if (exec) cudaGraphExecDestroy(exec);
+    exec = nullptr;
+    for (auto e : bucket_events) cudaEventDestroy(e);
+    bucket_events.clear();
+    if (comm_done) cudaEventDestroy(comm_done);
+    comm_done = nullptr;
+    for (void* p : owned) cudaFree(p);
+    owned.clear();
+  }
+
+  bool has_function(const std::string& fn) const override { return fn == "value_and_grad"; }
+
+  void* Pp(int i) const { return params + offs[i]; }
+  void* Gp(int i) const { return grads + offs[i]; }
+
+  sb_status dev(size_t bytes, void** p) {
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+    if (e != cudaSuccess) return make_status(SB_STATUS_RESOURCE_EXHAUSTED, "plan allocation failed");
+    owned.push_back(*p);
+    return nullptr;
+  }
+  template <typename T>
+  sb_status devt(size_t count, T** p) {
+    void* v = nullptr;
+    SB_TRY(dev(count * sizeof(T), &v));
+    *p = static_cast<T*>(v);
+    return nullptr;
+  }
+
+  GemmDesc desc(const void* A, long lda, bool a_mn, const void* Bm, long ldb, bool b_mn, int M, int Nn, int K,
+                void* out, long ldo, bool out_f32) const {
+    GemmDesc d;
+    d.A = A;
+    d.lda = lda;
+    d.a_mn = a_mn;
+    d.B = Bm;
+    d.ldb = ldb;
+    d.b_mn = b_mn;
+    d.M = M;
+    d.N = Nn;
+    d.K = K;
+    d.out = out;
+    d.ldo = ldo;
+    d.out_f32 = out_f32;
+    return d;
+  }
+
+  int gemm(const GemmDesc& d, cudaStream_t st, int* err) const {
+    return bf ? gemm_bf16(d, ws, ws_bytes, st, err) : gemm_f32(d, ws, ws_bytes, st, err);
+  }
+
+  // All GEMMs of one step (used for workspace sizing).
+  std::vector<GemmDesc> all_gemms() const {
+    std::vector<GemmDesc> v;
+    const bool f = !bf;
+    v.push_back(desc(nullptr, D, false, nullptr, D, false, N, 3 * D, D, nullptr, 3 * D, f));
+    v.push_back(desc(nullptr, D, false, nullptr, D, false, N, D, D, nullptr, D, true));
+    v.push_back(desc(nullptr, D, false, nullptr, D, false, N, 4 * D, D, nullptr, 4 * D, f));
+    v.push_back(desc(nullptr, 4 * D, false, nullptr, 4 * D, false, N, D, 4 * D, nullptr, D, true));
+    v.push_back(desc(nullptr, D, false, nullptr, D, false, N, V, D, nullptr, ldl, f));
+    v.push_back(desc(nullptr, ldl, false, nullptr, D, true, N, D, V, nullptr, D, true));
+    v.push_back(desc(nullptr, ldl, true, nullptr, D, true, V, D, N, nullptr, D, f));
+    v.push_back(desc(nullptr, D, true, nullptr, 4 * D, true, D, 4 * D, N, nullptr, 4 * D, f));
+    v.push_back(desc(nullptr, 4 * D, true, nullptr, D, true, 4 * D, D, N, nullptr, D, f));
+    v.push_back(desc(nullptr, D, true, nullptr, D, true, D, D, N, nullptr, D, f));
+    v.push_back(desc(nullptr, 3 * D, true, nullptr, D, true, 3 * D, D, N, nullptr, D, f));
+    return v;
+  }
+
+  sb_status build(const std::string& nm, const GptShape& shape) {
+    name = nm;
+    g = shape;
+    SB_RETURN_IF(g.elem != SB_ELEM_BF16 && g.elem != SB_ELEM_F32, SB_STATUS_INVALID_ARGUMENT,
+                 "gpt module element type must be bf16 or f32");
+    SB_RETURN_IF(g.n_layer <= 0 || g.n_head <= 0 || g.n_embd <= 0 || g.vocab <= 0 || g.batch <= 0 || g.seq <= 0,
+                 SB_STATUS_INVALID_ARGUMENT, "non-positive gpt dimension");
+    SB_RETURN_IF(g.n_embd % g.n_head != 0, SB_STATUS_INVALID_ARGUMENT, "n_embd must be divisible by n_head");
+    SB_RETURN_IF(g.seq > g.block_size, SB_STATUS_INVALID_ARGUMENT, "seq exceeds block_size (wpe rows)");
+    const int hd = g.n_embd / g.n_head;
+    SB_RETURN_IF(hd != 64 && hd != 32, SB_STATUS_UNIMPLEMENTED, "attention head dim must be 32 or 64");
+    SB_RETURN_IF(g.n_embd % 64 != 0, SB_STATUS_UNIMPLEMENTED, "n_embd must be a multiple of 64");
+    bf = g.elem == SB_ELEM_BF16;
+    es = bf ? 2 : 4;
+    L = g.n_layer;
+    H = g.n_head;
+    D = g.n_embd;
+    V = g.vocab;
+    P = g.block_size;
+    B = g.batch;
+    T = g.seq;
+    N = B * T;
+    ldl = (V + 7) / 8 * 8;
+    use_graph = !(std::getenv("SHEAF_B200_GRAPH") && std::string(std::getenv("SHEAF_B200_GRAPH")) == "0");
+
+    shapes.push_back({V, D});
+    for (int l = 0; l < L; ++l) {
+      shapes.push_back({3 * D, D});
+      shapes.push_back({D, D});
+      shapes.push_back({D});
+      shapes.push_back({D});
+      shapes.push_back({4 * D, D});
+      shapes.push_back({D, 4 * D});
+    }
+    shapes.push_back({D});
+    shapes.push_back({P, D});
+    shapes.push_back({V, D});
+    size_t off = 0;
+    for (auto& s : shapes) {
+      offs.push_back(off);
+      size_t n = es;
+      for (auto d : s) n *= static_cast<size_t>(d);
+      off = align256(off + n);
+    }
+    grads_bytes = off;
+    loss_off = off;
+    out_bytes = align256(off + 4);
+
+    void* v;
+    SB_TRY(dev(grads_bytes, &v));
+    params = static_cast<char*>(v);
+    SB_TRY(dev(out_bytes, &v));
+    grads = static_cast<char*>(v);
+    cudaMemset(grads, 0, out_bytes);
+    SB_TRY(devt(2 * static_cast<size_t>(N), &ids));
+    SB_TRY(devt(4, &loss_f32));
+    const size_t nd = static_cast<size_t>(N) * D;
+    for (int l = 0; l <= L; ++l) {
+      float* p;
+      SB_TRY(devt(nd, &p));
+      xs.push_back(p);
+    }
+    for (int l = 0; l < L; ++l) {
+      float* p;
+      SB_TRY(devt(nd, &p));
+      xmid.push_back(p);
+      for (auto* vec : {&mean1, &rstd1, &mean2, &rstd2}) {
+        SB_TRY(devt(N, &p));
+        vec->push_back(p);
+      }
+      SB_TRY(devt(static_cast<size_t>(B) * H * T, &p));
+      lse.push_back(p);
+      void* q;
+      SB_TRY(dev(nd * es, &q));
+      h1.push_back(q);
+      SB_TRY(dev(nd * es, &q));
+      h2.push_back(q);
+      SB_TRY(dev(3 * nd * es, &q));
+      qkv.push_back(q);
+      SB_TRY(dev(nd * es, &q));
+      att.push_back(q);
+      SB_TRY(dev(4 * nd * es, &q));
+      u.push_back(q);
+      SB_TRY(dev(4 * nd * es, &q));
+      gact.push_back(q);
+    }
+    SB_TRY(devt(N, &meanf));
+    SB_TRY(devt(N, &rstdf));
+    SB_TRY(dev(nd * es, &hf));
+    SB_TRY(dev(static_cast<size_t>(N) * ldl * es, &logits));
+    SB_TRY(dev(static_cast<size_t>(N) * ldl * es, &dlogits));
+    cudaMemset(logits, 0, static_cast<size_t>(N) * ldl * es);
+    cudaMemset(dlogits, 0, static_cast<size_t>(N) * ldl * es);
+    SB_TRY(devt(nd, &dres));
+    if (bf) SB_TRY(dev(nd * 2, &dres_bf));
+    SB_TRY(devt(nd, &dh));
+    SB_TRY(dev(4 * nd * es, &du));
+    SB_TRY(dev(nd * es, &dout));
+    SB_TRY(dev(3 * nd * es, &dqkv));
+
+    size_t w = 0;
+    for (auto& d : all_gemms()) w = std::max(w, gemm_workspace_bytes(d, bf));
+    w = std::max(w, layernorm_bwd_workspace_bytes(N, D));
+    w = std::max(w, cross_entropy_workspace_bytes(N));
+    w = std::max(w, attention_bwd_workspace_bytes(!bf, AttnShape{B, T, H, D / H}));
+    w = std::max(w, embedding_bwd_workspace_bytes(V, D));
+    ws_bytes = align256(w);
+    SB_TRY(devt(ws_bytes / 4 + 64, &ws));
+    return nullptr;
+  }
+
+  // Launches the whole fwd+VJP step on `st` (optionally with the gradient
+  // all-reduce on the session's comm stream).
+  sb_status enqueue(Session& s, cudaStream_t st) {
+    int* err = s.err_word;
+    const bool f32 = !bf;
+    const bool dp = s.comm != nullptr && s.world > 1;
+    const AttnShape ash{B, T, H, D / H};
+    int rc = 0;
+#define SB_K(expr)                                                                                  \
+  do {                                                                                              \
+    rc = (expr);                                                                                    \
+    if (rc) return make_status(SB_STATUS_INTERNAL, std::string("launch failed (") + std::to_string(rc) + "): " #expr); \
+  } while (0)
+    const int iw = 3 + 6 * L, ip = 2 + 6 * L, ilnf = 1 + 6 * L;
+
+    // ---- forward
+    SB_K(embedding_fwd(ids, Pp(iw), Pp(ip), f32, xs[0], N, T, V, D, st));
+    for (int l = 0; l < L; ++l) {
+      const int b0 = 1 + 6 * l;
+      SB_K(layernorm_fwd(xs[l], Pp(b0 + 2), f32, h1[l], f32, mean1[l], rstd1[l], N, D, st));
+      SB_K(gemm(desc(h1[l], D, false, Pp(b0 + 0), D, false, N, 3 * D, D, qkv[l], 3 * D, f32), st, err));
+      SB_K(attention_fwd(qkv[l], f32, att[l], lse[l], ash, st));
+      {
+        GemmDesc d = desc(att[l], D, false, Pp(b0 + 1), D, false, N, D, D, xmid[l], D, true);
+        d.epi = EPI_ADD;
+        d.aux = xs[l];
+        d.ldaux = D;
+        d.aux_f32 = true;
+        SB_K(gemm(d, st, err));
+      }
+      SB_K(layernorm_fwd(xmid[l], Pp(b0 + 3), f32, h2[l], f32, mean2[l], rstd2[l], N, D, st));
+      {
+        GemmDesc d = desc(h2[l], D, false, Pp(b0 + 4), D, false, N, 4 * D, D, u[l], 4 * D, f32);
+        d.epi = EPI_GELU;
+        d.out2 = gact[l];
+        d.ldo2 = 4 * D;
+        SB_K(gemm(d, st, err));
+      }
+      {
+        GemmDesc d = desc(gact[l], 4 * D, false, Pp(b0 + 5), 4 * D, false, N, D, 4 * D, xs[l + 1], D, true);
+        d.epi = EPI_ADD;
+        d.aux = xmid[l];
+        d.ldaux = D;
+        d.aux_f32 = true;
+        SB_K(gemm(d, st, err));
+      }
+    }
+    SB_K(layernorm_fwd(xs[L], Pp(ilnf), f32, hf, f32, meanf, rstdf, N, D, st));
+    SB_K(gemm(desc(hf, D, false, Pp(0), D, false, N, V, D, logits, ldl, f32), st, err));
+    SB_K(cross_entropy_fwd_bwd(logits, f32, ldl, N, V, ids + N, dlogits, ldl, ws, loss_f32, nullptr, st));
+
+    // ---- backward
+    SB_K(gemm(desc(dlogits, ldl, false, Pp(0), D, true, N, D, V, dh, D, true), st, err));
+    SB_K(gemm(desc(dlogits, ldl, true, hf, D, true, V, D, N, Gp(0), D, f32), st, err));
+    if (cudaMemsetAsync(dres, 0, static_cast<size_t>(N) * D * sizeof(float), st) != cudaSuccess)
+      return make_status(SB_STATUS_INTERNAL, "memset failed");
+    SB_K(layernorm_bwd(dh, true, xs[L], meanf, rstdf, Pp(ilnf), f32, dres, static_cast<__nv_bfloat16*>(dres_bf),
+                       Gp(ilnf), f32, ws, N, D, st));
+    int bucket = 0;
+    auto launch_bucket = [&](size_t lo_off, size_t hi_off) -> sb_status {
+      if (!dp) return nullptr;
+      cudaEvent_t ev = bucket_events[bucket++];
+      SB_CUDA_TRY(cudaEventRecord(ev, st));
+      SB_CUDA_TRY(cudaStreamWaitEvent(s.comm_stream, ev, 0));
+      return comm_allreduce_avg(s, grads + lo_off, (hi_off - lo_off) / es, g.elem, s.comm_stream);
+    };
+    SB_TRY(launch_bucket(offs[0], offs[1]));
+    const void* opnd = bf ? dres_bf : static_cast<void*>(dres);
+    for (int l = L - 1; l >= 0; --l) {
+      const int b0 = 1 + 6 * l;
+      SB_K(gemm(desc(opnd, D, true, gact[l], 4 * D, true, D, 4 * D, N, Gp(b0 + 5), 4 * D, f32), st, err));
+      {
+        GemmDesc d = desc(opnd, D, false, Pp(b0 + 5), 4 * D, true, N, 4 * D, D, du, 4 * D, f32);
+        d.epi = EPI_GELU_BWD;
+        d.aux = u[l];
+        d.ldaux = 4 * D;
+        d.aux_f32 = f32;
+        SB_K(gemm(d, st, err));
+      }
+      SB_K(gemm(desc(du, 4 * D, true, h2[l], D, true, 4 * D, D, N, Gp(b0 + 4), D, f32), st, err));
+      SB_K(gemm(desc(du, 4 * D, false, Pp(b0 + 4), D, true, N, D, 4 * D, dh, D, true), st, err));
+      SB_K(layernorm_bwd(dh, true, xmid[l], mean2[l], rstd2[l], Pp(b0 + 3), f32, dres,
+                         static_cast<__nv_bfloat16*>(dres_bf), Gp(b0 + 3), f32, ws, N, D, st));
+      SB_K(gemm(desc(opnd, D, true, att[l], D, true, D, D, N, Gp(b0 + 1), D, f32), st, err));
+      SB_K(gemm(desc(opnd, D, false, Pp(b0 + 1), D, true, N, D, D, dout, D, f32), st, err));
+      SB_K(attention_bwd(qkv[l], att[l], dout, lse[l], f32, dqkv, ws, ash, st));
+      SB_K(gemm(desc(dqkv, 3 * D, true, h1[l], D, true, 3 * D, D, N, Gp(b0 + 0), D, f32), st, err));
+      SB_K(gemm(desc(dqkv, 3 * D, false, Pp(b0 + 0), D, true, N, D, 3 * D, dh, D, true), st, err));
+      SB_K(layernorm_bwd(dh, true, xs[l], mean1[l], rstd1[l], Pp(b0 + 2), f32, dres,
+                         static_cast<__nv_bfloat16*>(dres_bf), Gp(b0 + 2), f32, ws, N, D, st));
+      // layer l's six gradients (plus ln_f after the last layer) are final
+      SB_TRY(launch_bucket(offs[b0], l == L - 1 ? offs[ip] : offs[b0 + 6]));
+    }
+    SB_K(embedding_bwd(ids, dres, B, T, P, V, D, Gp(iw), Gp(ip), f32, ws, st));
+    SB_TRY(launch_bucket(offs[ip], grads_bytes));
+    if (dp) {
+      SB_TRY(comm_allreduce_avg(s, loss_f32, 1, SB_ELEM_F32, s.comm_stream));
+      SB_CUDA_TRY(cudaEventRecord(comm_done, s.comm_stream));
+      SB_CUDA_TRY(cudaStreamWaitEvent(st, comm_done, 0));
+    }
+    if (bf)
+      SB_K(convert_f32_to_bf16(loss_f32, reinterpret_cast<__nv_bfloat16*>(grads + loss_off), 1, st));
+    else
+      SB_CUDA_TRY(cudaMemcpyAsync(grads + loss_off, loss_f32, 4, cudaMemcpyDeviceToDevice, st));
+#undef SB_K
+    return nullptr;
+  }
+
+  sb_status check_inputs(const std::vector<Buffer*>& in) const {
+    const size_t nleaf = shapes.size();
+    SB_RETURN_IF(in.size() != nleaf + 2, SB_STATUS_INVALID_ARGUMENT,
+                 "value_and_grad expects " + std::to_string(nleaf + 2) + " inputs, got " + std::to_string(in.size()));
+    for (size_t i = 0; i < nleaf; ++i) {
+      SB_RETURN_IF(in[i]->elem != g.elem, SB_STATUS_INVALID_ARGUMENT, "leaf " + std::to_string(i) + ": element type");
+      SB_RETURN_IF(in[i]->shape != shapes[i], SB_STATUS_INVALID_ARGUMENT, "leaf " + std::to_string(i) + ": shape");
+    }
+    for (size_t i = nleaf; i < nleaf + 2; ++i) {
+      SB_RETURN_IF(in[i]->elem != SB_ELEM_F32, SB_STATUS_INVALID_ARGUMENT, "token ids must be f32");
+      SB_RETURN_IF(in[i]->shape != std::vector<int64_t>({B, T}), SB_STATUS_INVALID_ARGUMENT,
+                   "token ids must be [batch, seq]");
+    }
+    return nullptr;
+  }
+
+  sb_status copy_in(Session& s, const std::vector<Buffer*>& in, cudaStream_t st) {
+    std::vector<std::pair<const void*, std::pair<void*, size_t>>> segs;
+    for (size_t i = 0; i < shapes.size(); ++i) segs.push_back({in[i]->data(), {Pp(static_cast<int>(i)), in[i]->bytes()}});
+    segs.push_back({in[shapes.size()]->data(), {ids, static_cast<size_t>(N) * 4}});
+    segs.push_back({in[shapes.size() + 1]->data(), {ids + N, static_cast<size_t>(N) * 4}});
+    for (size_t base = 0; base < segs.size(); base += kMaxSegs) {
+      CopySegs c{};
+      c.n = static_cast<int>(std::min<size_t>(kMaxSegs, segs.size() - base));
+      size_t maxb = 0;
+      for (int j = 0; j < c.n; ++j) {
+        c.src[j] = static_cast<const char*>(segs[base + j].first);
+        c.dst[j] = static_cast<char*>(segs[base + j].second.first);
+        c.bytes[j] = segs[base + j].second.second;
+        maxb = std::max<size_t>(maxb, c.bytes[j]);
+      }
+      const int gx = static_cast<int>(std::min<size_t>((maxb / 16 + 255) / 256 + 1, 64));
+      batched_copy_kernel<<<dim3(gx, c.n), 256, 0, st>>>(c);
+      SB_CUDA_TRY(cudaPeekAtLastError());
+      s.kernel_launches++;
+    }
+    return nullptr;
+  }
+
+  sb_status call(Session& s, const std::string& fn, const std::vector<Buffer*>& in,
+                 std::vector<Buffer*>& out) override {
+    SB_RETURN_IF(fn != "value_and_grad", SB_STATUS_NOT_FOUND, "unknown function " + fn);
+    SB_TRY(check_inputs(in));
+    cudaStream_t st = s.stream;
+    const bool dp = s.comm != nullptr && s.world > 1;
+    if (dp && bucket_events.empty()) {
+      for (int i = 0; i < L + 2; ++i) {
+        cudaEvent_t e;
+        SB_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        bucket_events.push_back(e);
+      }
+      SB_CUDA_TRY(cudaEventCreateWithFlags(&comm_done, cudaEventDisableTiming));
+    }
+    SB_TRY(copy_in(s, in, st));
+    if (!use_graph || eager_runs < 1) {
+      SB_TRY(enqueue(s, st));
+      ++eager_runs;
+    } else {
+      if (!exec) {
+        cudaGraph_t graph = nullptr;
+        SB_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        sb_status e = enqueue(s, st);
+        cudaError_t ce = cudaStreamEndCapture(st, &graph);
+        if (e) {
+          if (graph) cudaGraphDestroy(graph);
+          return e;
+        }
+        if (ce != cudaSuccess) return make_status(SB_STATUS_INTERNAL, std::string("graph capture: ") + cudaGetErrorString(ce));
+        size_t nnodes = 0;
+        cudaGraphGetNodes(graph, nullptr, &nnodes);
+        std::vector<cudaGraphNode_t> nodes(nnodes);
+        cudaGraphGetNodes(graph, nodes.data(), &nnodes);
+        kernels_per_step = 0;
+        for (auto n : nodes) {
+          cudaGraphNodeType t;
+          if (cudaGraphNodeGetType(n, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels_per_step;
+        }
+        ce = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ce != cudaSuccess) return make_status(SB_STATUS_INTERNAL, std::string("graph instantiate: ") + cudaGetErrorString(ce));
+        s.graph_captures++;
+      }
+      SB_CUDA_TRY(cudaGraphLaunch(exec, st));
+      s.graph_replays++;
+      s.kernel_launches += kernels_per_step;
+    }
+    // outputs: one pool allocation holds every gradient and the loss
+    Allocation* a = nullptr;
+    SB_TRY(session_alloc(s, out_bytes, &a));
+    SB_CUDA_TRY(cudaMemcpyAsync(a->ptr, grads, out_bytes, cudaMemcpyDeviceToDevice, st));
+    a->refs.store(static_cast<int>(shapes.size()) + 1);
+    out.push_back(buffer_new(s, a, loss_off, {}, g.elem));
+    for (size_t i = 0; i < shapes.size(); ++i) out.push_back(buffer_new(s, a, offs[i], shapes[i], g.elem));
+    return nullptr;
+  }
+};
+
+}  // namespace
+
+sb_status make_gpt_vag_module(Session& s, const std::string& name, const GptShape& g, std::unique_ptr<Module>* out) {
+  auto m = std::make_unique<GptVagModule>();
+  sb_status st = m->build(name, g);
+  if (st) return st;
+  *out = std::move(m);
+  return nullptr;
+}
+
+}  // namespace sb

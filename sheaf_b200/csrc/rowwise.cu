@@ -1,0 +1,518 @@
+// Bandwidth-bound row-wise kernels of the nanoGPT fwd+VJP step:
+//   * layer-norm without beta, forward and VJP   (examples/nanogpt/model.shf:11-14;
+//     two-pass population variance, lowering/codegen/reduction_builtins.rs:287-358;
+//     VJP from the `/`, `-`, `sqrt`, `var`, `mean` rules, autodiff/reverse.rs:551-583,
+//     847-914, 961-967)
+//   * cross-entropy loss with its VJP fused       (lib/nn.shf:28-30,44-50; one-hot
+//     via iota/compare/select, lowering/stablehlo/tensor_ops.rs:163-217)
+//   * token + position embedding gather and its scatter-add VJP
+//     (lowering/stablehlo/indexing_ops.rs:416-484, autodiff/reverse.rs:1077-1122,
+//     slice_grad/pad lowering/codegen/builtins.rs:208-271)
+// All loads/stores are 128-bit vectorised where the row layout allows; row
+// reductions use warp shuffles (plus shared memory across warps).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "sb_nn.h"
+
+namespace sb {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ float load1(const T* p);
+template <>
+__device__ __forceinline__ float load1<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float load1<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+template <typename T>
+__device__ __forceinline__ void store1(T* p, float v);
+template <>
+__device__ __forceinline__ void store1<float>(float* p, float v) { *p = v; }
+template <>
+__device__ __forceinline__ void store1<__nv_bfloat16>(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+// Loads 4 consecutive elements as floats (16-byte aligned for f32, 8 for bf16).
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p);
+template <>
+__device__ __forceinline__ float4 load4<float>(const float* p) { return *reinterpret_cast<const float4*>(p); }
+template <>
+__device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* p) {
+  uint2 u = *reinterpret_cast<const uint2*>(p);
+  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&u.x), b = *reinterpret_cast<__nv_bfloat162*>(&u.y);
+  float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+  return make_float4(fa.x, fa.y, fb.x, fb.y);
+}
+
+template <typename T>
+__device__ __forceinline__ void store4(T* p, float4 v);
+template <>
+__device__ __forceinline__ void store4<float>(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float4 v) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+// ---------------------------------------------------------------------------
+// Layer norm (no beta). One warp per row; each lane holds VPT float4 chunks
+// (lane*4 + j*128). D must be a multiple of 4 and <= VPT*128.
+// ---------------------------------------------------------------------------
+
+template <int VPT, typename TO>
+__global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x, const void* __restrict__ gamma,
+                                                     int gamma_f32, TO* __restrict__ y, float* __restrict__ mean_out,
+                                                     float* __restrict__ rstd_out, int rows, int D) {
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + threadIdx.x / 32; row < rows; row += gridDim.x * warps) {
+    const float* xr = x + static_cast<long>(row) * D;
+    float4 v[VPT];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = lane * 4 + j * 128;
+      v[j] = (c < D) ? load4(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    }
+    const float mean = warp_sum(s) / static_cast<float>(D);
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = lane * 4 + j * 128;
+      if (c < D) {
+        const float a = v[j].x - mean, b = v[j].y - mean, cc = v[j].z - mean, d = v[j].w - mean;
+        q += (a * a + b * b) + (cc * cc + d * d);
+      }
+    }
+    const float var = warp_sum(q) / static_cast<float>(D);
+    const float sd = sqrtf(var + 1e-5f);
+    const float rstd = 1.0f / sd;
+    TO* yr = y + static_cast<long>(row) * D;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = lane * 4 + j * 128;
+      if (c < D) {
+        float4 g;
+        if (gamma_f32)
+          g = load4(static_cast<const float*>(gamma) + c);
+        else
+          g = load4(static_cast<const __nv_bfloat16*>(gamma) + c);
+        float4 o = make_float4(((v[j].x - mean) / sd) * g.x, ((v[j].y - mean) / sd) * g.y,
+                               ((v[j].z - mean) / sd) * g.z, ((v[j].w - mean) / sd) * g.w);
+        store4(yr + c, o);
+      }
+    }
+    if (lane == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+}
+
+// dx = rstd * (dxh - mean(dxh) - xhat * mean(dxh * xhat)), dxh = dy * gamma.
+// dres (f32) += dx; optional bf16 copy of the updated dres; per-block partial
+// sums of dgamma = sum_rows dy * xhat into dgamma_part[blockIdx.x][D].
+template <int VPT, typename TI>
+__global__ void __launch_bounds__(256) ln_bwd_kernel(const TI* __restrict__ dy, const float* __restrict__ x,
+                                                     const float* __restrict__ mean_in,
+                                                     const float* __restrict__ rstd_in, const void* __restrict__ gamma,
+                                                     int gamma_f32, float* __restrict__ dres,
+                                                     __nv_bfloat16* __restrict__ dres_bf,
+                                                     float* __restrict__ dgamma_part, int rows, int D) {
+  extern __shared__ float sm_dg[];  // [warps][D]
+  const int warps = blockDim.x / 32;
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  float4 g[VPT], dg[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int c = lane * 4 + j * 128;
+    if (c < D)
+      g[j] = gamma_f32 ? load4(static_cast<const float*>(gamma) + c)
+                       : load4(static_cast<const __nv_bfloat16*>(gamma) + c);
+    else
+      g[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    dg[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int row = blockIdx.x * warps + warp; row < rows; row += gridDim.x * warps) {
+    const long off = static_cast<long>(row) * D;
+    const float mean = mean_in[row], rstd = rstd_in[row];
+    float4 xh[VPT], dxh[VPT];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = lane * 4 + j * 128;
+      if (c < D) {
+        const float4 xv = load4(x + off + c);
+        const float4 dv = load4(dy + off + c);
+        xh[j] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd, (xv.w - mean) * rstd);
+        dxh[j] = make_float4(dv.x * g[j].x, dv.y * g[j].y, dv.z * g[j].z, dv.w * g[j].w);
+        dg[j].x += dv.x * xh[j].x;
+        dg[j].y += dv.y * xh[j].y;
+        dg[j].z += dv.z * xh[j].z;
+        dg[j].w += dv.w * xh[j].w;
+        s1 += (dxh[j].x + dxh[j].y) + (dxh[j].z + dxh[j].w);
+        s2 += (dxh[j].x * xh[j].x + dxh[j].y * xh[j].y) + (dxh[j].z * xh[j].z + dxh[j].w * xh[j].w);
+      } else {
+        xh[j] = dxh[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    const float c1 = warp_sum(s1) / static_cast<float>(D);
+    const float c2 = warp_sum(s2) / static_cast<float>(D);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = lane * 4 + j * 128;
+      if (c < D) {
+        float4 r = load4(dres + off + c);
+        r.x += rstd * (dxh[j].x - c1 - xh[j].x * c2);
+        r.y += rstd * (dxh[j].y - c1 - xh[j].y * c2);
+        r.z += rstd * (dxh[j].z - c1 - xh[j].z * c2);
+        r.w += rstd * (dxh[j].w - c1 - xh[j].w * c2);
+        store4(dres + off + c, r);
+        if (dres_bf) store4(dres_bf + off + c, r);
+      }
+    }
+  }
+  // reduce dgamma over the block's warps, in a fixed order
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int c = lane * 4 + j * 128;
+    if (c < D) *reinterpret_cast<float4*>(&sm_dg[warp * D + c]) = dg[j];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float acc = 0.f;
+    for (int w = 0; w < warps; ++w) acc += sm_dg[w * D + c];
+    dgamma_part[static_cast<long>(blockIdx.x) * D + c] = acc;
+  }
+}
+
+// out[c] = sum_b part[b][c] (fixed order), written as f32 or bf16.
+__global__ void column_sum_kernel(const float* __restrict__ part, int nparts, int D, void* out, int out_f32) {
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < D; c += gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int b = 0; b < nparts; ++b) acc += part[static_cast<long>(b) * D + c];
+    if (out_f32)
+      static_cast<float*>(out)[c] = acc;
+    else
+      static_cast<__nv_bfloat16*>(out)[c] = __float2bfloat16_rn(acc);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Cross-entropy: per row r, lse = log-sum-exp, row contribution lp[y] =
+// x[y] - lse, dlogits = (softmax - onehot(y)) * (1/rows). One warp per row.
+// ---------------------------------------------------------------------------
+
+template <typename T>
+__global__ void __launch_bounds__(256) ce_fwd_bwd_kernel(const T* __restrict__ logits, long ld, int rows, int V,
+                                                         const float* __restrict__ targets, T* __restrict__ dlogits,
+                                                         long ldd, float* __restrict__ row_part, float inv_rows) {
+  const int warps = blockDim.x / 32;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  __shared__ float sm_part[32];
+  float part = 0.f;
+  for (int row = blockIdx.x * warps + warp; row < rows; row += gridDim.x * warps) {
+    const T* lr = logits + static_cast<long>(row) * ld;
+    float m = -INFINITY, s = 0.f;
+    for (int c = lane; c < V; c += 32) {
+      const float v = load1(lr + c);
+      const float nm = fmaxf(m, v);
+      s = s * expf(m - nm) + expf(v - nm);
+      m = nm;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const float nm = fmaxf(m, m2);
+      s = s * expf(m - nm) + s2 * expf(m2 - nm);
+      m = nm;
+    }
+    const float logs = logf(s);
+    const int y = static_cast<int>(targets[row]);  // f32 -> i32 truncation
+    if (lane == 0 && y >= 0 && y < V) part += (load1(lr + y) - m) - logs;
+    T* dr = dlogits + static_cast<long>(row) * ldd;
+    for (int c = lane; c < V; c += 32) {
+      const float p = expf((load1(lr + c) - m) - logs);
+      store1(dr + c, (p - (c == y ? 1.f : 0.f)) * inv_rows);
+    }
+  }
+  if (lane == 0) sm_part[warp] = part;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float acc = 0.f;
+    for (int w = 0; w < warps; ++w) acc += sm_part[w];
+    row_part[blockIdx.x] = acc;
+  }
+}
+
+// loss = -(sum of block partials) / rows, written as f32 and/or bf16.
+__global__ void ce_finish_kernel(const float* __restrict__ part, int nparts, float inv_rows, float* loss_f32,
+                                 __nv_bfloat16* loss_bf16) {
+  __shared__ float sm[256];
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) acc += part[i];
+  sm[threadIdx.x] = acc;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if (threadIdx.x < s) sm[threadIdx.x] += sm[threadIdx.x + s];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const float loss = -sm[0] * inv_rows;
+    if (loss_f32) *loss_f32 = loss;
+    if (loss_bf16) *loss_bf16 = __float2bfloat16_rn(loss);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Embedding: x[b*T+t, :] = wte[clamp(id)] + wpe[t]   (f32 residual stream)
+// ---------------------------------------------------------------------------
+
+template <typename TW>
+__global__ void embed_fwd_kernel(const float* __restrict__ ids, const TW* __restrict__ wte,
+                                 const TW* __restrict__ wpe, float* __restrict__ x, int ntok, int T, int V, int D) {
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x & 31;
+  for (int n = blockIdx.x * warps + threadIdx.x / 32; n < ntok; n += gridDim.x * warps) {
+    int id = static_cast<int>(ids[n]);
+    id = min(max(id, 0), V - 1);
+    const TW* a = wte + static_cast<long>(id) * D;
+    const TW* p = wpe + static_cast<long>(n % T) * D;
+    float* o = x + static_cast<long>(n) * D;
+    for (int c = lane * 4; c < D; c += 128) {
+      const float4 u = load4(a + c), w = load4(p + c);
+      store4(o + c, make_float4(u.x + w.x, u.y + w.y, u.z + w.z, u.w + w.w));
+    }
+  }
+}
+
+// dwte for a small vocabulary, deterministic: block (v, column chunk) sums the
+// rows of every token whose id is v, in token order.
+__global__ void embed_bwd_small_kernel(const float* __restrict__ ids, const float* __restrict__ dx, int ntok, int V,
+                                       int D, void* dwte, int out_f32) {
+  const int v = blockIdx.x;
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  __shared__ int sm_idx[1024];
+  float acc = 0.f;
+  for (int base = 0; base < ntok; base += 1024) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < 1024; i += blockDim.x)
+      sm_idx[i] = (base + i < ntok) ? static_cast<int>(ids[base + i]) : -1;
+    __syncthreads();
+    if (c < D) {
+      const int lim = min(1024, ntok - base);
+      for (int i = 0; i < lim; ++i)
+        if (sm_idx[i] == v) acc += dx[static_cast<long>(base + i) * D + c];
+    }
+  }
+  if (c < D) {
+    if (out_f32)
+      static_cast<float*>(dwte)[static_cast<long>(v) * D + c] = acc;
+    else
+      static_cast<__nv_bfloat16*>(dwte)[static_cast<long>(v) * D + c] = __float2bfloat16_rn(acc);
+  }
+}
+
+// dwte for a large vocabulary: fp32 atomics into a zeroed f32 accumulator.
+__global__ void embed_bwd_atomic_kernel(const float* __restrict__ ids, const float* __restrict__ dx, int ntok, int V,
+                                        int D, float* __restrict__ acc) {
+  const int warps = blockDim.x / 32;
+  const int lane = threadIdx.x & 31;
+  for (int n = blockIdx.x * warps + threadIdx.x / 32; n < ntok; n += gridDim.x * warps) {
+    const int id = static_cast<int>(ids[n]);
+    if (id < 0 || id >= V) continue;
+    const float* g = dx + static_cast<long>(n) * D;
+    float* o = acc + static_cast<long>(id) * D;
+    for (int c = lane; c < D; c += 32) atomicAdd(o + c, g[c]);
+  }
+}
+
+// dwpe[t, :] = sum_b dx[b*T + t, :] for t < T; rows T..P-1 are zero (pad).
+__global__ void embed_bwd_pos_kernel(const float* __restrict__ dx, int B, int T, int P, int D, void* dwpe,
+                                     int out_f32) {
+  const long total = static_cast<long>(P) * D;
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const long t = i / D, c = i % D;
+    float acc = 0.f;
+    if (t < T)
+      for (int b = 0; b < B; ++b) acc += dx[(static_cast<long>(b) * T + t) * D + c];
+    if (out_f32)
+      static_cast<float*>(dwpe)[i] = acc;
+    else
+      static_cast<__nv_bfloat16*>(dwpe)[i] = __float2bfloat16_rn(acc);
+  }
+}
+
+__global__ void convert_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, long n) {
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x)
+    out[i] = __float2bfloat16_rn(in[i]);
+}
+
+int grid_for(long work_items, int per_block) {
+  const long b = (work_items + per_block - 1) / per_block;
+  return static_cast<int>(std::max<long>(1, std::min<long>(b, 16L * num_sms_cached())));
+}
+
+}  // namespace
+
+int num_sms_cached() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+#define SB_LN_DISPATCH(VPT_EXPR, LAUNCH)          \
+  do {                                            \
+    const int vpt_ = (VPT_EXPR);                  \
+    if (vpt_ <= 1) { constexpr int V = 1; LAUNCH; } \
+    else if (vpt_ <= 2) { constexpr int V = 2; LAUNCH; } \
+    else if (vpt_ <= 3) { constexpr int V = 3; LAUNCH; } \
+    else if (vpt_ <= 4) { constexpr int V = 4; LAUNCH; } \
+    else if (vpt_ <= 6) { constexpr int V = 6; LAUNCH; } \
+    else if (vpt_ <= 8) { constexpr int V = 8; LAUNCH; } \
+    else if (vpt_ <= 16) { constexpr int V = 16; LAUNCH; } \
+    else if (vpt_ <= 32) { constexpr int V = 32; LAUNCH; } \
+    else return 1;                                \
+  } while (0)
+
+int layernorm_fwd(const float* x, const void* gamma, bool gamma_f32, void* y, bool y_f32, float* mean, float* rstd,
+                  int rows, int D, cudaStream_t s) {
+  if (rows <= 0 || D <= 0 || (D & 3)) return 1;
+  const int warps = 8;
+  const int grid = std::min((rows + warps - 1) / warps, 8 * num_sms_cached());
+  if (y_f32)
+    SB_LN_DISPATCH((D + 127) / 128, (ln_fwd_kernel<V, float><<<grid, warps * 32, 0, s>>>(
+                                        x, gamma, gamma_f32, static_cast<float*>(y), mean, rstd, rows, D)));
+  else
+    SB_LN_DISPATCH((D + 127) / 128, (ln_fwd_kernel<V, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
+                                        x, gamma, gamma_f32, static_cast<__nv_bfloat16*>(y), mean, rstd, rows, D)));
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+size_t layernorm_bwd_workspace_bytes(int rows, int D) {
+  const int grid = std::min((rows + 7) / 8, 2 * num_sms_cached());
+  return static_cast<size_t>(grid) * D * sizeof(float);
+}
+
+int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean, const float* rstd, const void* gamma,
+                  bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma, bool dgamma_f32, float* ws,
+                  int rows, int D, cudaStream_t s) {
+  if (rows <= 0 || D <= 0 || (D & 3)) return 1;
+  const int warps = 8;
+  const int grid = std::min((rows + warps - 1) / warps, 2 * num_sms_cached());
+  const size_t smem = static_cast<size_t>(warps) * D * sizeof(float);
+  if (smem > 200 * 1024) return 1;
+  if (dy_f32)
+    SB_LN_DISPATCH((D + 127) / 128, ({
+      auto k = ln_bwd_kernel<V, float>;
+      if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      k<<<grid, warps * 32, smem, s>>>(static_cast<const float*>(dy), x, mean, rstd, gamma, gamma_f32, dres, dres_bf,
+                                       ws, rows, D);
+    }));
+  else
+    SB_LN_DISPATCH((D + 127) / 128, ({
+      auto k = ln_bwd_kernel<V, __nv_bfloat16>;
+      if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      k<<<grid, warps * 32, smem, s>>>(static_cast<const __nv_bfloat16*>(dy), x, mean, rstd, gamma, gamma_f32, dres,
+                                       dres_bf, ws, rows, D);
+    }));
+  if (cudaPeekAtLastError() != cudaSuccess) return 4;
+  column_sum_kernel<<<(D + 255) / 256, 256, 0, s>>>(ws, grid, D, dgamma, dgamma_f32);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+size_t cross_entropy_workspace_bytes(int rows) {
+  return static_cast<size_t>(std::min((rows + 7) / 8, 4 * num_sms_cached())) * sizeof(float);
+}
+
+int cross_entropy_fwd_bwd(const void* logits, bool f32, long ld, int rows, int V, const float* targets, void* dlogits,
+                          long ldd, float* ws, float* loss_f32, __nv_bfloat16* loss_bf16, cudaStream_t s) {
+  if (rows <= 0 || V <= 0) return 1;
+  const int warps = 8;
+  const int grid = std::min((rows + warps - 1) / warps, 4 * num_sms_cached());
+  const float inv = 1.0f / static_cast<float>(rows);
+  if (f32)
+    ce_fwd_bwd_kernel<float><<<grid, warps * 32, 0, s>>>(static_cast<const float*>(logits), ld, rows, V, targets,
+                                                         static_cast<float*>(dlogits), ldd, ws, inv);
+  else
+    ce_fwd_bwd_kernel<__nv_bfloat16><<<grid, warps * 32, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), ld, rows,
+                                                                 V, targets, static_cast<__nv_bfloat16*>(dlogits), ldd,
+                                                                 ws, inv);
+  if (cudaPeekAtLastError() != cudaSuccess) return 4;
+  ce_finish_kernel<<<1, 256, 0, s>>>(ws, grid, inv, loss_f32, loss_bf16);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+int embedding_fwd(const float* ids, const void* wte, const void* wpe, bool f32, float* x, int ntok, int T, int V,
+                  int D, cudaStream_t s) {
+  if (ntok <= 0 || (D & 3)) return 1;
+  const int grid = std::min((ntok + 7) / 8, 8 * num_sms_cached());
+  if (f32)
+    embed_fwd_kernel<float><<<grid, 256, 0, s>>>(ids, static_cast<const float*>(wte), static_cast<const float*>(wpe),
+                                                 x, ntok, T, V, D);
+  else
+    embed_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(ids, static_cast<const __nv_bfloat16*>(wte),
+                                                         static_cast<const __nv_bfloat16*>(wpe), x, ntok, T, V, D);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+size_t embedding_bwd_workspace_bytes(int V, int D) {
+  return (V > kEmbedSmallVocab) ? static_cast<size_t>(V) * D * sizeof(float) : 0;
+}
+
+int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V, int D, void* dwte, void* dwpe,
+                  bool out_f32, float* ws, cudaStream_t s) {
+  const int ntok = B * T;
+  if (V <= kEmbedSmallVocab) {
+    dim3 grid(V, (D + 127) / 128);
+    embed_bwd_small_kernel<<<grid, 128, 0, s>>>(ids, dx, ntok, V, D, dwte, out_f32);
+  } else {
+    float* acc = out_f32 ? static_cast<float*>(dwte) : ws;
+    if (!acc) return 5;
+    cudaMemsetAsync(acc, 0, static_cast<size_t>(V) * D * sizeof(float), s);
+    embed_bwd_atomic_kernel<<<std::min((ntok + 7) / 8, 8 * num_sms_cached()), 256, 0, s>>>(ids, dx, ntok, V, D, acc);
+    if (!out_f32) {
+      const long n = static_cast<long>(V) * D;
+      convert_kernel<<<grid_for(n, 256), 256, 0, s>>>(acc, static_cast<__nv_bfloat16*>(dwte), n);
+    }
+  }
+  if (cudaPeekAtLastError() != cudaSuccess) return 4;
+  const long total = static_cast<long>(P) * D;
+  embed_bwd_pos_kernel<<<grid_for(total, 256), 256, 0, s>>>(dx, B, T, P, D, dwpe, out_f32);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+int convert_f32_to_bf16(const float* in, __nv_bfloat16* out, long n, cudaStream_t s) {
+  convert_kernel<<<grid_for(n, 256), 256, 0, s>>>(in, out, n);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+}  // namespace sb

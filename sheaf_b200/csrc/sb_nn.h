@@ -1,0 +1,55 @@
+// Host launch interface of the non-GEMM kernels (internal to the library).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+
+#include "sb_kernels.h"
+
+namespace sb {
+
+// Vocabularies up to this size use the deterministic per-row embedding VJP;
+// larger ones accumulate with fp32 atomics.
+constexpr int kEmbedSmallVocab = 4096;
+
+int num_sms_cached();
+int* device_error_word();
+
+// y = (x - mean) / sqrt(var + 1e-5) * gamma over the last dim (rows x D, f32 in).
+int layernorm_fwd(const float* x, const void* gamma, bool gamma_f32, void* y, bool y_f32, float* mean, float* rstd,
+                  int rows, int D, cudaStream_t s);
+// dres += LN-VJP(dy); dres_bf (optional) = bf16(dres); dgamma = sum_rows dy * xhat.
+size_t layernorm_bwd_workspace_bytes(int rows, int D);
+int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean, const float* rstd, const void* gamma,
+                  bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma, bool dgamma_f32, float* ws,
+                  int rows, int D, cudaStream_t s);
+
+// loss = -mean(log_softmax(logits)[target]); dlogits = (softmax - onehot) / rows.
+size_t cross_entropy_workspace_bytes(int rows);
+int cross_entropy_fwd_bwd(const void* logits, bool f32, long ld, int rows, int V, const float* targets, void* dlogits,
+                          long ldd, float* ws, float* loss_f32, __nv_bfloat16* loss_bf16, cudaStream_t s);
+
+// x[b*T+t] = wte[clamp(ids)] + wpe[t] (f32 out).
+int embedding_fwd(const float* ids, const void* wte, const void* wpe, bool f32, float* x, int ntok, int T, int V, int D,
+                  cudaStream_t s);
+// dwte = scatter-add of dx rows by id; dwpe[t] = sum_b dx[b,t] (rows >= T zero).
+size_t embedding_bwd_workspace_bytes(int V, int D);
+int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V, int D, void* dwte, void* dwpe,
+                  bool out_f32, float* ws, cudaStream_t s);
+
+int convert_f32_to_bf16(const float* in, __nv_bfloat16* out, long n, cudaStream_t s);
+
+// Causal attention over packed qkv [B*T, 3*D] (q | k | v, heads of Hd=D/H
+// columns), o [B*T, D], lse [B*H*T] (natural-log units of the scaled scores).
+struct AttnShape {
+  int B, T, H, Hd;
+};
+int attention_fwd(const void* qkv, bool f32, void* o, float* lse, const AttnShape& sh, cudaStream_t s);
+// dqkv [B*T, 3*D] from dO, O, qkv, lse. `ws` holds B*H*T floats (row dots)
+// plus, for the tensor-core path, a f32 dQ accumulator.
+size_t attention_bwd_workspace_bytes(bool f32, const AttnShape& sh);
+int attention_bwd(const void* qkv, const void* o, const void* dout, const float* lse, bool f32, void* dqkv, float* ws,
+                  const AttnShape& sh, cudaStream_t s);
+
+}  // namespace sb

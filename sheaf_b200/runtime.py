@@ -1,0 +1,202 @@
+"""Python mirror of the executor C ABI (include/sheaf_b200.h).
+
+Mirrors how Sheaf's runtime drives IREE (sheaf/src/runtime/iree_session.rs):
+a process-wide session per GPU, buffers uploaded from host arrays
+(buffer_convert.rs:14-123, bf16 rounded to nearest-even on the host), modules
+loaded into the session and invoked by "<module>.<function>" with flat leaf
+lists (iree_dispatch.rs:172-176), outputs returned as device-resident buffers
+that are read back on demand (device_buffer.rs:47-134).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import ELEM_BF16, ELEM_F16, ELEM_F32, ELEM_I32, lib
+
+NUMPY_OF_ELEM = {ELEM_F32: np.float32, ELEM_I32: np.int32}
+ELEM_SIZE = {ELEM_F32: 4, ELEM_I32: 4, ELEM_BF16: 2, ELEM_F16: 2}
+
+
+class SheafB200Error(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+        self.message = message
+
+
+def _check(status) -> None:
+    if status:
+        L = lib()
+        code = L.sb_status_code(status)
+        msg = L.sb_status_message(status).decode()
+        L.sb_status_free(status)
+        raise SheafB200Error(code, msg)
+
+
+def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    """Host-side RNE rounding of f32 to bf16 bit patterns (the conversion
+    Sheaf applies before a bf16 upload, sheaf/src/core/dtype.rs:204-216)."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    bits = a.view(np.uint32)
+    with np.errstate(over="ignore"):
+        r = ((bits + np.uint32(0x7FFF) + ((bits >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)).astype(np.uint16)
+    nan = np.isnan(a)
+    if nan.any():
+        r[nan] = (bits[nan] >> np.uint32(16)).astype(np.uint16) | np.uint16(0x40)
+    return r
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << np.uint32(16)).view(np.float32)
+
+
+class Session:
+    """One executor session on one GPU (sb_session_create)."""
+
+    def __init__(self, device: int = 0):
+        self._h = C.c_void_p()
+        _check(lib().sb_session_create(device, C.byref(self._h)))
+        self.device = device
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self) -> None:
+        if self._h:
+            lib().sb_session_release(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def synchronize(self, timeout_s: float = 60.0) -> None:
+        _check(lib().sb_session_synchronize(self._h, int(timeout_s * 1e9)))
+
+    @property
+    def stream(self) -> int:
+        return lib().sb_session_stream(self._h) or 0
+
+    def stats(self) -> dict:
+        st = _lib.SessionStats()
+        _check(lib().sb_session_get_stats(self._h, C.byref(st)))
+        return {f: getattr(st, f) for f, _ in st._fields_}
+
+    # -- groups ------------------------------------------------------------
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = (C.c_char * 128)()
+        _check(lib().sb_nccl_unique_id(buf, 128))
+        return bytes(buf)
+
+    def join_group(self, nccl_id: bytes, rank: int, world: int) -> None:
+        _check(lib().sb_session_join_group(self._h, nccl_id, len(nccl_id), rank, world))
+
+    # -- buffers -----------------------------------------------------------
+    def upload(self, array, elem: int = ELEM_F32) -> "Buffer":
+        """Host array -> new device buffer of element type `elem`."""
+        a = np.asarray(array)
+        if elem == ELEM_BF16:
+            host = f32_to_bf16_bits(a.astype(np.float32))
+        elif elem == ELEM_F32:
+            host = np.ascontiguousarray(a, dtype=np.float32)
+        elif elem == ELEM_I32:
+            host = np.ascontiguousarray(a, dtype=np.int32)
+        else:
+            raise ValueError("unsupported element type")
+        shape = (C.c_int64 * max(1, a.ndim))(*a.shape)
+        h = C.c_void_p()
+        _check(lib().sb_buffer_alloc_copy(self._h, shape, a.ndim, elem, host.ctypes.data_as(C.c_void_p),
+                                          host.nbytes, C.byref(h)))
+        return Buffer(h)
+
+    def empty(self, shape: Sequence[int], elem: int) -> "Buffer":
+        shp = (C.c_int64 * max(1, len(shape)))(*shape)
+        h = C.c_void_p()
+        _check(lib().sb_buffer_alloc(self._h, shp, len(shape), elem, C.byref(h)))
+        return Buffer(h)
+
+    # -- modules -----------------------------------------------------------
+    def load_stablehlo(self, text: str) -> str:
+        data = text.encode()
+        name = C.c_char_p()
+        _check(lib().sb_module_load_stablehlo(self._h, data, len(data), C.byref(name)))
+        return name.value.decode()
+
+    def create_gpt_vag(self, name: str, *, n_layer, n_head, n_embd, block_size, vocab_size, batch, seq,
+                       elem=ELEM_BF16) -> str:
+        cfg = _lib.GptConfig(n_layer, n_head, n_embd, block_size, vocab_size, batch, seq, elem)
+        _check(lib().sb_module_create_gpt_vag(self._h, name.encode(), C.byref(cfg)))
+        return name
+
+    def call(self, qualified_name: str, inputs: Sequence["Buffer"], max_outputs: int = 1024) -> list["Buffer"]:
+        arr = (C.c_void_p * max(1, len(inputs)))(*[b._h for b in inputs])
+        outs = (C.c_void_p * max_outputs)()
+        n = C.c_size_t()
+        _check(lib().sb_call(self._h, qualified_name.encode(), arr, len(inputs), outs, max_outputs, C.byref(n)))
+        return [Buffer(C.c_void_p(outs[i])) for i in range(n.value)]
+
+
+class Buffer:
+    """A device buffer view (sb_buffer); released when garbage collected."""
+
+    def __init__(self, handle):
+        self._h = handle
+
+    def release(self) -> None:
+        if self._h:
+            lib().sb_buffer_release(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+    @property
+    def shape(self) -> tuple[int, ...]:
+        L = lib()
+        return tuple(L.sb_buffer_dim(self._h, i) for i in range(L.sb_buffer_rank(self._h)))
+
+    @property
+    def elem(self) -> int:
+        return lib().sb_buffer_elem_type(self._h)
+
+    @property
+    def nbytes(self) -> int:
+        return lib().sb_buffer_byte_length(self._h)
+
+    @property
+    def device_ptr(self) -> int:
+        return lib().sb_buffer_device_ptr(self._h) or 0
+
+    def write(self, host: np.ndarray) -> None:
+        h = np.ascontiguousarray(host)
+        _check(lib().sb_buffer_h2d(self._h, h.ctypes.data_as(C.c_void_p), h.nbytes))
+
+    def to_host(self, timeout_s: float = 60.0) -> np.ndarray:
+        """D2H + widening to f32 (as device_buffer.rs to_host does)."""
+        e = self.elem
+        n = self.nbytes
+        if e in (ELEM_BF16, ELEM_F16):
+            raw = np.empty(n // 2, dtype=np.uint16)
+        elif e == ELEM_I32:
+            raw = np.empty(n // 4, dtype=np.int32)
+        else:
+            raw = np.empty(n // 4, dtype=np.float32)
+        _check(lib().sb_buffer_d2h(self._h, raw.ctypes.data_as(C.c_void_p), n, int(timeout_s * 1e9)))
+        if e == ELEM_BF16:
+            out = bf16_bits_to_f32(raw)
+        elif e == ELEM_F16:
+            out = raw.view(np.float16).astype(np.float32)
+        else:
+            out = raw
+        return out.reshape(self.shape)
