@@ -338,6 +338,15 @@ int attn_bwd_t(const T* qkv, const T* o, const T* dout, const float* lse, T* dqk
 
 }  // namespace
 
+int attention_delta_bf16(const void* o, const void* dout, float* delta, const AttnShape& sh, cudaStream_t s) {
+  const long rows = static_cast<long>(sh.B) * sh.H * sh.T;
+  const int g = static_cast<int>(std::min<long>((rows + 7) / 8, 8L * num_sms_cached()));
+  attn_delta<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(o),
+                                               static_cast<const __nv_bfloat16*>(dout), delta, sh.B, sh.T, sh.H,
+                                               sh.Hd);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
 int attention_fwd_simt(const void* qkv, bool f32, void* o, float* lse, const AttnShape& sh, cudaStream_t s) {
   if (f32) return attn_fwd_t(static_cast<const float*>(qkv), static_cast<float*>(o), lse, sh, s);
   return attn_fwd_t(static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(o), lse, sh, s);

@@ -1,0 +1,599 @@
+// Fused causal self-attention on the tcgen05 tensor cores (bf16 operands,
+// fp32 accumulation in TMEM): the nanoGPT attention block
+// (examples/nanogpt/model.shf:55-70)
+//   s = (q @ k^T) / sqrt(Hd); s = where(tril(ones[T,T]) == 1, s, -1e10);
+//   p = softmax(s) (lib/nn.shf:24-26); o = p @ v; heads merged to [B*T, D]
+// and its VJP (the `@`, `/`, `where` and softmax rules of
+// autodiff/reverse.rs:585-689, 551-583, 1014-1019, 814-828).
+// Masked scores contribute exp(-1e10 - max) == 0, so masked keys are skipped.
+//
+// Forward, one CTA per (batch, head, 128-query tile); 192 threads:
+//   warp 0    TMA: Q tile once, K/V tiles of 128 keys (2-stage ring)
+//   warp 1    TMEM owner + single-thread UMMA issuer:
+//             S = Q K^T (M=128, N=128, K=64) into TMEM;
+//             O_j = P V (M=128, N=64, K=128) into TMEM
+//   warps 2-5 softmax: thread = query row; reads its S row from TMEM, keeps
+//             the running max / sum, writes P (bf16, 128B-swizzled K-major)
+//             to shared memory for the P V UMMA, accumulates O_j in registers.
+// Backward, one CTA per (batch, head, 128-key tile), looping over the query
+// tiles at or after it:
+//   S^T = K Q^T and dP^T = V dO^T into TMEM (thread = key row);
+//   P^T, dS^T = P^T * (dP^T - delta) / sqrt(Hd) written to shared memory;
+//   dV += P^T dO, dK += dS^T Q (accumulated in TMEM across query tiles);
+//   dQ_i = dS K (the dS^T tile read as an MN-major operand), added into an
+//   fp32 dQ buffer with atomics, converted to bf16 at the end.
+// Q/K/V/dO tiles are 128 rows x 64 bf16 (128-byte rows), the same smem tile
+// serving as a K-major operand (rows = M/N) and an MN-major one (rows = K).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "sb_kernels.h"
+#include "sb_nn.h"
+#include "sb_ptx.cuh"
+
+namespace sb {
+
+namespace {
+
+constexpr int kT = 128;   // rows per tile
+constexpr int kHd = 64;   // head dim handled by the tensor-core path
+constexpr uint32_t kTileBytes = kT * kHd * 2;  // 16 KB
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AttnArgs {
+  int B, T, H, D;
+  int ntiles;  // ceil(T / 128)
+  float scale;  // 1 / sqrt(Hd)
+  __nv_bfloat16* out;
+  float* lse;
+  const float* delta;
+  float* dq_acc;
+  __nv_bfloat16* dqkv;
+  int* err;
+};
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ void named_bar_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Writes 32 bf16 values (columns 32c .. 32c+31 of row r) into a 128-row,
+// 128-column tile stored as two 64-column K-major SW128 atoms of 16 KB.
+__device__ __forceinline__ void store_row32(uint32_t tile, int r, int c, const uint32_t (&pk)[16]) {
+  const uint32_t row = tile + (c >> 1) * 16384 + r * 128;
+  const int c0 = (c & 1) * 4;
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    st_shared_v4(row + (((c0 + k) ^ (r & 7)) << 4), pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+}
+
+__device__ __forceinline__ uint64_t kdesc(uint32_t tile, int kk) {  // K-major, 64-wide K atom
+  return make_sw128_desc(tile + kk * 32, 16, 1024);
+}
+__device__ __forceinline__ uint64_t kdesc2(uint32_t tile, int kk) {  // K-major, K=128 as two atoms
+  return make_sw128_desc(tile + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+}
+__device__ __forceinline__ uint64_t mndesc(uint32_t tile, int kk, uint32_t lbo) {  // MN-major, K rows
+  return make_sw128_desc(tile + kk * 2048, lbo, 1024);
+}
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+
+constexpr size_t kFwdSmem = 1024 + kTileBytes /*Q*/ + 2 * kTileBytes /*K*/ + 2 * kTileBytes /*V*/ +
+                            2 * kTileBytes /*P*/ + 16 * 8 + 16;
+
+__global__ void __launch_bounds__(192, 1) attn_fwd_tc(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = sm;
+  uint8_t* sK = sQ + kTileBytes;
+  uint8_t* sV = sK + 2 * kTileBytes;
+  uint8_t* sP = sV + 2 * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kTileBytes);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* o_full = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = a.ntiles - 1 - static_cast<int>(blockIdx.x % a.ntiles);  // long rows first
+  const int bh = blockIdx.x / a.ntiles;
+  const int b = bh / a.H, h = bh % a.H;
+  const int nkv = qt + 1;
+  const int row0 = b * a.T;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(o_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_2d(sQ, &tm, q_full, h * kHd, row0 + qt * kT);
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, a.err, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
+        tma_load_2d(sK + s * kTileBytes, &tm, &kv_full[s], a.D + h * kHd, row0 + j * kT);
+        tma_load_2d(sV + s * kTileBytes, &tm, &kv_full[s], 2 * a.D + h * kHd, row0 + j * kT);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idO = make_idesc_bf16(128, 64, false, true);
+      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+      if (mbar_wait(q_full, 0, a.err, abort_flag)) {
+        for (int j = 0; j < nkv; ++j) {
+          const int s = j & 1;
+          if (!mbar_wait(&kv_full[s], (j >> 1) & 1, a.err, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sK + s * kTileBytes), v_addr = smem_u32(sV + s * kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) umma_f16(tS, kdesc(q_addr, kk), kdesc(k_addr, kk), idS, kk > 0);
+          umma_commit(s_full);
+          if (!mbar_wait(p_full, j & 1, a.err, abort_flag)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) umma_f16(tO, kdesc2(p_addr, kk), mndesc(v_addr, kk, 8192), idO, kk > 0);
+          umma_commit(o_full);
+          umma_commit(&kv_empty[s]);
+        }
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int q = qt * kT + r;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const float sl = a.scale * kLog2e;  // scores -> log2 units
+    float m = -INFINITY, l = 0.f;
+    float o[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) o[i] = 0.f;
+    const uint32_t p_addr = smem_u32(sP);
+    bool ok = true;
+    for (int j = 0; j < nkv && ok; ++j) {
+      if (!mbar_wait(s_full, j & 1, a.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int kbase = j * kT;
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tS + lane_base + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t)
+          if (kbase + c * 32 + t <= q) mx = fmaxf(mx, __uint_as_float(v[t]) * sl);
+      }
+      const float mn = fmaxf(m, mx);
+      const float corr = exp2f(m - mn);
+      float rs = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tS + lane_base + c * 32, v);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          const float p0 = (kbase + c * 32 + t <= q) ? exp2f(__uint_as_float(v[t]) * sl - mn) : 0.f;
+          const float p1 = (kbase + c * 32 + t + 1 <= q) ? exp2f(__uint_as_float(v[t + 1]) * sl - mn) : 0.f;
+          rs += p0 + p1;
+          pk[t >> 1] = pack_bf16x2(p0, p1);
+        }
+        store_row32(p_addr, r, c, pk);
+      }
+      l = l * corr + rs;
+      m = mn;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (!mbar_wait(o_full, j & 1, a.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld32(tO + lane_base, v0);
+      tmem_ld32(tO + lane_base + 32, v1);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        o[i] = o[i] * corr + __uint_as_float(v0[i]);
+        o[32 + i] = o[32 + i] * corr + __uint_as_float(v1[i]);
+      }
+      tc_fence_before();
+    }
+    if (ok && q < a.T) {
+      const float inv = 1.f / l;
+      __nv_bfloat16* orow = a.out + static_cast<long>(row0 + q) * a.D + h * kHd;
+#pragma unroll
+      for (int i = 0; i < 64; i += 8) {
+        uint4 pk = make_uint4(pack_bf16x2(o[i] * inv, o[i + 1] * inv), pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv),
+                              pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv), pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv));
+        *reinterpret_cast<uint4*>(orow + i) = pk;
+      }
+      // natural-log log-sum-exp of the scaled scores
+      a.lse[static_cast<long>(bh) * a.T + q] = (m + log2f(l)) / kLog2e;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------
+
+constexpr size_t kBwdSmem = 1024 + 2 * kTileBytes /*K,V*/ + 4 * kTileBytes /*Q,dO x2*/ +
+                            4 * kTileBytes /*P^T, dS^T*/ + 4 * kT * 4 /*lse, delta x2*/ + 16 * 8 + 16;
+
+__global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CUtensorMap tm_qkv,
+                                                      const __grid_constant__ CUtensorMap tm_do, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = sm;
+  uint8_t* sV = sK + kTileBytes;
+  uint8_t* sQ = sV + kTileBytes;      // [2]
+  uint8_t* sdO = sQ + 2 * kTileBytes;  // [2]
+  uint8_t* sPT = sdO + 2 * kTileBytes;  // 32 KB
+  uint8_t* sdST = sPT + 2 * kTileBytes;  // 32 KB
+  float* sLse = reinterpret_cast<float*>(sdST + 2 * kTileBytes);  // [2][128]
+  float* sDel = sLse + 2 * kT;                                     // [2][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 2 * kT);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qd_full = bars + 1;   // [2]
+  uint64_t* qd_empty = bars + 3;  // [2]
+  uint64_t* st_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* dq_full = bars + 7;
+  uint64_t* dq_empty = bars + 8;
+  uint64_t* acc_full = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = static_cast<int>(blockIdx.x % a.ntiles);  // long columns (kt = 0) first
+  const int bh = blockIdx.x / a.ntiles;
+  const int b = bh / a.H, h = bh % a.H;
+  const int row0 = b * a.T;
+  const int nq = a.ntiles - kt;  // query tiles kt .. ntiles-1
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&qd_full[s], 1);
+      mbar_init(&qd_empty[s], 1);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 4);
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_qkv);
+    tma_prefetch_desc(&tm_do);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tST = tmem, tdPT = tmem + 128, tdV = tmem + 256, tdK = tmem + 320, tdQ = tmem + 384;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * kTileBytes);
+      tma_load_2d(sK, &tm_qkv, kv_full, a.D + h * kHd, row0 + kt * kT);
+      tma_load_2d(sV, &tm_qkv, kv_full, 2 * a.D + h * kHd, row0 + kt * kT);
+      for (int it = 0; it < nq; ++it) {
+        const int s = it & 1, i = kt + it;
+        if (!mbar_wait(&qd_empty[s], ((it >> 1) & 1) ^ 1, a.err, abort_flag)) break;
+        mbar_arrive_expect_tx(&qd_full[s], 2 * kTileBytes);
+        tma_load_2d(sQ + s * kTileBytes, &tm_qkv, &qd_full[s], h * kHd, row0 + i * kT);
+        tma_load_2d(sdO + s * kTileBytes, &tm_do, &qd_full[s], h * kHd, row0 + i * kT);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = make_idesc_bf16(128, 128, false, false);
+      constexpr uint32_t idKV = make_idesc_bf16(128, 64, false, true);
+      constexpr uint32_t idQ = make_idesc_bf16(128, 64, true, true);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      const uint32_t pt_addr = smem_u32(sPT), dst_addr = smem_u32(sdST);
+      bool ok = mbar_wait(kv_full, 0, a.err, abort_flag);
+      for (int it = 0; it < nq && ok; ++it) {
+        const int s = it & 1;
+        if (!mbar_wait(&qd_full[s], (it >> 1) & 1, a.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + s * kTileBytes), do_addr = smem_u32(sdO + s * kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) umma_f16(tST, kdesc(k_addr, kk), kdesc(q_addr, kk), idS, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) umma_f16(tdPT, kdesc(v_addr, kk), kdesc(do_addr, kk), idS, kk > 0);
+        umma_commit(st_full);
+        if (!mbar_wait(p_full, it & 1, a.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16(tdV, kdesc2(pt_addr, kk), mndesc(do_addr, kk, 8192), idKV, (it > 0 || kk > 0));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16(tdK, kdesc2(dst_addr, kk), mndesc(q_addr, kk, 8192), idKV, (it > 0 || kk > 0));
+        if (it > 0) {
+          if (!mbar_wait(dq_empty, (it - 1) & 1, a.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16(tdQ, mndesc(dst_addr, kk, 16384), mndesc(k_addr, kk, 8192), idQ, kk > 0);
+        umma_commit(dq_full);
+        umma_commit(&qd_empty[s]);
+      }
+      if (ok) umma_commit(acc_full);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int tid = quarter * 32 + lane;  // 0..127: key row (S^T, dK, dV) / query row (dQ)
+    const int key = kt * kT + tid;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const float sl = a.scale * kLog2e;
+    const uint32_t pt_addr = smem_u32(sPT), dst_addr = smem_u32(sdST);
+    bool ok = true;
+    for (int it = 0; it < nq; ++it) {
+      const int s = it & 1, i = kt + it;
+      {
+        const int q = i * kT + tid;
+        sLse[s * kT + tid] = (q < a.T) ? a.lse[static_cast<long>(bh) * a.T + q] * kLog2e : INFINITY;
+        sDel[s * kT + tid] = (q < a.T) ? a.delta[static_cast<long>(bh) * a.T + q] : 0.f;
+      }
+      named_bar_softmax();
+      if (!mbar_wait(st_full, it & 1, a.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float* lse2 = sLse + s * kT;
+      const float* del = sDel + s * kT;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tST + lane_base + c * 32, sv);
+        tmem_ld32(tdPT + lane_base + c * 32, dv);
+        tmem_wait_ld();
+        uint32_t pp[16], pd[16];
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          float p[2], d[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int qi = c * 32 + t + u;
+            const int q = i * kT + qi;
+            p[u] = (key <= q) ? exp2f(__uint_as_float(sv[t + u]) * sl - lse2[qi]) : 0.f;
+            d[u] = p[u] * (__uint_as_float(dv[t + u]) - del[qi]) * a.scale;
+          }
+          pp[t >> 1] = pack_bf16x2(p[0], p[1]);
+          pd[t >> 1] = pack_bf16x2(d[0], d[1]);
+        }
+        store_row32(pt_addr, tid, c, pp);
+        store_row32(dst_addr, tid, c, pd);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      // dQ tile partial: TMEM lane = query row of tile i
+      if (!mbar_wait(dq_full, it & 1, a.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t q0[32], q1[32];
+      tmem_ld32(tdQ + lane_base, q0);
+      tmem_ld32(tdQ + lane_base + 32, q1);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
+      const int q = i * kT + tid;
+      if (q < a.T) {
+        float* dst = a.dq_acc + static_cast<long>(row0 + q) * a.D + h * kHd;
+#pragma unroll
+        for (int u = 0; u < 32; ++u) {
+          atomicAdd(dst + u, __uint_as_float(q0[u]));
+          atomicAdd(dst + 32 + u, __uint_as_float(q1[u]));
+        }
+      }
+    }
+    if (ok && mbar_wait(acc_full, 0, a.err, abort_flag)) {
+      tc_fence_after();
+      uint32_t k0[32], k1[32], v0[32], v1[32];
+      tmem_ld32(tdK + lane_base, k0);
+      tmem_ld32(tdK + lane_base + 32, k1);
+      tmem_ld32(tdV + lane_base, v0);
+      tmem_ld32(tdV + lane_base + 32, v1);
+      tmem_wait_ld();
+      if (key < a.T) {
+        __nv_bfloat16* dk = a.dqkv + static_cast<long>(row0 + key) * 3 * a.D + a.D + h * kHd;
+        __nv_bfloat16* dvp = dk + a.D;
+#pragma unroll
+        for (int u = 0; u < 32; u += 8) {
+          *reinterpret_cast<uint4*>(dk + u) =
+              make_uint4(pack_bf16x2(__uint_as_float(k0[u]), __uint_as_float(k0[u + 1])),
+                         pack_bf16x2(__uint_as_float(k0[u + 2]), __uint_as_float(k0[u + 3])),
+                         pack_bf16x2(__uint_as_float(k0[u + 4]), __uint_as_float(k0[u + 5])),
+                         pack_bf16x2(__uint_as_float(k0[u + 6]), __uint_as_float(k0[u + 7])));
+          *reinterpret_cast<uint4*>(dk + 32 + u) =
+              make_uint4(pack_bf16x2(__uint_as_float(k1[u]), __uint_as_float(k1[u + 1])),
+                         pack_bf16x2(__uint_as_float(k1[u + 2]), __uint_as_float(k1[u + 3])),
+                         pack_bf16x2(__uint_as_float(k1[u + 4]), __uint_as_float(k1[u + 5])),
+                         pack_bf16x2(__uint_as_float(k1[u + 6]), __uint_as_float(k1[u + 7])));
+          *reinterpret_cast<uint4*>(dvp + u) =
+              make_uint4(pack_bf16x2(__uint_as_float(v0[u]), __uint_as_float(v0[u + 1])),
+                         pack_bf16x2(__uint_as_float(v0[u + 2]), __uint_as_float(v0[u + 3])),
+                         pack_bf16x2(__uint_as_float(v0[u + 4]), __uint_as_float(v0[u + 5])),
+                         pack_bf16x2(__uint_as_float(v0[u + 6]), __uint_as_float(v0[u + 7])));
+          *reinterpret_cast<uint4*>(dvp + 32 + u) =
+              make_uint4(pack_bf16x2(__uint_as_float(v1[u]), __uint_as_float(v1[u + 1])),
+                         pack_bf16x2(__uint_as_float(v1[u + 2]), __uint_as_float(v1[u + 3])),
+                         pack_bf16x2(__uint_as_float(v1[u + 4]), __uint_as_float(v1[u + 5])),
+                         pack_bf16x2(__uint_as_float(v1[u + 6]), __uint_as_float(v1[u + 7])));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dq (bf16, columns [0, D) of dqkv) = dq_acc (f32 [N, D])
+__global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv, long n, int D) {
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n / 4;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const long e = i * 4, r = e / D, c = e % D;
+    const float4 v = reinterpret_cast<const float4*>(acc)[i];
+    uint2 u;
+    u.x = pack_bf16x2(v.x, v.y);
+    u.y = pack_bf16x2(v.z, v.w);
+    *reinterpret_cast<uint2*>(dqkv + r * 3 * D + c) = u;
+  }
+}
+
+size_t dq_offset_floats(const AttnShape& sh) {
+  return ((static_cast<size_t>(sh.B) * sh.H * sh.T + 63) / 64 + 1) * 64;
+}
+
+}  // namespace
+
+// delta is computed by the CUDA-core path's helper (attention_simt.cu)
+int attention_delta_bf16(const void* o, const void* dout, float* delta, const AttnShape& sh, cudaStream_t s);
+
+bool attention_tc_supported(const AttnShape& sh) { return sh.Hd == kHd && sh.T >= 1 && sh.B >= 1 && sh.H >= 1; }
+
+int attention_fwd_tc(const void* qkv, void* o, float* lse, const AttnShape& sh, cudaStream_t s, int* err) {
+  const int D = sh.H * sh.Hd, N = sh.B * sh.T;
+  alignas(64) CUtensorMap tm;
+  if (!make_tma_2d_bf16(&tm, qkv, N, 3L * D, 3L * D, 64, kT)) return 2;
+  AttnArgs a{};
+  a.B = sh.B;
+  a.T = sh.T;
+  a.H = sh.H;
+  a.D = D;
+  a.ntiles = (sh.T + kT - 1) / kT;
+  a.scale = 1.0f / sqrtf(static_cast<float>(sh.Hd));
+  a.out = static_cast<__nv_bfloat16*>(o);
+  a.lse = lse;
+  a.err = err;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFwdSmem)) !=
+        cudaSuccess)
+      return 3;
+    attr = true;
+  }
+  attn_fwd_tc<<<sh.B * sh.H * a.ntiles, 192, kFwdSmem, s>>>(tm, a);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+size_t attention_bwd_tc_workspace_bytes(const AttnShape& sh) {
+  const size_t n = static_cast<size_t>(sh.B) * sh.T;
+  return (dq_offset_floats(sh) + n * sh.H * sh.Hd) * sizeof(float);
+}
+
+int attention_bwd_tc(const void* qkv, const void* o, const void* dout, const float* lse, void* dqkv, float* ws,
+                     const AttnShape& sh, cudaStream_t s, int* err) {
+  const int D = sh.H * sh.Hd, N = sh.B * sh.T;
+  float* delta = ws;
+  float* dq_acc = ws + dq_offset_floats(sh);
+  if (attention_delta_bf16(o, dout, delta, sh, s)) return 4;
+  if (cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(N) * D * sizeof(float), s) != cudaSuccess) return 4;
+  alignas(64) CUtensorMap tq, td;
+  if (!make_tma_2d_bf16(&tq, qkv, N, 3L * D, 3L * D, 64, kT)) return 2;
+  if (!make_tma_2d_bf16(&td, dout, N, D, D, 64, kT)) return 2;
+  AttnArgs a{};
+  a.B = sh.B;
+  a.T = sh.T;
+  a.H = sh.H;
+  a.D = D;
+  a.ntiles = (sh.T + kT - 1) / kT;
+  a.scale = 1.0f / sqrtf(static_cast<float>(sh.Hd));
+  a.lse = const_cast<float*>(lse);
+  a.delta = delta;
+  a.dq_acc = dq_acc;
+  a.dqkv = static_cast<__nv_bfloat16*>(dqkv);
+  a.err = err;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_bwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBwdSmem)) !=
+        cudaSuccess)
+      return 3;
+    attr = true;
+  }
+  attn_bwd_tc<<<sh.B * sh.H * a.ntiles, 192, kBwdSmem, s>>>(tq, td, a);
+  if (cudaPeekAtLastError() != cudaSuccess) return 4;
+  const long n = static_cast<long>(N) * D;
+  const int blocks = static_cast<int>(std::min<long>((n / 4 + 255) / 256, 8L * num_sms()));
+  dq_convert_kernel<<<blocks, 256, 0, s>>>(dq_acc, static_cast<__nv_bfloat16*>(dqkv), n, D);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+}  // namespace sb

@@ -435,6 +435,10 @@ Plan plan_for(const GemmDesc& d) {
 
 }  // namespace
 
+bool make_tma_2d_bf16(void* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows) {
+  return make_map_bf16(static_cast<CUtensorMap*>(map), base, rows, cols, ld, box_cols, box_rows);
+}
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {

@@ -207,16 +207,33 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const TI* __restrict__ dy, 
   }
 }
 
-// out[c] = sum_b part[b][c] (fixed order), written as f32 or bf16.
-__global__ void column_sum_kernel(const float* __restrict__ part, int nparts, int D, void* out, int out_f32) {
-  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < D; c += gridDim.x * blockDim.x) {
-    float acc = 0.f;
-    for (int b = 0; b < nparts; ++b) acc += part[static_cast<long>(b) * D + c];
+// out[c] = sum_b part[b][c] in a fixed order, written as f32 or bf16. Block
+// of 256 threads per 32 columns: warp w sums partial rows w, w+8, ... (lane =
+// column, coalesced), then the 8 warp sums are combined in order.
+__global__ void __launch_bounds__(256) column_sum_kernel(const float* __restrict__ part, int nparts, long D, void* out,
+                                                         int out_f32) {
+  __shared__ float sm[8][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long c = static_cast<long>(blockIdx.x) * 32 + lane;
+  float acc = 0.f;
+  if (c < D)
+    for (int b = warp; b < nparts; b += 8) acc += part[static_cast<long>(b) * D + c];
+  sm[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && c < D) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += sm[w][lane];
     if (out_f32)
-      static_cast<float*>(out)[c] = acc;
+      static_cast<float*>(out)[c] = t;
     else
-      static_cast<__nv_bfloat16*>(out)[c] = __float2bfloat16_rn(acc);
+      static_cast<__nv_bfloat16*>(out)[c] = __float2bfloat16_rn(t);
   }
+}
+
+int column_sum(const float* part, int nparts, long D, void* out, bool out_f32, cudaStream_t s) {
+  column_sum_kernel<<<static_cast<unsigned>((D + 31) / 32), 256, 0, s>>>(part, nparts, D, out, out_f32);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
 // ---------------------------------------------------------------------------
@@ -307,32 +324,30 @@ __global__ void embed_fwd_kernel(const float* __restrict__ ids, const TW* __rest
   }
 }
 
-// dwte for a small vocabulary, deterministic: block (v, column chunk) sums the
-// rows of every token whose id is v, in token order.
-__global__ void embed_bwd_small_kernel(const float* __restrict__ ids, const float* __restrict__ dx, int ntok, int V,
-                                       int D, void* dwte, int out_f32) {
-  const int v = blockIdx.x;
-  const int c = blockIdx.y * blockDim.x + threadIdx.x;
-  __shared__ int sm_idx[1024];
-  float acc = 0.f;
-  for (int base = 0; base < ntok; base += 1024) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < 1024; i += blockDim.x)
-      sm_idx[i] = (base + i < ntok) ? static_cast<int>(ids[base + i]) : -1;
-    __syncthreads();
-    if (c < D) {
-      const int lim = min(1024, ntok - base);
-      for (int i = 0; i < lim; ++i)
-        if (sm_idx[i] == v) acc += dx[static_cast<long>(base + i) * D + c];
-    }
+// dwte for a small vocabulary, deterministic: block b accumulates the tokens
+// [b*chunk, (b+1)*chunk) in order into a private [V, D] copy in shared memory
+// (thread = column, so no two threads touch one word), then writes it to
+// part[b]; the partials are summed in block order by column_sum.
+__global__ void embed_bwd_priv_kernel(const float* __restrict__ ids, const float* __restrict__ dx, int ntok, int V,
+                                      int D, int chunk, float* __restrict__ part) {
+  extern __shared__ float acc[];
+  const int VD = V * D;
+  for (int i = threadIdx.x; i < VD; i += blockDim.x) acc[i] = 0.f;
+  __syncthreads();
+  const int t0 = blockIdx.x * chunk, t1 = min(ntok, t0 + chunk);
+  for (int t = t0; t < t1; ++t) {
+    const int id = static_cast<int>(ids[t]);
+    if (id < 0 || id >= V) continue;
+    const float* g = dx + static_cast<long>(t) * D;
+    float* a = acc + id * D;
+    for (int c = threadIdx.x; c < D; c += blockDim.x) a[c] += g[c];
   }
-  if (c < D) {
-    if (out_f32)
-      static_cast<float*>(dwte)[static_cast<long>(v) * D + c] = acc;
-    else
-      static_cast<__nv_bfloat16*>(dwte)[static_cast<long>(v) * D + c] = __float2bfloat16_rn(acc);
-  }
+  __syncthreads();
+  float* p = part + static_cast<long>(blockIdx.x) * VD;
+  for (int i = threadIdx.x; i < VD; i += blockDim.x) p[i] = acc[i];
 }
+
+constexpr int kEmbedPrivBlocks = 64;
 
 // dwte for a large vocabulary: fp32 atomics into a zeroed f32 accumulator.
 __global__ void embed_bwd_atomic_kernel(const float* __restrict__ ids, const float* __restrict__ dx, int ntok, int V,
@@ -445,8 +460,7 @@ int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean
                                        dres_bf, ws, rows, D);
     }));
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
-  column_sum_kernel<<<(D + 255) / 256, 256, 0, s>>>(ws, grid, D, dgamma, dgamma_f32);
-  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+  return column_sum(ws, grid, D, dgamma, dgamma_f32, s);
 }
 
 size_t cross_entropy_workspace_bytes(int rows) {
@@ -484,16 +498,25 @@ int embedding_fwd(const float* ids, const void* wte, const void* wpe, bool f32, 
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
+static bool embed_small(int V, int D) { return static_cast<size_t>(V) * D * sizeof(float) <= 160 * 1024; }
+
 size_t embedding_bwd_workspace_bytes(int V, int D) {
-  return (V > kEmbedSmallVocab) ? static_cast<size_t>(V) * D * sizeof(float) : 0;
+  return embed_small(V, D) ? static_cast<size_t>(kEmbedPrivBlocks) * V * D * sizeof(float)
+                           : static_cast<size_t>(V) * D * sizeof(float);
 }
 
 int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V, int D, void* dwte, void* dwpe,
                   bool out_f32, float* ws, cudaStream_t s) {
   const int ntok = B * T;
-  if (V <= kEmbedSmallVocab) {
-    dim3 grid(V, (D + 127) / 128);
-    embed_bwd_small_kernel<<<grid, 128, 0, s>>>(ids, dx, ntok, V, D, dwte, out_f32);
+  if (embed_small(V, D)) {
+    if (!ws) return 5;
+    const int chunk = (ntok + kEmbedPrivBlocks - 1) / kEmbedPrivBlocks;
+    const size_t smem = static_cast<size_t>(V) * D * sizeof(float);
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(embed_bwd_priv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    embed_bwd_priv_kernel<<<kEmbedPrivBlocks, 384, smem, s>>>(ids, dx, ntok, V, D, chunk, ws);
+    if (cudaPeekAtLastError() != cudaSuccess) return 4;
+    if (column_sum(ws, kEmbedPrivBlocks, static_cast<long>(V) * D, dwte, out_f32, s)) return 4;
   } else {
     float* acc = out_f32 ? static_cast<float*>(dwte) : ws;
     if (!acc) return 5;

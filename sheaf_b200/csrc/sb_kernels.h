@@ -49,4 +49,9 @@ size_t gemm_f32_workspace_bytes(const GemmDesc& d);
 
 int num_sms();
 
+// 2-D bf16 TMA descriptor over a row-major [rows, cols] matrix (row stride
+// `ld` elements), box {box_cols, box_rows}, 128-byte swizzle, zero fill.
+// `map` points at a CUtensorMap (64-byte aligned storage).
+bool make_tma_2d_bf16(void* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows);
+
 }  // namespace sb
