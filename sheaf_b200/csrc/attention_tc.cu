@@ -48,15 +48,12 @@ struct AttnArgs {
   float scale;  // 1 / sqrt(Hd)
   __nv_bfloat16* out;
   float* lse;
-  const float* delta;
+  const __nv_bfloat16* o;     // backward: forward output [B*T, D]
+  const __nv_bfloat16* dout;  // backward: upstream gradient [B*T, D]
   float* dq_acc;
   __nv_bfloat16* dqkv;
   int* err;
 };
-
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
 
 __device__ __forceinline__ void named_bar_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -397,9 +394,27 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
     for (int it = 0; it < nq; ++it) {
       const int s = it & 1, i = kt + it;
       {
+        // per query row of tile i: lse (log2 units) and delta = rowsum(dO * O)
         const int q = i * kT + tid;
+        float dl = 0.f;
+        if (q < a.T) {
+          const long off = static_cast<long>(row0 + q) * a.D + h * kHd;
+#pragma unroll
+          for (int u = 0; u < kHd; u += 8) {
+            const uint4 ov = *reinterpret_cast<const uint4*>(a.o + off + u);
+            const uint4 dv = *reinterpret_cast<const uint4*>(a.dout + off + u);
+            const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              dl += bf16_bits_to_f32(static_cast<uint16_t>(ow[k] & 0xFFFFu)) *
+                    bf16_bits_to_f32(static_cast<uint16_t>(dw[k] & 0xFFFFu));
+              dl += bf16_bits_to_f32(static_cast<uint16_t>(ow[k] >> 16)) *
+                    bf16_bits_to_f32(static_cast<uint16_t>(dw[k] >> 16));
+            }
+          }
+        }
         sLse[s * kT + tid] = (q < a.T) ? a.lse[static_cast<long>(bh) * a.T + q] * kLog2e : INFINITY;
-        sDel[s * kT + tid] = (q < a.T) ? a.delta[static_cast<long>(bh) * a.T + q] : 0.f;
+        sDel[s * kT + tid] = dl;
       }
       named_bar_softmax();
       if (!mbar_wait(st_full, it & 1, a.err, abort_flag)) {
@@ -518,14 +533,7 @@ __global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* 
   }
 }
 
-size_t dq_offset_floats(const AttnShape& sh) {
-  return ((static_cast<size_t>(sh.B) * sh.H * sh.T + 63) / 64 + 1) * 64;
-}
-
 }  // namespace
-
-// delta is computed by the CUDA-core path's helper (attention_simt.cu)
-int attention_delta_bf16(const void* o, const void* dout, float* delta, const AttnShape& sh, cudaStream_t s);
 
 bool attention_tc_supported(const AttnShape& sh) { return sh.Hd == kHd && sh.T >= 1 && sh.B >= 1 && sh.H >= 1; }
 
@@ -555,16 +563,13 @@ int attention_fwd_tc(const void* qkv, void* o, float* lse, const AttnShape& sh, 
 }
 
 size_t attention_bwd_tc_workspace_bytes(const AttnShape& sh) {
-  const size_t n = static_cast<size_t>(sh.B) * sh.T;
-  return (dq_offset_floats(sh) + n * sh.H * sh.Hd) * sizeof(float);
+  return static_cast<size_t>(sh.B) * sh.T * sh.H * sh.Hd * sizeof(float);
 }
 
 int attention_bwd_tc(const void* qkv, const void* o, const void* dout, const float* lse, void* dqkv, float* ws,
                      const AttnShape& sh, cudaStream_t s, int* err) {
   const int D = sh.H * sh.Hd, N = sh.B * sh.T;
-  float* delta = ws;
-  float* dq_acc = ws + dq_offset_floats(sh);
-  if (attention_delta_bf16(o, dout, delta, sh, s)) return 4;
+  float* dq_acc = ws;
   if (cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(N) * D * sizeof(float), s) != cudaSuccess) return 4;
   alignas(64) CUtensorMap tq, td;
   if (!make_tma_2d_bf16(&tq, qkv, N, 3L * D, 3L * D, 64, kT)) return 2;
@@ -577,7 +582,8 @@ int attention_bwd_tc(const void* qkv, const void* o, const void* dout, const flo
   a.ntiles = (sh.T + kT - 1) / kT;
   a.scale = 1.0f / sqrtf(static_cast<float>(sh.Hd));
   a.lse = const_cast<float*>(lse);
-  a.delta = delta;
+  a.o = static_cast<const __nv_bfloat16*>(o);
+  a.dout = static_cast<const __nv_bfloat16*>(dout);
   a.dq_acc = dq_acc;
   a.dqkv = static_cast<__nv_bfloat16*>(dqkv);
   a.err = err;

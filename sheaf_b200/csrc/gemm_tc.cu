@@ -8,11 +8,13 @@
 // across CTAs) instead of B per-batch partial products plus a reduce.
 //
 // Kernel structure (one CTA per SM, persistent over output tiles):
-//   warp 0     : TMA producer (one elected lane), STAGES-deep smem ring
+//   warp 0     : TMA producer (one lane), STAGES-deep smem ring
 //   warp 1     : TMEM allocator + single-thread UMMA issuer (M=128, N=BN, K=16)
-//   warps 2..5 : epilogue; warp w reads TMEM lanes 32*(w%4)..+31, i.e. one
-//                accumulator row per thread, applies the fused epilogue and
-//                stores to global memory.
+//   warps 2..5 : epilogue; warp w owns TMEM lanes 32*(w%4)..+31 (32 output
+//                rows). Each 32-row x 128-byte block of the tile is converted
+//                in registers (fused epilogue), written to a 128B-swizzled
+//                4 KB staging slot and stored with a TMA bulk tensor store;
+//                two slots per warp let conversion overlap the stores.
 // Accumulators are double-buffered in TMEM (2*BN columns) so the epilogue of
 // tile i overlaps the main loop of tile i+1.
 #include <cuda.h>
@@ -33,22 +35,18 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr uint32_t kABytes = kBM * kBK * 2;
+constexpr uint32_t kSlotBytes = 32 * 128;          // one 32-row x 128-byte staging block
+constexpr uint32_t kStagingBytes = 4 * 2 * kSlotBytes;  // 4 epilogue warps x 2 slots
 
 struct GemmArgs {
   int M, N, K;
   int m_tiles, n_tiles;
   int splits, kb_per_split, kb_total;
   int epi;
-  void* out;
-  long ldo;
-  int out_f32;
+  int out_f32;     // output element type (split-K partials are f32)
+  int partial;     // split-K: rows of split s start at s * m_tiles * 128
   const void* aux;
   long ldaux;
-  int aux_f32;
-  void* out2;
-  long ldo2;
-  long split_stride;  // elements between split-K partial slices (f32 workspace)
-  int vec_ok;         // 16-byte vector stores are aligned for every full chunk
   int* err;
 };
 
@@ -65,131 +63,30 @@ __device__ __forceinline__ float gelu_grad(float x) {
   return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * 0.7978846f * (1.0f + 0.134145f * x2);
 }
 
-__device__ __forceinline__ float ld_elem(const void* p, long idx, int is_f32) {
-  if (is_f32) return static_cast<const float*>(p)[idx];
-  return bf16_bits_to_f32(static_cast<const uint16_t*>(p)[idx]);
-}
-
-__device__ __forceinline__ void st_elem(void* p, long idx, int is_f32, float v) {
-  if (is_f32)
-    static_cast<float*>(p)[idx] = v;
-  else
-    static_cast<__nv_bfloat16*>(p)[idx] = __float2bfloat16_rn(v);
-}
-
-// Stores 32 consecutive accumulator columns [col0, col0+32) of one row.
-__device__ __forceinline__ void epilogue_row32(const GemmArgs& a, int row, int col0, const uint32_t (&v)[32],
-                                               int split) {
-  if (row >= a.M) return;
-  float f[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-  const bool full = (col0 + 32 <= a.N) && a.vec_ok;
-
-  if (a.epi == EPI_STORE) {
-    if (a.out_f32) {
-      float* o = static_cast<float*>(a.out) + split * a.split_stride + static_cast<long>(row) * a.ldo + col0;
-      if (full) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-      } else {
-        for (int j = 0; j < 32 && col0 + j < a.N; ++j) o[j] = f[j];
-      }
-    } else {
-      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + static_cast<long>(row) * a.ldo + col0;
-      if (full) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          uint4 pk = make_uint4(pack_bf16x2(f[j], f[j + 1]), pack_bf16x2(f[j + 2], f[j + 3]),
-                                pack_bf16x2(f[j + 4], f[j + 5]), pack_bf16x2(f[j + 6], f[j + 7]));
-          *reinterpret_cast<uint4*>(o + j) = pk;
-        }
-      } else {
-        for (int j = 0; j < 32 && col0 + j < a.N; ++j) o[j] = __float2bfloat16_rn(f[j]);
-      }
-    }
-  } else if (a.epi == EPI_ADD) {
-    // f32 residual stream: out = aux + acc (aux may alias out).
-    const float* x = static_cast<const float*>(a.aux) + static_cast<long>(row) * a.ldaux + col0;
-    float* o = static_cast<float*>(a.out) + static_cast<long>(row) * a.ldo + col0;
-    if (full) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        float4 r = *reinterpret_cast<const float4*>(x + j);
-        *reinterpret_cast<float4*>(o + j) = make_float4(r.x + f[j], r.y + f[j + 1], r.z + f[j + 2], r.w + f[j + 3]);
-      }
-    } else {
-      for (int j = 0; j < 32 && col0 + j < a.N; ++j) o[j] = x[j] + f[j];
-    }
-  } else if (a.epi == EPI_GELU) {
-    __nv_bfloat16* u = static_cast<__nv_bfloat16*>(a.out) + static_cast<long>(row) * a.ldo + col0;
-    __nv_bfloat16* g = static_cast<__nv_bfloat16*>(a.out2) + static_cast<long>(row) * a.ldo2 + col0;
-    if (full) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        float ur[8], gr[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          ur[t] = __bfloat162float(__float2bfloat16_rn(f[j + t]));
-          gr[t] = gelu_fwd(ur[t]);
-        }
-        *reinterpret_cast<uint4*>(u + j) = make_uint4(pack_bf16x2(ur[0], ur[1]), pack_bf16x2(ur[2], ur[3]),
-                                                      pack_bf16x2(ur[4], ur[5]), pack_bf16x2(ur[6], ur[7]));
-        *reinterpret_cast<uint4*>(g + j) = make_uint4(pack_bf16x2(gr[0], gr[1]), pack_bf16x2(gr[2], gr[3]),
-                                                      pack_bf16x2(gr[4], gr[5]), pack_bf16x2(gr[6], gr[7]));
-      }
-    } else {
-      for (int j = 0; j < 32 && col0 + j < a.N; ++j) {
-        float ur = __bfloat162float(__float2bfloat16_rn(f[j]));
-        u[j] = __float2bfloat16_rn(ur);
-        g[j] = __float2bfloat16_rn(gelu_fwd(ur));
-      }
-    }
-  } else {  // EPI_GELU_BWD: out = acc * gelu'(u), u read from aux (bf16)
-    const __nv_bfloat16* u = static_cast<const __nv_bfloat16*>(a.aux) + static_cast<long>(row) * a.ldaux + col0;
-    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + static_cast<long>(row) * a.ldo + col0;
-    if (full) {
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint4 ur = *reinterpret_cast<const uint4*>(u + j);
-        const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&ur);
-        float r[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) r[t] = f[j + t] * gelu_grad(__bfloat162float(ub[t]));
-        *reinterpret_cast<uint4*>(o + j) = make_uint4(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]),
-                                                      pack_bf16x2(r[4], r[5]), pack_bf16x2(r[6], r[7]));
-      }
-    } else {
-      for (int j = 0; j < 32 && col0 + j < a.N; ++j)
-        o[j] = __float2bfloat16_rn(f[j] * gelu_grad(__bfloat162float(u[j])));
-    }
-  }
-}
-
-template <int BN>
-__host__ __device__ constexpr uint32_t tmem_cols_for() {
-  return (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+__host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
+  return (2 * bn <= 32) ? 32 : (2 * bn <= 64) ? 64 : (2 * bn <= 128) ? 128 : (2 * bn <= 256) ? 256 : 512;
 }
 
 template <int BN, int STAGES>
 constexpr size_t smem_bytes_for() {
-  return 1024 /*alignment slack*/ + static_cast<size_t>(STAGES) * (kABytes + BN * kBK * 2) +
+  return 1024 /*alignment slack*/ + static_cast<size_t>(STAGES) * (kABytes + BN * kBK * 2) + kStagingBytes +
          (2 * STAGES + 4) * sizeof(uint64_t) + 16;
 }
 
 template <int BN, bool A_MN, bool B_MN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs a) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, GemmArgs a) {
   constexpr uint32_t kBBytes = BN * kBK * 2;
-  constexpr uint32_t kTmemCols = tmem_cols_for<BN>();
-  static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16,256]");
-  static_assert(!B_MN || BN % 64 == 0, "MN-major B tiles are loaded in 64-wide chunks");
+  constexpr uint32_t kTmemCols = tmem_cols_for(BN);
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "tile width must be 64, 128, 192 or 256");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * kBBytes);
+  uint8_t* sStg = sB + STAGES * kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sStg + kStagingBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -214,6 +111,8 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+    tma_prefetch_desc(&tmC2);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -294,6 +193,26 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int q = warp & 3;
+    const uint32_t stg = smem_u32(sStg) + (warp - 2) * 2 * kSlotBytes;
+    uint32_t cc = 0;  // bulk stores issued by this warp (lane 0 commits them)
+    auto stage = [&](const uint32_t(&w)[32], const CUtensorMap* map, int x, int y) {
+      const uint32_t slot = stg + (cc & 1) * kSlotBytes;
+      if (cc >= 2) {
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+      }
+      st_row128_sw(slot, lane, w);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                         reinterpret_cast<uint64_t>(map)),
+                     "r"(slot), "r"(x), "r"(y)
+                     : "memory");
+        bulk_commit();
+      }
+      ++cc;
+    };
     int local = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const int split = u % a.splits;
@@ -303,19 +222,114 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t aph = (local >> 1) & 1;
       if (!mbar_wait(&tfull[as], aph, a.err, abort_flag)) break;
       tc_fence_after();
-      const int row = mt * kBM + q * 32 + lane;
+      const int row0 = mt * kBM + q * 32;
+      const int row = row0 + lane;
+      const int store_y = a.partial ? split * a.m_tiles * kBM + row0 : row0;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + as * BN;
+      if (a.out_f32) {
+        // 32 f32 columns (128 B) per block: STORE or ADD (residual stream)
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(t_row + c * 32, v);
-        tmem_wait_ld();
-        epilogue_row32(a, row, nt * BN + c * 32, v, split);
+        for (int c = 0; c < BN / 32; ++c) {
+          const int col0 = nt * BN + c * 32;
+          if (col0 >= a.N) break;
+          uint32_t v[32];
+          tmem_ld32(t_row + c * 32, v);
+          tmem_wait_ld();
+          if (a.epi == EPI_ADD && row < a.M) {
+            const float* x = static_cast<const float*>(a.aux) + static_cast<long>(row) * a.ldaux + col0;
+            if (col0 + 32 <= a.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 r = *reinterpret_cast<const float4*>(x + j);
+                v[j] = __float_as_uint(__uint_as_float(v[j]) + r.x);
+                v[j + 1] = __float_as_uint(__uint_as_float(v[j + 1]) + r.y);
+                v[j + 2] = __float_as_uint(__uint_as_float(v[j + 2]) + r.z);
+                v[j + 3] = __float_as_uint(__uint_as_float(v[j + 3]) + r.w);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < a.N) v[j] = __float_as_uint(__uint_as_float(v[j]) + x[j]);
+            }
+          }
+          stage(v, &tmC, col0, store_y);
+        }
+      } else {
+        // 64 bf16 columns (128 B) per block: STORE, GELU (two outputs), GELU_BWD
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          const int col0 = nt * BN + c * 64;
+          if (col0 >= a.N) break;
+          uint32_t v0[32], v1[32];
+          tmem_ld32(t_row + c * 64, v0);
+          tmem_ld32(t_row + c * 64 + 32, v1);
+          tmem_wait_ld();
+          uint32_t w[32];
+          if (a.epi == EPI_STORE) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              w[j] = pack_bf16x2(__uint_as_float(v0[2 * j]), __uint_as_float(v0[2 * j + 1]));
+              w[16 + j] = pack_bf16x2(__uint_as_float(v1[2 * j]), __uint_as_float(v1[2 * j + 1]));
+            }
+            stage(w, &tmC, col0, store_y);
+          } else if (a.epi == EPI_GELU) {
+            uint32_t g[32];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float u0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[2 * j])));
+              const float u1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[2 * j + 1])));
+              w[j] = pack_bf16x2(u0, u1);
+              g[j] = pack_bf16x2(gelu_fwd(u0), gelu_fwd(u1));
+              const float u2 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[2 * j])));
+              const float u3 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[2 * j + 1])));
+              w[16 + j] = pack_bf16x2(u2, u3);
+              g[16 + j] = pack_bf16x2(gelu_fwd(u2), gelu_fwd(u3));
+            }
+            stage(w, &tmC, col0, store_y);
+            stage(g, &tmC2, col0, store_y);
+          } else {  // EPI_GELU_BWD: acc * gelu'(u), u = aux (bf16)
+            uint32_t uw[32];
+            if (row < a.M) {
+              const __nv_bfloat16* up =
+                  static_cast<const __nv_bfloat16*>(a.aux) + static_cast<long>(row) * a.ldaux + col0;
+              if (col0 + 64 <= a.N) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                  const uint4 r = *reinterpret_cast<const uint4*>(up + 2 * j);
+                  uw[j] = r.x;
+                  uw[j + 1] = r.y;
+                  uw[j + 2] = r.z;
+                  uw[j + 3] = r.w;
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const uint16_t lo = (col0 + 2 * j < a.N) ? reinterpret_cast<const uint16_t*>(up)[2 * j] : 0;
+                  const uint16_t hi = (col0 + 2 * j + 1 < a.N) ? reinterpret_cast<const uint16_t*>(up)[2 * j + 1] : 0;
+                  uw[j] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) uw[j] = 0;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              w[j] = pack_bf16x2(__uint_as_float(v0[2 * j]) * gelu_grad(bf16_bits_to_f32(uw[j] & 0xFFFFu)),
+                                 __uint_as_float(v0[2 * j + 1]) * gelu_grad(bf16_bits_to_f32(uw[j] >> 16)));
+              w[16 + j] = pack_bf16x2(__uint_as_float(v1[2 * j]) * gelu_grad(bf16_bits_to_f32(uw[16 + j] & 0xFFFFu)),
+                                      __uint_as_float(v1[2 * j + 1]) * gelu_grad(bf16_bits_to_f32(uw[16 + j] >> 16)));
+            }
+            stage(w, &tmC, col0, store_y);
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[as]);
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
 done:
@@ -327,9 +341,10 @@ done:
   }
 }
 
-// Sums split-K partial slices: out[r, c] = sum_s ws[s][r][c].
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, long slice, int M, int N,
-                                     void* out, long ldo, int out_f32) {
+// Sums split-K partial slices: out[r, c] = sum_s ws[s][r][c] (slice = stride
+// elements between splits).
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, long slice, int M, int N, void* out,
+                                     long ldo, int out_f32) {
   const long total = static_cast<long>(M) * N;
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long>(gridDim.x) * blockDim.x) {
@@ -356,26 +371,30 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// 2-D bf16 tensor map over a row-major [rows, cols] matrix with row stride
-// `ld` elements; box = {box_cols (inner), box_rows}, 128-byte swizzle,
-// out-of-bounds elements read as zero.
-bool make_map_bf16(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows) {
+// 2-D tensor map over a row-major [rows, cols] matrix with row stride `ld`
+// elements; box = {box_cols (inner), box_rows}, 128-byte swizzle,
+// out-of-bounds elements read as zero (and are not written by stores).
+bool make_map(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, long rows, long cols, long ld,
+              int box_cols, int box_rows) {
   auto fn = get_encode_fn();
-  if (!fn) return false;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || ((ld * 2) & 15) != 0) return false;
+  if (!fn || !base) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || ((ld * esize) & 15) != 0) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * esize)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
+bool make_map_bf16(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows) {
+  return make_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols, ld, box_cols, box_rows);
+}
+
 template <int BN, bool A_MN, bool B_MN, int STAGES>
-int launch_tc(const GemmDesc& d, const GemmArgs& args, int grid, cudaStream_t s) {
-  CUtensorMap ta, tb;
+int launch_tc(const GemmDesc& d, const GemmArgs& args, void* out, long ldo, long out_rows, int grid, cudaStream_t s) {
+  alignas(64) CUtensorMap ta, tb, tc, tc2;
   bool ok;
   if (!A_MN)
     ok = make_map_bf16(&ta, d.A, d.M, d.K, d.lda, kBK, kBM);
@@ -387,7 +406,18 @@ int launch_tc(const GemmDesc& d, const GemmArgs& args, int grid, cudaStream_t s)
   else
     ok = make_map_bf16(&tb, d.B, d.K, d.N, d.ldb, 64, kBK);
   if (!ok) return 2;
+  if (args.out_f32)
+    ok = make_map(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, out, out_rows, d.N, ldo, 32, 32);
+  else
+    ok = make_map_bf16(&tc, out, out_rows, d.N, ldo, 64, 32);
+  if (!ok) return 2;
+  if (args.epi == EPI_GELU) {
+    if (!make_map_bf16(&tc2, d.out2, d.M, d.N, d.ldo2, 64, 32)) return 2;
+  } else {
+    tc2 = tc;
+  }
   constexpr size_t smem = smem_bytes_for<BN, STAGES>();
+  static_assert(smem <= 232448, "shared memory budget");
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(gemm_tc_kernel<BN, A_MN, B_MN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -395,16 +425,16 @@ int launch_tc(const GemmDesc& d, const GemmArgs& args, int grid, cudaStream_t s)
       return 3;
     attr_set = true;
   }
-  gemm_tc_kernel<BN, A_MN, B_MN, STAGES><<<grid, 192, smem, s>>>(ta, tb, args);
+  gemm_tc_kernel<BN, A_MN, B_MN, STAGES><<<grid, 192, smem, s>>>(ta, tb, tc, tc2, args);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
 template <int BN, int STAGES>
-int dispatch_major(const GemmDesc& d, const GemmArgs& args, int grid, cudaStream_t s) {
-  if (!d.a_mn && !d.b_mn) return launch_tc<BN, false, false, STAGES>(d, args, grid, s);
-  if (!d.a_mn && d.b_mn) return launch_tc<BN, false, true, STAGES>(d, args, grid, s);
-  if (d.a_mn && d.b_mn) return launch_tc<BN, true, true, STAGES>(d, args, grid, s);
-  return launch_tc<BN, true, false, STAGES>(d, args, grid, s);
+int dispatch_major(const GemmDesc& d, const GemmArgs& a, void* out, long ldo, long rows, int grid, cudaStream_t s) {
+  if (!d.a_mn && !d.b_mn) return launch_tc<BN, false, false, STAGES>(d, a, out, ldo, rows, grid, s);
+  if (!d.a_mn && d.b_mn) return launch_tc<BN, false, true, STAGES>(d, a, out, ldo, rows, grid, s);
+  if (d.a_mn && d.b_mn) return launch_tc<BN, true, true, STAGES>(d, a, out, ldo, rows, grid, s);
+  return launch_tc<BN, true, false, STAGES>(d, a, out, ldo, rows, grid, s);
 }
 
 struct Plan {
@@ -414,8 +444,7 @@ struct Plan {
 Plan plan_for(const GemmDesc& d) {
   Plan p;
   p.bn = d.bn;
-  if (p.bn == 0) p.bn = (d.N > 128) ? 256 : 128;
-  if (d.b_mn && p.bn % 64) p.bn = 128;
+  if (p.bn == 0) p.bn = (d.N > 128) ? 256 : (d.N > 64 ? 128 : 64);
   p.m_tiles = (d.M + kBM - 1) / kBM;
   p.n_tiles = (d.N + p.bn - 1) / p.bn;
   p.kb_total = (d.K + kBK - 1) / kBK;
@@ -454,11 +483,13 @@ size_t gemm_workspace_bytes(const GemmDesc& d, bool bf16) {
   if (!bf16) return gemm_f32_workspace_bytes(d);
   Plan p = plan_for(d);
   if (p.splits <= 1) return 0;
-  return static_cast<size_t>(p.splits) * d.M * d.N * sizeof(float);
+  return static_cast<size_t>(p.splits) * p.m_tiles * kBM * d.N * sizeof(float);
 }
 
 int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* err) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0) return 1;
+  const bool f32_epi = d.epi == EPI_ADD || (d.epi == EPI_STORE && d.out_f32);
+  if ((d.epi == EPI_ADD && !d.out_f32) || ((d.epi == EPI_GELU || d.epi == EPI_GELU_BWD) && d.out_f32)) return 1;
   Plan p = plan_for(d);
   GemmArgs a{};
   a.M = d.M;
@@ -471,37 +502,32 @@ int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaS
   a.kb_total = p.kb_total;
   a.epi = d.epi;
   a.err = err;
+  a.aux = d.aux;
+  a.ldaux = d.ldaux;
   const bool split = p.splits > 1;
+  void* out = d.out;
+  long ldo = d.ldo, rows = d.M;
   if (split) {
-    const size_t need = static_cast<size_t>(p.splits) * d.M * d.N * sizeof(float);
+    const size_t need = static_cast<size_t>(p.splits) * p.m_tiles * kBM * d.N * sizeof(float);
     if (!workspace || workspace_bytes < need) return 5;
-    a.out = workspace;
-    a.ldo = d.N;
+    out = workspace;
+    ldo = d.N;
+    rows = static_cast<long>(p.splits) * p.m_tiles * kBM;
     a.out_f32 = 1;
-    a.split_stride = static_cast<long>(d.M) * d.N;
-    a.vec_ok = (d.N % 4 == 0);
+    a.partial = 1;
   } else {
-    a.out = d.out;
-    a.ldo = d.ldo;
-    a.out_f32 = d.out_f32;
-    a.aux = d.aux;
-    a.ldaux = d.ldaux;
-    a.aux_f32 = d.aux_f32;
-    a.out2 = d.out2;
-    a.ldo2 = d.ldo2;
-    a.split_stride = 0;
-    auto al = [](const void* ptr, long ld, int esz) {
-      return ptr == nullptr || ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ((ld * esz) & 15) == 0);
-    };
-    a.vec_ok = al(d.out, d.ldo, d.out_f32 ? 4 : 2) && al(d.aux, d.ldaux, d.aux_f32 ? 4 : 2) && al(d.out2, d.ldo2, 2);
+    a.out_f32 = f32_epi ? 1 : 0;
+    a.partial = 0;
   }
+  if (d.aux && (((reinterpret_cast<uintptr_t>(d.aux) & 15) != 0) || ((d.ldaux * (d.aux_f32 ? 4 : 2)) & 15) != 0))
+    return 2;
   const int units = p.m_tiles * p.n_tiles * p.splits;
   const int grid = std::min(units, num_sms());
   int rc;
   switch (p.bn) {
-    case 256: rc = dispatch_major<256, 4>(d, a, grid, s); break;
-    case 128: rc = dispatch_major<128, 6>(d, a, grid, s); break;
-    case 64: rc = dispatch_major<64, 8>(d, a, grid, s); break;
+    case 256: rc = dispatch_major<256, 4>(d, a, out, ldo, rows, grid, s); break;
+    case 128: rc = dispatch_major<128, 6>(d, a, out, ldo, rows, grid, s); break;
+    case 64: rc = dispatch_major<64, 8>(d, a, out, ldo, rows, grid, s); break;
     default: return 6;
   }
   if (rc) return rc;
@@ -509,7 +535,8 @@ int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaS
     const long total = static_cast<long>(d.M) * d.N;
     const int threads = 256;
     const int blocks = static_cast<int>(std::min<long>((total + threads - 1) / threads, 4L * num_sms()));
-    splitk_reduce_kernel<<<blocks, threads, 0, s>>>(workspace, p.splits, total, d.M, d.N, d.out, d.ldo, d.out_f32);
+    splitk_reduce_kernel<<<blocks, threads, 0, s>>>(workspace, p.splits, static_cast<long>(p.m_tiles) * kBM * d.N,
+                                                    d.M, d.N, d.out, d.ldo, d.out_f32);
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
   }
   return 0;

@@ -335,19 +335,26 @@ __global__ void embed_bwd_priv_kernel(const float* __restrict__ ids, const float
   for (int i = threadIdx.x; i < VD; i += blockDim.x) acc[i] = 0.f;
   __syncthreads();
   const int t0 = blockIdx.x * chunk, t1 = min(ntok, t0 + chunk);
-  for (int t = t0; t < t1; ++t) {
-    const int id = static_cast<int>(ids[t]);
-    if (id < 0 || id >= V) continue;
-    const float* g = dx + static_cast<long>(t) * D;
-    float* a = acc + id * D;
-    for (int c = threadIdx.x; c < D; c += blockDim.x) a[c] += g[c];
+  const int c = threadIdx.x;  // one column per thread (blockDim >= D)
+  for (int t = t0; t < t1; t += 8) {
+    int id[8];
+    float g[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int tt = t + u;
+      id[u] = (tt < t1) ? static_cast<int>(ids[tt]) : -1;
+      g[u] = (tt < t1 && c < D) ? dx[static_cast<long>(tt) * D + c] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (id[u] >= 0 && id[u] < V && c < D) acc[id[u] * D + c] += g[u];
   }
   __syncthreads();
   float* p = part + static_cast<long>(blockIdx.x) * VD;
   for (int i = threadIdx.x; i < VD; i += blockDim.x) p[i] = acc[i];
 }
 
-constexpr int kEmbedPrivBlocks = 64;
+constexpr int kEmbedPrivBlocks = 148;
 
 // dwte for a large vocabulary: fp32 atomics into a zeroed f32 accumulator.
 __global__ void embed_bwd_atomic_kernel(const float* __restrict__ ids, const float* __restrict__ dx, int ntok, int V,
@@ -498,7 +505,7 @@ int embedding_fwd(const float* ids, const void* wte, const void* wpe, bool f32, 
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
-static bool embed_small(int V, int D) { return static_cast<size_t>(V) * D * sizeof(float) <= 160 * 1024; }
+static bool embed_small(int V, int D) { return static_cast<size_t>(V) * D * sizeof(float) <= 160 * 1024 && D <= 1024; }
 
 size_t embedding_bwd_workspace_bytes(int V, int D) {
   return embed_small(V, D) ? static_cast<size_t>(kEmbedPrivBlocks) * V * D * sizeof(float)
@@ -514,7 +521,7 @@ int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V,
     const size_t smem = static_cast<size_t>(V) * D * sizeof(float);
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(embed_bwd_priv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    embed_bwd_priv_kernel<<<kEmbedPrivBlocks, 384, smem, s>>>(ids, dx, ntok, V, D, chunk, ws);
+    embed_bwd_priv_kernel<<<kEmbedPrivBlocks, (D + 31) / 32 * 32, smem, s>>>(ids, dx, ntok, V, D, chunk, ws);
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
     if (column_sum(ws, kEmbedPrivBlocks, static_cast<long>(V) * D, dwte, out_f32, s)) return 4;
   } else {
