@@ -33,6 +33,7 @@ extern "C" {
 #define SB_OPERR_TMA 2         /* operand not 16-byte aligned for TMA */
 #define SB_OPERR_LAUNCH 4      /* kernel launch failed */
 #define SB_OPERR_WORKSPACE 5   /* workspace missing or too small */
+#define SB_OPERR_SCRATCH 6     /* size beyond a fixed built-in scratch array */
 
 /* C[M,N] = op(A) @ op(B), fp32 accumulation.
  * Replaces `stablehlo.dot_general` with contracting_dims = [1] x [0]
@@ -66,6 +67,23 @@ SB_API size_t sb_op_layernorm_bwd_workspace_size(int32_t rows, int32_t d);
 SB_API int sb_op_layernorm_bwd(uint32_t elem, const void* dy, const void* x, const void* mean, const void* rstd,
                                const void* gamma, void* dres, void* dgamma, void* workspace, size_t workspace_bytes,
                                int32_t rows, int32_t d, void* stream);
+
+/* The same layer-norm VJP for callers that cannot allocate device memory
+ * while they run (a host runtime that owns the device heap through its own
+ * allocator and passes only finished buffers and a stream, or a
+ * latency-critical loop that cannot afford cudaMalloc's device-wide
+ * synchronisation). No counterpart in the reference: it exists for such
+ * callers of this library. It takes no workspace: the dgamma partial sums go
+ * to a fixed 128 KB array compiled into the library (held on every GPU that
+ * uses it until the library is unloaded). d must be a multiple of 4 and at
+ * most 4096; a larger d returns SB_OPERR_SCRATCH before any GPU work.
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture. All calls
+ * share the array, so calls that overlap on the GPU race: serialise them.
+ * Allocates nothing (no cudaMalloc / cudaFree). */
+SB_API int sb_op_layernorm_bwd_noalloc(uint32_t elem, const void* dy, const void* x, const void* mean,
+                                       const void* rstd, const void* gamma, void* dres, void* dgamma, int32_t rows,
+                                       int32_t d, void* stream);
 
 /* cross-entropy-loss fused with its VJP (sheaf/lib/nn.shf:28-30,44-50):
  *   loss_f32[0] = -mean_r log_softmax(logits[r])[targets[r]];

@@ -470,6 +470,25 @@ int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean
   return column_sum(ws, grid, D, dgamma, dgamma_f32, s);
 }
 
+// Same VJP with the number of blocks capped at `max_blocks`, so that the
+// dgamma partial sums fit a caller-provided scratch of max_blocks * D floats.
+int layernorm_bwd_capped(const float* dy, const float* x, const float* mean, const float* rstd, const void* gamma,
+                         bool gamma_f32, float* dres, void* dgamma, bool dgamma_f32, float* scratch, int max_blocks,
+                         int rows, int D, cudaStream_t s) {
+  if (rows <= 0 || D <= 0 || (D & 3) || max_blocks <= 0) return 1;
+  const int warps = 8;
+  const int grid = std::min(std::min((rows + warps - 1) / warps, 2 * num_sms_cached()), max_blocks);
+  const size_t smem = static_cast<size_t>(warps) * D * sizeof(float);
+  if (smem > 200 * 1024) return 1;
+  SB_LN_DISPATCH((D + 127) / 128, ({
+    auto k = ln_bwd_kernel<V, float>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    k<<<grid, warps * 32, smem, s>>>(dy, x, mean, rstd, gamma, gamma_f32, dres, nullptr, scratch, rows, D);
+  }));
+  if (cudaPeekAtLastError() != cudaSuccess) return 4;
+  return column_sum(scratch, grid, D, dgamma, dgamma_f32, s);
+}
+
 size_t cross_entropy_workspace_bytes(int rows) {
   return static_cast<size_t>(std::min((rows + 7) / 8, 4 * num_sms_cached())) * sizeof(float);
 }

@@ -25,6 +25,12 @@ int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean
                   bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma, bool dgamma_f32, float* ws,
                   int rows, int D, cudaStream_t s);
 
+// layernorm_bwd (f32 dy) with at most `max_blocks` blocks; `scratch` holds
+// max_blocks * D floats of dgamma partials.
+int layernorm_bwd_capped(const float* dy, const float* x, const float* mean, const float* rstd, const void* gamma,
+                         bool gamma_f32, float* dres, void* dgamma, bool dgamma_f32, float* scratch, int max_blocks,
+                         int rows, int D, cudaStream_t s);
+
 // loss = -mean(log_softmax(logits)[target]); dlogits = (softmax - onehot) / rows.
 size_t cross_entropy_workspace_bytes(int rows);
 int cross_entropy_fwd_bwd(const void* logits, bool f32, long ld, int rows, int V, const float* targets, void* dlogits,
