@@ -262,10 +262,19 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc(const __grid_constant__ CU
 // ---------------------------------------------------------------------------
 
 constexpr size_t kBwdSmem = 1024 + 2 * kTileBytes /*K,V*/ + 4 * kTileBytes /*Q,dO x2*/ +
-                            4 * kTileBytes /*P^T, dS^T*/ + 4 * kT * 4 /*lse, delta x2*/ + 16 * 8 + 16;
+                            4 * kTileBytes /*P^T, dS^T*/ + 2 * kTileBytes /*dQ staging*/ +
+                            4 * kT * 4 /*lse, delta x2*/ + 16 * 8 + 16;
+
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t smem_src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_src), "r"(x), "r"(y)
+               : "memory");
+}
 
 __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CUtensorMap tm_qkv,
-                                                      const __grid_constant__ CUtensorMap tm_do, AttnArgs a) {
+                                                      const __grid_constant__ CUtensorMap tm_do,
+                                                      const __grid_constant__ CUtensorMap tm_dq, AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = sm;
@@ -274,7 +283,8 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
   uint8_t* sdO = sQ + 2 * kTileBytes;  // [2]
   uint8_t* sPT = sdO + 2 * kTileBytes;  // 32 KB
   uint8_t* sdST = sPT + 2 * kTileBytes;  // 32 KB
-  float* sLse = reinterpret_cast<float*>(sdST + 2 * kTileBytes);  // [2][128]
+  uint8_t* sStg = sdST + 2 * kTileBytes;  // 4 warps x 2 x (32 rows x 128 B) dQ staging
+  float* sLse = reinterpret_cast<float*>(sStg + 2 * kTileBytes);  // [2][128]
   float* sDel = sLse + 2 * kT;                                     // [2][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 2 * kT);
   uint64_t* kv_full = bars + 0;
@@ -312,6 +322,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_dq);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -464,16 +475,29 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_empty);
-      const int q = i * kT + tid;
-      if (q < a.T) {
-        float* dst = a.dq_acc + static_cast<long>(row0 + q) * a.D + h * kHd;
-#pragma unroll
-        for (int u = 0; u < 32; ++u) {
-          atomicAdd(dst + u, __uint_as_float(q0[u]));
-          atomicAdd(dst + 32 + u, __uint_as_float(q1[u]));
+      // This warp's 32 query rows x 64 columns of dQ are added into the fp32
+      // accumulator with two bulk tensor reduce-adds (32 columns each). Rows
+      // past T hold exact zeros (their P and dS are zero).
+      {
+        const uint32_t slot0 = smem_u32(sStg) + (warp - 2) * 8192, slot1 = slot0 + 4096;
+        if (it > 0) {
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+        }
+        st_row128_sw(slot0, lane, q0);
+        st_row128_sw(slot1, lane, q1);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int y = row0 + i * kT + quarter * 32;
+          tma_reduce_add_2d(&tm_dq, slot0, h * kHd, y);
+          tma_reduce_add_2d(&tm_dq, slot1, h * kHd + 32, y);
+          bulk_commit();
         }
       }
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
     if (ok && mbar_wait(acc_full, 0, a.err, abort_flag)) {
       tc_fence_after();
       uint32_t k0[32], k1[32], v0[32], v1[32];
@@ -571,9 +595,10 @@ int attention_bwd_tc(const void* qkv, const void* o, const void* dout, const flo
   const int D = sh.H * sh.Hd, N = sh.B * sh.T;
   float* dq_acc = ws;
   if (cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(N) * D * sizeof(float), s) != cudaSuccess) return 4;
-  alignas(64) CUtensorMap tq, td;
+  alignas(64) CUtensorMap tq, td, tdq;
   if (!make_tma_2d_bf16(&tq, qkv, N, 3L * D, 3L * D, 64, kT)) return 2;
   if (!make_tma_2d_bf16(&td, dout, N, D, D, 64, kT)) return 2;
+  if (!make_tma_2d_f32(&tdq, dq_acc, N, D, D, 32, 32)) return 2;
   AttnArgs a{};
   a.B = sh.B;
   a.T = sh.T;
@@ -594,7 +619,7 @@ int attention_bwd_tc(const void* qkv, const void* o, const void* dout, const flo
       return 3;
     attr = true;
   }
-  attn_bwd_tc<<<sh.B * sh.H * a.ntiles, 192, kBwdSmem, s>>>(tq, td, a);
+  attn_bwd_tc<<<sh.B * sh.H * a.ntiles, 192, kBwdSmem, s>>>(tq, td, tdq, a);
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
   const long n = static_cast<long>(N) * D;
   const int blocks = static_cast<int>(std::min<long>((n / 4 + 255) / 256, 8L * num_sms()));

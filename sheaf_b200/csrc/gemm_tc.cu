@@ -444,7 +444,19 @@ struct Plan {
 Plan plan_for(const GemmDesc& d) {
   Plan p;
   p.bn = d.bn;
-  if (p.bn == 0) p.bn = (d.N > 128) ? 256 : (d.N > 64 ? 128 : 64);
+  if (p.bn == 0) {
+    // widest tile among {256, 192, 128, 64} with the least column padding
+    // (N = 384 -> 192 x 2, N = 1152 -> 192 x 6, N = 1536 -> 256 x 6)
+    p.bn = 64;
+    long best = (d.N + 63) / 64 * 64L;
+    for (int bn : {128, 192, 256}) {
+      const long padded = static_cast<long>((d.N + bn - 1) / bn) * bn;
+      if (padded <= best) {
+        best = padded;
+        p.bn = bn;
+      }
+    }
+  }
   p.m_tiles = (d.M + kBM - 1) / kBM;
   p.n_tiles = (d.N + p.bn - 1) / p.bn;
   p.kb_total = (d.K + kBK - 1) / kBK;
@@ -466,6 +478,11 @@ Plan plan_for(const GemmDesc& d) {
 
 bool make_tma_2d_bf16(void* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows) {
   return make_map_bf16(static_cast<CUtensorMap*>(map), base, rows, cols, ld, box_cols, box_rows);
+}
+
+bool make_tma_2d_f32(void* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows) {
+  return make_map(static_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, ld, box_cols,
+                  box_rows);
 }
 
 int num_sms() {
@@ -526,6 +543,7 @@ int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaS
   int rc;
   switch (p.bn) {
     case 256: rc = dispatch_major<256, 4>(d, a, out, ldo, rows, grid, s); break;
+    case 192: rc = dispatch_major<192, 4>(d, a, out, ldo, rows, grid, s); break;
     case 128: rc = dispatch_major<128, 6>(d, a, out, ldo, rows, grid, s); break;
     case 64: rc = dispatch_major<64, 8>(d, a, out, ldo, rows, grid, s); break;
     default: return 6;

@@ -53,5 +53,6 @@ int num_sms();
 // `ld` elements), box {box_cols, box_rows}, 128-byte swizzle, zero fill.
 // `map` points at a CUtensorMap (64-byte aligned storage).
 bool make_tma_2d_bf16(void* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows);
+bool make_tma_2d_f32(void* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows);
 
 }  // namespace sb
