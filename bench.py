@@ -253,6 +253,142 @@ def measure_kernel_roofline(session, reps: int = 20):
     return sum(times) / len(times), 2.0 * N * D * 4 * D
 
 
+# --------------------------------------------------------------------------
+# Primitive op sweep (bf16 and fp32): dot_general M=N=K in {512, 2048, 8192},
+# attention [16, 12, 1024, 64] fwd + VJP, layer-norm and gelu over
+# [8192, 4096]; N(0,1) values, seed 0. One JSON line per op.
+# --------------------------------------------------------------------------
+
+def _time_op(fn, reps: int, flush=None) -> float:
+    """Average ms per call of fn() over `reps`, CUDA events on the current
+    stream, L2 flushed before every timed call."""
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(reps):
+        if flush is not None:
+            flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+    return tot / reps
+
+
+def sweep_ops(only: str | None = None, reps: int = 10):
+    import torch
+
+    import sheaf_b200 as sb
+
+    L = sb.lib()
+    dev = torch.device("cuda:0")
+    torch.manual_seed(0)
+    hbm, tc_burst, _, src = peaks()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    st = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+    lines = []
+
+    def emit(d):
+        d.update({"data": "synthetic N(0,1) seed 0", "peak_source": src})
+        print(json.dumps(d), flush=True)
+        lines.append(d)
+
+    def want(name):
+        return only is None or only == name
+
+    for kind, elem, dt in [("bf16", BF16, torch.bfloat16), ("f32", F32, torch.float32)]:
+        for n in (512, 2048, 8192):
+            name = f"gemm_{kind}_{n}"
+            if not want(name):
+                continue
+            a = torch.randn(n, n, device=dev).to(dt)
+            b = torch.randn(n, n, device=dev).to(dt)
+            c = torch.empty(n, n, device=dev, dtype=dt)
+            wsb = L.sb_op_matmul_workspace_size(elem, 0, 0, n, n, n)
+            ws = torch.empty(max(wsb // 4, 1), device=dev)
+            fn = lambda: L.sb_op_matmul(elem, a.data_ptr(), n, 0, b.data_ptr(), n, 0, n, n, n, c.data_ptr(), n,  # noqa
+                                        elem, ws.data_ptr(), wsb, st())
+            ms = _time_op(fn, reps, flush)
+            tf = 2.0 * n ** 3 / (ms / 1e3) / 1e12
+            emit({"op": name, "ms": ms, "achieved": tf, "unit": "TFLOP/s", "bound": "tensor" if kind == "bf16" else
+                  "fp32 FFMA", "frac_of_bf16_peak": tf / tc_burst})
+        name = f"gemm_{kind}_step_fc"  # the step's fc GEMM: [16384, 384] x [384, 1536]^T
+        if want(name):
+            M, N, K = CFG["batch"] * CFG["seq"], 4 * CFG["n_embd"], CFG["n_embd"]
+            a = torch.randn(M, K, device=dev).to(dt)
+            w = torch.randn(N, K, device=dev).to(dt)
+            c = torch.empty(M, N, device=dev, dtype=dt)
+            fn = lambda: L.sb_op_matmul(elem, a.data_ptr(), K, 0, w.data_ptr(), K, 1, M, N, K, c.data_ptr(), N,  # noqa
+                                        elem, None, 0, st())
+            ms = _time_op(fn, reps, flush)
+            tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+            emit({"op": name, "ms": ms, "achieved": tf, "unit": "TFLOP/s", "bound": "tensor" if kind == "bf16" else
+                  "fp32 FFMA", "frac_of_bf16_peak": tf / tc_burst})
+        B, T, H, Hd = 16, 1024, 12, 64
+        name = f"attention_{kind}_16x12x1024x64"
+        if want(name):
+            D = H * Hd
+            qkv = torch.randn(B * T, 3 * D, device=dev).to(dt)
+            o = torch.empty(B * T, D, device=dev, dtype=dt)
+            do = torch.randn(B * T, D, device=dev).to(dt)
+            dqkv = torch.empty(B * T, 3 * D, device=dev, dtype=dt)
+            lse = torch.empty(B * H * T, device=dev)
+            wsb = L.sb_op_attention_bwd_workspace_size(elem, B, T, H, Hd)
+            ws = torch.empty(wsb // 4 + 1, device=dev)
+            f_fwd = lambda: L.sb_op_attention_fwd(elem, qkv.data_ptr(), o.data_ptr(), lse.data_ptr(), B, T, H, Hd,  # noqa
+                                                  st())
+            f_bwd = lambda: L.sb_op_attention_bwd(elem, qkv.data_ptr(), o.data_ptr(), do.data_ptr(),  # noqa
+                                                  lse.data_ptr(), dqkv.data_ptr(), ws.data_ptr(), wsb, B, T, H, Hd,
+                                                  st())
+            mf, mb = _time_op(f_fwd, reps, flush), _time_op(f_bwd, reps, flush)
+            dense = 4.0 * B * H * T * T * Hd
+            emit({"op": name, "fwd_ms": mf, "vjp_ms": mb, "dense_fwd_gflop": dense / 1e9,
+                  "achieved_fwd": dense / 2 / (mf / 1e3) / 1e12, "achieved_vjp": 2.5 * dense / 2 / (mb / 1e3) / 1e12,
+                  "unit": "TFLOP/s (causal: half the dense count)", "bound": "tensor",
+                  "frac_fwd": dense / 2 / (mf / 1e3) / 1e12 / tc_burst})
+        R, C = 8192, 4096
+        es = 2 if kind == "bf16" else 4
+        name = f"layernorm_{kind}_8192x4096"
+        if want(name):
+            x = torch.randn(R, C, device=dev)
+            g = torch.randn(C, device=dev).to(dt)
+            y = torch.empty(R, C, device=dev, dtype=dt)
+            mean, rstd = torch.empty(R, device=dev), torch.empty(R, device=dev)
+            dy, dres = torch.randn(R, C, device=dev), torch.zeros(R, C, device=dev)
+            dg = torch.empty(C, device=dev, dtype=dt)
+            wsb = L.sb_op_layernorm_bwd_workspace_size(R, C)
+            ws = torch.empty(wsb // 4 + 1, device=dev)
+            f_fwd = lambda: L.sb_op_layernorm_fwd(elem, x.data_ptr(), g.data_ptr(), y.data_ptr(), mean.data_ptr(),  # noqa
+                                                  rstd.data_ptr(), R, C, st())
+            f_bwd = lambda: L.sb_op_layernorm_bwd(elem, dy.data_ptr(), x.data_ptr(), mean.data_ptr(),  # noqa
+                                                  rstd.data_ptr(), g.data_ptr(), dres.data_ptr(), dg.data_ptr(),
+                                                  ws.data_ptr(), wsb, R, C, st())
+            mf, mb = _time_op(f_fwd, reps, flush), _time_op(f_bwd, reps, flush)
+            bf = R * C * (4 + es)          # x (f32) in, y out
+            bb = R * C * (4 + 4 + 4 + 4)   # dy, x in; dres in/out
+            emit({"op": name, "fwd_ms": mf, "vjp_ms": mb, "achieved_fwd": bf / (mf / 1e3) / 1e9,
+                  "achieved_vjp": bb / (mb / 1e3) / 1e9, "unit": "GB/s", "bound": "hbm", "peak": hbm,
+                  "frac_fwd": bf / (mf / 1e3) / 1e9 / hbm, "frac_vjp": bb / (mb / 1e3) / 1e9 / hbm})
+        name = f"gelu_{kind}_8192x4096"
+        if want(name):
+            n = R * C
+            x = torch.randn(n, device=dev).to(dt)
+            gg = torch.randn(n, device=dev).to(dt)
+            y = torch.empty(n, device=dev, dtype=dt)
+            mf = _time_op(lambda: L.sb_op_gelu_fwd(elem, x.data_ptr(), y.data_ptr(), n, st()), reps, flush)
+            mb = _time_op(lambda: L.sb_op_gelu_bwd(elem, x.data_ptr(), gg.data_ptr(), y.data_ptr(), n, st()), reps,
+                          flush)
+            emit({"op": name, "fwd_ms": mf, "vjp_ms": mb, "achieved_fwd": 2 * n * es / (mf / 1e3) / 1e9,
+                  "achieved_vjp": 3 * n * es / (mb / 1e3) / 1e9, "unit": "GB/s", "bound": "hbm", "peak": hbm,
+                  "frac_fwd": 2 * n * es / (mf / 1e3) / 1e9 / hbm, "frac_vjp": 3 * n * es / (mb / 1e3) / 1e9 / hbm})
+    return lines
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -260,7 +396,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="sheaf_b200", choices=["sheaf_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="primitive op sweep (one JSON line per op)")
+    ap.add_argument("--op", default=None, help="run only this op of the sweep (e.g. gemm_bf16_8192)")
     args = ap.parse_args()
+    if args.sweep or args.op:
+        sweep_ops(args.op, reps=args.steps if args.op else 10)
+        return
     world, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, world, rank)

@@ -95,6 +95,14 @@ SB_API int sb_op_cross_entropy(uint32_t elem, const void* logits, int64_t ld, in
                                const void* targets, void* dlogits, int64_t ldd, void* workspace,
                                size_t workspace_bytes, void* loss_f32, void* stream);
 
+/* GELU, tanh form (sheaf/lib/nn.shf:10-11), elementwise over n values of
+ * type `elem`: y = gelu(x). The VJP (chain rule through the inlined tanh /
+ * multiply / add ops, sheaf/src/autodiff/reverse.rs:969-975) is
+ * dx = g * gelu'(x). Inside the fused plans GELU lives in GEMM epilogues;
+ * these standalone forms serve the primitive sweep and other graphs. */
+SB_API int sb_op_gelu_fwd(uint32_t elem, const void* x, void* y, int64_t n, void* stream);
+SB_API int sb_op_gelu_bwd(uint32_t elem, const void* x, const void* g, void* dx, int64_t n, void* stream);
+
 /* Token + position embedding: x[n] = wte[clamp(ids[n])] + wpe[n % t] (f32 out)
  * (`stablehlo.convert` + `stablehlo.gather`,
  * sheaf/src/lowering/stablehlo/indexing_ops.rs:416-484; wpe `slice`). */

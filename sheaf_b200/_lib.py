@@ -46,6 +46,8 @@ SIGNATURES: dict[str, tuple] = {
     "sb_op_cross_entropy_workspace_size": (C.c_size_t, [C.c_int32]),
     "sb_op_cross_entropy": (C.c_int, [C.c_uint32, _P, C.c_int64, C.c_int32, C.c_int32, _P, _P, C.c_int64, _P,
                                       C.c_size_t, _P, _P]),
+    "sb_op_gelu_fwd": (C.c_int, [C.c_uint32, _P, _P, C.c_int64, _P]),
+    "sb_op_gelu_bwd": (C.c_int, [C.c_uint32, _P, _P, _P, C.c_int64, _P]),
     "sb_op_embedding_fwd": (C.c_int, [C.c_uint32, _P, _P, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P]),
     "sb_op_embedding_bwd_workspace_size": (C.c_size_t, [C.c_int32, C.c_int32]),
     "sb_op_embedding_bwd": (C.c_int, [C.c_uint32, _P, _P, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P,

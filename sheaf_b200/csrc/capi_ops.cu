@@ -98,6 +98,16 @@ int sb_op_cross_entropy(uint32_t elem, const void* logits, int64_t ld, int32_t r
                                    nullptr, static_cast<cudaStream_t>(stream));
 }
 
+int sb_op_gelu_fwd(uint32_t elem, const void* x, void* y, int64_t n, void* stream) {
+  if (!float_elem(elem) || !x || !y || n <= 0) return SB_OPERR_ARGS;
+  return sb::gelu(x, nullptr, y, elem == SB_ELEM_F32, false, n, static_cast<cudaStream_t>(stream));
+}
+
+int sb_op_gelu_bwd(uint32_t elem, const void* x, const void* g, void* dx, int64_t n, void* stream) {
+  if (!float_elem(elem) || !x || !g || !dx || n <= 0) return SB_OPERR_ARGS;
+  return sb::gelu(x, g, dx, elem == SB_ELEM_F32, true, n, static_cast<cudaStream_t>(stream));
+}
+
 int sb_op_embedding_fwd(uint32_t elem, const void* ids, const void* wte, const void* wpe, void* x, int32_t ntok,
                         int32_t t, int32_t v, int32_t d, void* stream) {
   if (!float_elem(elem) || !ids || !wte || !wpe || !x || t <= 0 || v <= 0) return SB_OPERR_ARGS;

@@ -466,6 +466,9 @@ class GptVagModule : public Module {
           cudaGraphNodeType t;
           if (cudaGraphNodeGetType(n, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels_per_step;
         }
+        // NCCL's own kernels (one per bucket all-reduce and one for the loss)
+        // are not library kernels
+        if (dp) kernels_per_step -= std::min<uint64_t>(kernels_per_step, static_cast<uint64_t>(L) + 3);
         ce = cudaGraphInstantiate(&exec, graph, 0);
         cudaGraphDestroy(graph);
         if (ce != cudaSuccess) return make_status(SB_STATUS_INTERNAL, std::string("graph instantiate: ") + cudaGetErrorString(ce));

@@ -387,6 +387,43 @@ __global__ void embed_bwd_pos_kernel(const float* __restrict__ dx, int B, int T,
   }
 }
 
+// Standalone GELU (tanh form, lib/nn.shf:10-11) and its VJP, 8 elements per
+// thread per iteration (16-byte bf16 / 2 x 16-byte f32 accesses).
+__device__ __forceinline__ float gelu_f(float x) {
+  const float inner = x + 0.044715f * (x * (x * x));
+  return 0.5f * (x * (1.0f + tanhf(0.7978846f * inner)));
+}
+__device__ __forceinline__ float gelu_df(float x) {
+  const float x2 = x * x;
+  const float t = tanhf(0.7978846f * (x + 0.044715f * (x * x2)));
+  return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * 0.7978846f * (1.0f + 0.134145f * x2);
+}
+
+template <typename T, bool BWD>
+__global__ void gelu_kernel(const T* __restrict__ x, const T* __restrict__ g, T* __restrict__ y, long n) {
+  const long n8 = n / 8;
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const float4 a0 = load4(x + 8 * i), a1 = load4(x + 8 * i + 4);
+    float4 r0, r1;
+    if (BWD) {
+      const float4 g0 = load4(g + 8 * i), g1 = load4(g + 8 * i + 4);
+      r0 = make_float4(g0.x * gelu_df(a0.x), g0.y * gelu_df(a0.y), g0.z * gelu_df(a0.z), g0.w * gelu_df(a0.w));
+      r1 = make_float4(g1.x * gelu_df(a1.x), g1.y * gelu_df(a1.y), g1.z * gelu_df(a1.z), g1.w * gelu_df(a1.w));
+    } else {
+      r0 = make_float4(gelu_f(a0.x), gelu_f(a0.y), gelu_f(a0.z), gelu_f(a0.w));
+      r1 = make_float4(gelu_f(a1.x), gelu_f(a1.y), gelu_f(a1.z), gelu_f(a1.w));
+    }
+    store4(y + 8 * i, r0);
+    store4(y + 8 * i + 4, r1);
+  }
+  for (long i = n8 * 8 + blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const float a = load1(x + i);
+    store1(y + i, BWD ? load1(g + i) * gelu_df(a) : gelu_f(a));
+  }
+}
+
 __global__ void convert_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, long n) {
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long>(gridDim.x) * blockDim.x)
@@ -556,6 +593,27 @@ int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V,
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
   const long total = static_cast<long>(P) * D;
   embed_bwd_pos_kernel<<<grid_for(total, 256), 256, 0, s>>>(dx, B, T, P, D, dwpe, out_f32);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+int gelu(const void* x, const void* g, void* y, bool f32, bool bwd, long n, cudaStream_t s) {
+  if (n <= 0) return 1;
+  const int blocks = grid_for((n + 7) / 8, 256);
+  if (f32) {
+    if (bwd)
+      gelu_kernel<float, true><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), static_cast<const float*>(g),
+                                                      static_cast<float*>(y), n);
+    else
+      gelu_kernel<float, false><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), nullptr, static_cast<float*>(y),
+                                                       n);
+  } else {
+    using B = __nv_bfloat16;
+    if (bwd)
+      gelu_kernel<B, true><<<blocks, 256, 0, s>>>(static_cast<const B*>(x), static_cast<const B*>(g),
+                                                  static_cast<B*>(y), n);
+    else
+      gelu_kernel<B, false><<<blocks, 256, 0, s>>>(static_cast<const B*>(x), nullptr, static_cast<B*>(y), n);
+  }
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 

@@ -45,6 +45,8 @@ int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V,
                   bool out_f32, float* ws, cudaStream_t s);
 
 int convert_f32_to_bf16(const float* in, __nv_bfloat16* out, long n, cudaStream_t s);
+// y = gelu(x) or, with bwd, y = g * gelu'(x), elementwise over n values.
+int gelu(const void* x, const void* g, void* y, bool f32, bool bwd, long n, cudaStream_t s);
 
 // Causal attention over packed qkv [B*T, 3*D] (q | k | v, heads of Hd=D/H
 // columns), o [B*T, D], lse [B*H*T] (natural-log units of the scaled scores).

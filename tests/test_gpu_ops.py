@@ -180,3 +180,23 @@ def test_attention(kind, B, T, H, Hd, cuda):
         assert_close(got[:, i * D:(i + 1) * D], ref[:, i * D:(i + 1) * D], tol, nm)
     torch.cuda.synchronize()
     assert L.sb_op_device_error() == 0
+
+
+@pytest.mark.parametrize("kind", ["f32", "bf16"])
+def test_gelu(kind, cuda):
+    import torch
+    import sheaf_b200 as sb
+
+    L = sb.lib()
+    dt = torch.float32 if kind == "f32" else torch.bfloat16
+    rng = np.random.default_rng(5)
+    n = 100003  # not a multiple of 8: exercises the tail loop
+    x = _rt((rng.standard_normal(n) * 3).astype(np.float32), kind)
+    g = _rt(rng.standard_normal(n).astype(np.float32), kind)
+    xd, gd = _dev(x, dt, cuda), _dev(g, dt, cuda)
+    y = torch.empty(n, dtype=dt, device=cuda)
+    assert L.sb_op_gelu_fwd(ELEMS[kind], xd.data_ptr(), y.data_ptr(), n, _stream()) == 0
+    tol = TOL_F32 if kind == "f32" else TOL_BF16
+    assert_close(y.float().cpu().numpy(), ops.gelu(x.astype(np.float64)), tol, "gelu")
+    assert L.sb_op_gelu_bwd(ELEMS[kind], xd.data_ptr(), gd.data_ptr(), y.data_ptr(), n, _stream()) == 0
+    assert_close(y.float().cpu().numpy(), ops.gelu_vjp(x.astype(np.float64), g.astype(np.float64)), tol, "gelu vjp")
