@@ -117,6 +117,18 @@ SB_API void* sb_buffer_device_ptr(const sb_buffer* buffer);
  * registered in the session under its `module @<name>`. */
 SB_API sb_status sb_module_load_stablehlo(sb_session* session, const char* mlir_text, size_t length,
                                           const char** out_module_name);
+/* Parses and plans a StableHLO module without a device (the checks
+ * sb_module_load_stablehlo makes before touching the GPU) and writes a short
+ * summary (ops per function, arena size, recognised model) into `buf`.
+ * UNIMPLEMENTED for ops outside the library's surface. */
+SB_API sb_status sb_stablehlo_validate(const char* mlir_text, size_t length, char* buf, size_t capacity);
+
+/* Writes a one-line-per-function description of how a loaded module executes
+ * (fused nanoGPT plan, verified or not, or the generic op-by-op executor) into
+ * `buf` (NUL-terminated, truncated to `capacity`). No reference counterpart:
+ * IREE's equivalent is `--jit-profile` / the dispatch trace. */
+SB_API sb_status sb_module_describe(sb_session* session, const char* module_name, char* buf, size_t capacity);
+
 /* Registers the fused nanoGPT value_and_grad module (the graph of
  * examples/nanogpt/model.shf + cross-entropy) for a configuration without
  * going through text. Function "value_and_grad": inputs are the 4*...-leaf

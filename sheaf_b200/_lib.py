@@ -83,6 +83,8 @@ SIGNATURES: dict[str, tuple] = {
     "sb_buffer_device_ptr": (_P, [_P]),
     "sb_module_load_stablehlo": (_P, [_P, C.c_char_p, C.c_size_t, C.POINTER(C.c_char_p)]),
     "sb_module_create_gpt_vag": (_P, [_P, C.c_char_p, C.POINTER(GptConfig)]),
+    "sb_module_describe": (_P, [_P, C.c_char_p, C.c_char_p, C.c_size_t]),
+    "sb_stablehlo_validate": (_P, [C.c_char_p, C.c_size_t, C.c_char_p, C.c_size_t]),
     "sb_call": (_P, [_P, C.c_char_p, C.POINTER(_P), C.c_size_t, C.POINTER(_P), C.c_size_t, C.POINTER(C.c_size_t)]),
 }
 

@@ -304,6 +304,32 @@ sb_status sb_module_load_stablehlo(sb_session* s, const char* text, size_t len, 
   return nullptr;
 }
 
+sb_status sb_stablehlo_validate(const char* text, size_t length, char* buf, size_t capacity) {
+  SB_RETURN_IF(!text || (!buf && capacity), SB_STATUS_INVALID_ARGUMENT, "null argument");
+  std::string summary;
+  SB_TRY(validate_stablehlo(text, length, &summary));
+  if (capacity) {
+    const size_t n = std::min(capacity - 1, summary.size());
+    std::memcpy(buf, summary.data(), n);
+    buf[n] = '\0';
+  }
+  return nullptr;
+}
+
+sb_status sb_module_describe(sb_session* s, const char* module_name, char* buf, size_t capacity) {
+  SB_RETURN_IF(!s || !module_name || (!buf && capacity), SB_STATUS_INVALID_ARGUMENT, "null argument");
+  std::lock_guard<std::mutex> lk(s->mu);
+  auto it = s->modules.find(module_name);
+  if (it == s->modules.end()) return make_status(SB_STATUS_NOT_FOUND, std::string("module not loaded: ") + module_name);
+  const std::string d = describe_stablehlo_module(it->second.get());
+  if (capacity) {
+    const size_t n = std::min(capacity - 1, d.size());
+    std::memcpy(buf, d.data(), n);
+    buf[n] = '\0';
+  }
+  return nullptr;
+}
+
 sb_status sb_call(sb_session* s, const char* qualified_name, sb_buffer* const* inputs, size_t in_count,
                   sb_buffer** outputs, size_t out_capacity, size_t* out_count) {
   SB_RETURN_IF(!s || !qualified_name || (in_count && !inputs) || !out_count, SB_STATUS_INVALID_ARGUMENT,
@@ -313,6 +339,9 @@ sb_status sb_call(sb_session* s, const char* qualified_name, sb_buffer* const* i
   SB_RETURN_IF(dot == std::string::npos, SB_STATUS_INVALID_ARGUMENT, "expected <module>.<function>");
   const std::string mod = q.substr(0, dot), fn = q.substr(dot + 1);
   cudaSetDevice(s->device);
+  // a runtime error left by the caller's own CUDA work must not be reported
+  // as a failure of this call's launches
+  (void)cudaGetLastError();
   std::vector<Buffer*> in(inputs, inputs + in_count);
   for (Buffer* b : in) {
     SB_RETURN_IF(!b, SB_STATUS_INVALID_ARGUMENT, "null input buffer");

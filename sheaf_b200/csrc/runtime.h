@@ -108,6 +108,8 @@ sb_status make_gpt_vag_module(Session& s, const std::string& name, const GptShap
 
 // Parses StableHLO text and maps it onto the kernel library (stablehlo.cpp).
 sb_status load_stablehlo_module(Session& s, const char* text, size_t len, std::unique_ptr<Module>* out);
+std::string describe_stablehlo_module(Module* m);
+sb_status validate_stablehlo(const char* text, size_t len, std::string* summary);
 
 // NCCL data-parallel group (comm.cpp).
 sb_status comm_init(Session& s, const void* unique_id, size_t id_bytes, int rank, int world);

@@ -130,6 +130,11 @@ class Session:
         _check(lib().sb_module_load_stablehlo(self._h, data, len(data), C.byref(name)))
         return name.value.decode()
 
+    def describe(self, module: str) -> str:
+        buf = C.create_string_buffer(4096)
+        _check(lib().sb_module_describe(self._h, module.encode(), buf, 4096))
+        return buf.value.decode()
+
     def create_gpt_vag(self, name: str, *, n_layer, n_head, n_embd, block_size, vocab_size, batch, seq,
                        elem=ELEM_BF16) -> str:
         cfg = _lib.GptConfig(n_layer, n_head, n_embd, block_size, vocab_size, batch, seq, elem)
@@ -142,6 +147,15 @@ class Session:
         n = C.c_size_t()
         _check(lib().sb_call(self._h, qualified_name.encode(), arr, len(inputs), outs, max_outputs, C.byref(n)))
         return [Buffer(C.c_void_p(outs[i])) for i in range(n.value)]
+
+
+def validate_stablehlo(text: str) -> str:
+    """Parses and plans a StableHLO module on the host (no device needed);
+    returns the summary or raises SheafB200Error (UNIMPLEMENTED = 12)."""
+    data = text.encode()
+    buf = C.create_string_buffer(8192)
+    _check(lib().sb_stablehlo_validate(data, len(data), buf, 8192))
+    return buf.value.decode()
 
 
 class Buffer:

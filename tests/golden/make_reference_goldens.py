@@ -56,6 +56,11 @@ def main(root: Path) -> None:
             return [int(v.strip(), 0) for v in s.split(",")]
         out["threefry_kat"].append({"counter": parse(m.group(1)), "key": parse(m.group(2)),
                                     "expected": parse(m.group(3))})
+    # the worked StableHLO example printed in docs/key-concepts.md (a module
+    # exactly as the emitter produces it, wrapped lines and comments included)
+    doc = (root / "docs" / "key-concepts.md").read_text()
+    start = doc.index("```mlir", doc.index("produces typed MLIR")) + len("```mlir")
+    out["docs_mlir_forward"] = doc[start:doc.index("```", start)].strip("\n") + "\n"
     (HERE / "reference_goldens.json").write_text(json.dumps(out, indent=1) + "\n")
     print(f"wrote {len(out['vag'])} VAG, {len(out['forward'])} forward, {len(out['threefry_kat'])} KAT cases")
 

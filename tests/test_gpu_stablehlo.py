@@ -1,0 +1,152 @@
+"""The StableHLO front door on the GPU (sb_module_load_stablehlo + sb_call).
+
+* the module printed in the reference's docs (docs/key-concepts.md:170-184);
+* modules built from the reference's own value-and-grad goldens
+  (sheaf/tests/vag_tests.yaml) in the emitter's text forms: the executor must
+  reproduce the expected loss and gradient;
+* the MLP value_and_grad (the MLP workload) against the oracle;
+* the nanoGPT value_and_grad: recognised, run through the fused plan after a
+  first-call check against the generic executor, and compared to the oracle.
+"""
+import json
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import dtype as odt
+from oracle import hlo_emit, models
+from oracle.hlo_emit import Emitter, arg
+from tests.parity import TOL_BF16, TOL_F32, assert_close
+
+pytestmark = pytest.mark.gpu
+
+GOLD = json.loads((Path(__file__).parent / "golden" / "reference_goldens.json").read_text())
+NUM = re.compile(r"-?\d+(?:\.\d*)?(?:e-?\d+)?")
+F32, BF16 = 0x21000020, 0x22000010
+
+
+@pytest.fixture(scope="module")
+def session(cuda):
+    from sheaf_b200.runtime import Session
+
+    return Session(0)
+
+
+def run(session, text, inputs, elems):
+    name = session.load_stablehlo(text)
+    fn = re.search(r"func\.func @([\w]+)", text).group(1)
+    bufs = [session.upload(a, e) for a, e in zip(inputs, elems)]
+    outs = session.call(f"{name}.{fn}", bufs)
+    return name, [o.to_host() for o in outs]
+
+
+def test_docs_forward_module(session):
+    rng = np.random.default_rng(0)
+    W = rng.standard_normal((768, 768)).astype(np.float32) * 0.05
+    b = rng.standard_normal(768).astype(np.float32)
+    x = rng.standard_normal((4, 768)).astype(np.float32)
+    _, (out,) = run(session, GOLD["docs_mlir_forward"], [W, b, x], [F32] * 3)
+    assert_close(out, x.astype(np.float64) @ W + b, TOL_F32, "forward")
+
+
+def _golden(name):
+    """Sheaf expression of vag_tests.yaml -> (module text, wrt argument)."""
+    e = Emitter()
+    if name == "vag-matmul":
+        w = arg(0, (2, 2), "f32")
+        x = e.const_array([[1.0, 2.0]])
+        y = e.matmul(x, w)
+        loss = e.sum_all(y)
+        g = e.matmul(e.transpose(x, [1, 0]), e.splat(1.0, (1, 2), "f32"))
+        return e.module("__vag_g", "value_and_grad", [w], [loss, g]), np.eye(2, dtype=np.float32)
+    if name == "vag-gelu":
+        x = arg(0, (2,), "f32")
+        loss = e.sum_all(hlo_emit.gelu(e, x))
+        g = hlo_emit.gelu_vjp(e, x, e.splat(1.0, (2,), "f32"))
+        return e.module("__vag_g", "value_and_grad", [x], [loss, g]), np.array([0.0, 1.0], np.float32)
+    if name == "vag-softmax":
+        x = arg(0, (3,), "f32")
+        sm = hlo_emit.softmax(e, x)
+        sel = e.const_array([1.0, 0.0, 0.0])
+        loss = e.sum_all(e.mul(sm, sel))
+        g = e.mul(sm, e.sub(sel, e.sum(e.mul(sel, sm), -1, keepdims=True)))
+        return e.module("__vag_g", "value_and_grad", [x], [loss, g]), np.array([1.0, 2.0, 3.0], np.float32)
+    if name == "vag-cross-entropy-loss":
+        w = arg(0, (3, 3), "f32")
+        x = e.const_array([[1.0, 2.0, 3.0]])
+        logits = e.matmul(x, w)
+        tgt = e.const_array([[2.0]])
+        loss, dlogits = hlo_emit.cross_entropy(e, e.reshape(logits, (1, 1, 3)), tgt)
+        g = e.matmul(e.transpose(x, [1, 0]), e.reshape(dlogits, (1, 3)))
+        return e.module("__vag_g", "value_and_grad", [w], [loss, g]), np.eye(3, dtype=np.float32)
+    if name == "vag-get-embedding-repeated":
+        emb = arg(0, (3, 2), "f32")
+        ids = e.const_array([0.0, 0.0, 1.0])
+        loss = e.sum_all(e.gather_rows(emb, ids))
+        oh = e.one_hot(ids, 3)
+        g = e.matmul(e.transpose(oh, [1, 0]), e.splat(1.0, (3, 2), "f32"))
+        return e.module("__vag_g", "value_and_grad", [emb], [loss, g]), \
+            np.array([[1, 2], [3, 4], [5, 6]], np.float32)
+    raise KeyError(name)
+
+
+@pytest.mark.parametrize("name", ["vag-matmul", "vag-gelu", "vag-softmax", "vag-cross-entropy-loss",
+                                  "vag-get-embedding-repeated"])
+def test_vag_goldens_through_the_front_door(session, name):
+    text, x = _golden(name)
+    _, (loss, grad) = run(session, text, [x], [F32])
+    got = np.concatenate([[float(loss)], grad.reshape(-1)])
+    exp = np.array([float(v) for v in NUM.findall(GOLD["vag"][name]["expected"])])
+    np.testing.assert_allclose(got, exp, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_mlp_vag_front_door(session, dt):
+    leaves, x, y = models.mlp_inputs()
+    text = hlo_emit.mlp_vag_module(dt=dt)
+    elem = F32 if dt == "f32" else BF16
+    ins = [np.asarray(v, np.float32) for v in leaves + [x, y]]
+    if dt == "bf16":
+        ins = [odt.round_bf16(v) for v in ins]
+        leaves = ins[:4]
+    name, outs = run(session, text, ins, [elem] * 6)
+    assert "generic executor" in session.describe(name)
+    ref_loss, ref_grads = models.mlp_value_and_grad(ins[:4], ins[4], ins[5], dtype=np.float64)
+    tol = TOL_F32 if dt == "f32" else TOL_BF16
+    assert abs(float(outs[0]) - ref_loss) <= tol * abs(ref_loss)
+    for nm, g, r in zip(["dW1", "db1", "dW2", "db2"], outs[1:], ref_grads):
+        assert_close(g, r, tol if dt == "f32" else 4e-2, nm)
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f32"])
+def test_nanogpt_vag_front_door_uses_verified_fused_plan(session, dt):
+    cfg = models.GPTConfig(n_layer=2, n_head=2, n_embd=128, block_size=64, vocab_size=65, batch=4, seq=64)
+    leaves, x, y = models.gpt_inputs(cfg)
+    if dt == "bf16":
+        leaves = [odt.round_bf16(l) for l in leaves]
+    elem = BF16 if dt == "bf16" else F32
+    text = hlo_emit.gpt_vag_module(cfg, dt)
+    name = session.load_stablehlo(text)
+    assert "pending first-call verification" in session.describe(name)
+    bufs = [session.upload(l, elem) for l in leaves] + [session.upload(x, F32), session.upload(y, F32)]
+    first = [o.to_host() for o in session.call(f"{name}.value_and_grad", bufs)]
+    assert "verified" in session.describe(name), session.describe(name)
+    second = [o.to_host() for o in session.call(f"{name}.value_and_grad", bufs)]
+    ref_loss, ref_grads = models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float64)
+    tol = TOL_F32 if dt == "f32" else TOL_BF16
+    for outs in (first, second):
+        assert abs(float(outs[0]) - ref_loss) <= tol * abs(ref_loss)
+        for nm, g, r in zip(models.gpt_leaf_names(cfg), outs[1:], ref_grads):
+            assert_close(g, r, tol, nm)
+
+
+def test_unimplemented_op_fails_like_a_compile_error(session):
+    from sheaf_b200.runtime import SheafB200Error
+
+    text = ("module @m {\n func.func @f(%arg0: tensor<4xf32>) -> tensor<4xf32> {\n"
+            "    %0 = stablehlo.cbrt %arg0 : tensor<4xf32>\n    return %0 : tensor<4xf32>\n }\n}\n")
+    with pytest.raises(SheafB200Error) as e:
+        session.load_stablehlo(text)
+    assert e.value.code == 12
