@@ -95,6 +95,19 @@ def test_vag_full_nanogpt_properties(cuda):
     assert abs(loss - ref) <= TOL_BF16 * abs(ref), (loss, ref)
 
 
+def test_gpt2_small_shape_matches_oracle(cuda):
+    """GPT-2-small shape (12L/12H/768, V=50304, block 1024), bf16, at one
+    sequence of 64 tokens (the oracle's fp64 evaluation stays in seconds)."""
+    cfg = models.GPTConfig(n_layer=12, n_head=12, n_embd=768, block_size=1024, vocab_size=50304, batch=1, seq=64)
+    leaves, x, y = models.gpt_inputs(cfg)
+    leaves = [odt.round_bf16(l) for l in leaves]
+    (out,) = run_vag(cfg, "bf16", leaves, x, y)
+    ref_loss, ref_grads = models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float64)
+    assert abs(float(out[0]) - ref_loss) <= TOL_BF16 * abs(ref_loss)
+    for nm, g, r in zip(models.gpt_leaf_names(cfg), out[1:], ref_grads):
+        assert_close(g, r, TOL_BF16, nm)
+
+
 def test_vag_rejects_bad_inputs(cuda):
     from sheaf_b200.runtime import SheafB200Error, Session
 

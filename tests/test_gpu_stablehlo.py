@@ -142,6 +142,26 @@ def test_nanogpt_vag_front_door_uses_verified_fused_plan(session, dt):
             assert_close(g, r, tol, nm)
 
 
+def test_full_nanogpt_text_module_verifies_at_full_size(session):
+    """The 1948-op nanoGPT-char value_and_grad text (B=64, T=256): the first
+    call runs the generic executor and the fused plan on the same inputs and
+    keeps the fused plan; the loss agrees with the oracle's forward."""
+    from oracle import ops
+
+    cfg = models.NANOGPT_CHAR
+    leaves, x, y = models.gpt_inputs(cfg)
+    leaves = [odt.round_bf16(l) for l in leaves]
+    name = session.load_stablehlo(hlo_emit.gpt_vag_module(cfg, "bf16"))
+    bufs = [session.upload(l, BF16) for l in leaves] + [session.upload(x, F32), session.upload(y, F32)]
+    out = session.call(f"{name}.value_and_grad", bufs)
+    assert "verified" in session.describe(name), session.describe(name)
+    loss = float(out[0].to_host())
+    ref = float(ops.cross_entropy(models.gpt_forward_logits(leaves, x, cfg, dtype=np.float32), y))
+    assert abs(loss - ref) <= TOL_BF16 * abs(ref)
+    out2 = session.call(f"{name}.value_and_grad", bufs)
+    assert abs(float(out2[0].to_host()) - loss) <= 1e-6 * abs(loss)
+
+
 def test_unimplemented_op_fails_like_a_compile_error(session):
     from sheaf_b200.runtime import SheafB200Error
 
