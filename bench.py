@@ -255,7 +255,8 @@ def measure_kernel_roofline(session, reps: int = 20):
 
 # --------------------------------------------------------------------------
 # Primitive op sweep (bf16 and fp32): dot_general M=N=K in {512, 2048, 8192},
-# attention [16, 12, 1024, 64] fwd + VJP, layer-norm and gelu over
+# attention [16, 12, 1024, 64] and the step's [64, 6, 256, 64] fwd + VJP,
+# layer-norm over [8192, 4096] and the step's [16384, 384], gelu over
 # [8192, 4096]; N(0,1) values, seed 0. One JSON line per op.
 # --------------------------------------------------------------------------
 
@@ -329,9 +330,10 @@ def sweep_ops(only: str | None = None, reps: int = 10):
             tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
             emit({"op": name, "ms": ms, "achieved": tf, "unit": "TFLOP/s", "bound": "tensor" if kind == "bf16" else
                   "fp32 FFMA", "frac_of_bf16_peak": tf / tc_burst})
-        B, T, H, Hd = 16, 1024, 12, 64
-        name = f"attention_{kind}_16x12x1024x64"
-        if want(name):
+        for B, T, H, Hd in ((16, 1024, 12, 64), (CFG["batch"], CFG["seq"], CFG["n_head"], CFG["n_embd"] // CFG["n_head"])):
+            name = f"attention_{kind}_{B}x{H}x{T}x{Hd}"
+            if not want(name):
+                continue
             D = H * Hd
             qkv = torch.randn(B * T, 3 * D, device=dev).to(dt)
             o = torch.empty(B * T, D, device=dev, dtype=dt)
@@ -351,10 +353,11 @@ def sweep_ops(only: str | None = None, reps: int = 10):
                   "achieved_fwd": dense / 2 / (mf / 1e3) / 1e12, "achieved_vjp": 2.5 * dense / 2 / (mb / 1e3) / 1e12,
                   "unit": "TFLOP/s (causal: half the dense count)", "bound": "tensor",
                   "frac_fwd": dense / 2 / (mf / 1e3) / 1e12 / tc_burst})
-        R, C = 8192, 4096
         es = 2 if kind == "bf16" else 4
-        name = f"layernorm_{kind}_8192x4096"
-        if want(name):
+        for R, C in ((8192, 4096), (CFG["batch"] * CFG["seq"], CFG["n_embd"])):
+            name = f"layernorm_{kind}_{R}x{C}"
+            if not want(name):
+                continue
             x = torch.randn(R, C, device=dev)
             g = torch.randn(C, device=dev).to(dt)
             y = torch.empty(R, C, device=dev, dtype=dt)
@@ -374,6 +377,7 @@ def sweep_ops(only: str | None = None, reps: int = 10):
             emit({"op": name, "fwd_ms": mf, "vjp_ms": mb, "achieved_fwd": bf / (mf / 1e3) / 1e9,
                   "achieved_vjp": bb / (mb / 1e3) / 1e9, "unit": "GB/s", "bound": "hbm", "peak": hbm,
                   "frac_fwd": bf / (mf / 1e3) / 1e9 / hbm, "frac_vjp": bb / (mb / 1e3) / 1e9 / hbm})
+        R, C = 8192, 4096
         name = f"gelu_{kind}_8192x4096"
         if want(name):
             n = R * C

@@ -8,7 +8,7 @@
 // Masked scores contribute exp(-1e10 - max) == 0, so masked keys are skipped.
 //
 // Forward, one CTA per (batch, head, 128-query tile); 192 threads:
-//   warp 0    TMA: Q tile once, K/V tiles of 128 keys (2-stage ring)
+//   warp 0    TMA: Q tile once, K/V tiles of 128 keys (one slot each)
 //   warp 1    TMEM owner + single-thread UMMA issuer:
 //             S = Q K^T (M=128, N=128, K=64) into TMEM;
 //             O_j = P V (M=128, N=64, K=128) into TMEM
@@ -81,20 +81,24 @@ __device__ __forceinline__ uint64_t mndesc(uint32_t tile, int kk, uint32_t lbo) 
 // forward
 // ---------------------------------------------------------------------------
 
-constexpr size_t kFwdSmem = 1024 + kTileBytes /*Q*/ + 2 * kTileBytes /*K*/ + 2 * kTileBytes /*V*/ +
+constexpr size_t kFwdSmem = 1024 + kTileBytes /*Q*/ + kTileBytes /*K*/ + kTileBytes /*V*/ +
                             2 * kTileBytes /*P*/ + 16 * 8 + 16;
 
-__global__ void __launch_bounds__(192, 1) attn_fwd_tc(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+// ~82 KB of shared memory and 256 TMEM columns: two CTAs per SM, so one CTA's
+// softmax overlaps the other's loads and UMMAs.
+__global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = sm;
   uint8_t* sK = sQ + kTileBytes;
-  uint8_t* sV = sK + 2 * kTileBytes;
-  uint8_t* sP = sV + 2 * kTileBytes;
+  uint8_t* sV = sK + kTileBytes;
+  uint8_t* sP = sV + kTileBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kTileBytes);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 2;
+  uint64_t* v_full = bars + 3;
+  uint64_t* v_empty = bars + 4;
   uint64_t* s_full = bars + 5;
   uint64_t* p_full = bars + 6;
   uint64_t* o_full = bars + 7;
@@ -109,14 +113,7 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc(const __grid_constant__ CU
   const int row0 = b * a.T;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-    }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
-    mbar_init(o_full, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&bars[i], i == 6 ? 4 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -132,15 +129,19 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc(const __grid_constant__ CU
   const uint32_t tS = tmem, tO = tmem + 128;
 
   if (warp == 0) {
+    // K_j is reloaded once S_{j-1} has consumed the single K slot, V_j once
+    // P_{j-1} V_{j-1} has consumed the V slot; both land during softmax.
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, kTileBytes);
       tma_load_2d(sQ, &tm, q_full, h * kHd, row0 + qt * kT);
       for (int j = 0; j < nkv; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, a.err, abort_flag)) break;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * kTileBytes);
-        tma_load_2d(sK + s * kTileBytes, &tm, &kv_full[s], a.D + h * kHd, row0 + j * kT);
-        tma_load_2d(sV + s * kTileBytes, &tm, &kv_full[s], 2 * a.D + h * kHd, row0 + j * kT);
+        const uint32_t ph = (j & 1) ^ 1;
+        if (!mbar_wait(k_empty, ph, a.err, abort_flag)) break;
+        mbar_arrive_expect_tx(k_full, kTileBytes);
+        tma_load_2d(sK, &tm, k_full, a.D + h * kHd, row0 + j * kT);
+        if (!mbar_wait(v_empty, ph, a.err, abort_flag)) break;
+        mbar_arrive_expect_tx(v_full, kTileBytes);
+        tma_load_2d(sV, &tm, v_full, 2 * a.D + h * kHd, row0 + j * kT);
       }
     }
   } else if (warp == 1) {
@@ -148,21 +149,23 @@ __global__ void __launch_bounds__(192, 1) attn_fwd_tc(const __grid_constant__ CU
       constexpr uint32_t idS = make_idesc_bf16(128, 128, false, false);
       constexpr uint32_t idO = make_idesc_bf16(128, 64, false, true);
       const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       if (mbar_wait(q_full, 0, a.err, abort_flag)) {
         for (int j = 0; j < nkv; ++j) {
-          const int s = j & 1;
-          if (!mbar_wait(&kv_full[s], (j >> 1) & 1, a.err, abort_flag)) break;
+          const uint32_t ph = j & 1;
+          if (!mbar_wait(k_full, ph, a.err, abort_flag)) break;
           tc_fence_after();
-          const uint32_t k_addr = smem_u32(sK + s * kTileBytes), v_addr = smem_u32(sV + s * kTileBytes);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) umma_f16(tS, kdesc(q_addr, kk), kdesc(k_addr, kk), idS, kk > 0);
           umma_commit(s_full);
-          if (!mbar_wait(p_full, j & 1, a.err, abort_flag)) break;
+          umma_commit(k_empty);
+          if (!mbar_wait(p_full, ph, a.err, abort_flag)) break;
+          if (!mbar_wait(v_full, ph, a.err, abort_flag)) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) umma_f16(tO, kdesc2(p_addr, kk), mndesc(v_addr, kk, 8192), idO, kk > 0);
           umma_commit(o_full);
-          umma_commit(&kv_empty[s]);
+          umma_commit(v_empty);
         }
       }
     }
@@ -443,17 +446,21 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
         tmem_wait_ld();
         uint32_t pp[16], pd[16];
 #pragma unroll
-        for (int t = 0; t < 32; t += 2) {
-          float p[2], d[2];
+        for (int t = 0; t < 32; t += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(lse2 + c * 32 + t);
+          const float4 d4 = *reinterpret_cast<const float4*>(del + c * 32 + t);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dl[4] = {d4.x, d4.y, d4.z, d4.w};
+          float p[4], d[4];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int qi = c * 32 + t + u;
-            const int q = i * kT + qi;
-            p[u] = (key <= q) ? exp2f(__uint_as_float(sv[t + u]) * sl - lse2[qi]) : 0.f;
-            d[u] = p[u] * (__uint_as_float(dv[t + u]) - del[qi]) * a.scale;
+          for (int u = 0; u < 4; ++u) {
+            const int q = i * kT + c * 32 + t + u;
+            p[u] = (key <= q) ? exp2f(__uint_as_float(sv[t + u]) * sl - lv[u]) : 0.f;
+            d[u] = p[u] * (__uint_as_float(dv[t + u]) - dl[u]) * a.scale;
           }
           pp[t >> 1] = pack_bf16x2(p[0], p[1]);
+          pp[(t >> 1) + 1] = pack_bf16x2(p[2], p[3]);
           pd[t >> 1] = pack_bf16x2(d[0], d[1]);
+          pd[(t >> 1) + 1] = pack_bf16x2(d[2], d[3]);
         }
         store_row32(pt_addr, tid, c, pp);
         store_row32(dst_addr, tid, c, pd);

@@ -38,14 +38,14 @@ struct F32Args {
   long split_stride;
 };
 
-__device__ __forceinline__ float gelu_fwd32(float x) {
-  float inner = x + 0.044715f * (x * (x * x));
-  return 0.5f * (x * (1.0f + tanhf(0.7978846f * inner)));
-}
-__device__ __forceinline__ float gelu_grad32(float x) {
-  float x2 = x * x;
-  float t = tanhf(0.7978846f * (x + 0.044715f * (x * x2)));
-  return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * 0.7978846f * (1.0f + 0.134145f * x2);
+// gelu(x) = 0.5 * (x * (1 + tanh(0.7978846 * (x + 0.044715 * (x * (x * x))))))
+// (lib/nn.shf:10-11) and its derivative by the chain rule of those primitive
+// ops, from one tanh.
+__device__ __forceinline__ void gelu_and_grad32(float x, float& g, float& d) {
+  const float x2 = x * x;
+  const float t = tanhf(0.7978846f * (x + 0.044715f * (x * x2)));
+  g = 0.5f * (x * (1.0f + t));
+  d = 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * 0.7978846f * (1.0f + 0.134145f * x2);
 }
 
 // Loads a TK x 128 panel of an operand into registers (8 values/thread).
@@ -148,11 +148,14 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(F32Args a) {
       switch (a.epi) {
         case EPI_STORE: a.out[split * a.split_stride + o] = v; break;
         case EPI_ADD: a.out[o] = a.aux[static_cast<long>(row) * a.ldaux + col] + v; break;
-        case EPI_GELU:
-          a.out[o] = v;
-          a.out2[static_cast<long>(row) * a.ldo2 + col] = gelu_fwd32(v);
+        case EPI_GELU: {
+          float g, dg;
+          gelu_and_grad32(v, g, dg);
+          a.out[o] = g;
+          a.out2[static_cast<long>(row) * a.ldo2 + col] = dg;
           break;
-        default: a.out[o] = v * gelu_grad32(a.aux[static_cast<long>(row) * a.ldaux + col]); break;
+        }
+        default: a.out[o] = v * a.aux[static_cast<long>(row) * a.ldaux + col]; break;
       }
     }
   }

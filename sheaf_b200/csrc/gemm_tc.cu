@@ -50,17 +50,23 @@ struct GemmArgs {
   int* err;
 };
 
-__device__ __forceinline__ float gelu_fwd(float x) {
-  // 0.5 * (x * (1 + tanh(0.7978846 * (x + 0.044715 * (x * (x * x))))))   (lib/nn.shf:10-11)
-  float inner = x + 0.044715f * (x * (x * x));
-  return 0.5f * (x * (1.0f + tanhf(0.7978846f * inner)));
+// Hardware tanh (PTX tanh.approx.f32, one MUFU op; relative error about
+// 2^-11, below the 2^-9 rounding of the bf16 results it feeds).
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-__device__ __forceinline__ float gelu_grad(float x) {
-  // d/dx of gelu_fwd by the chain rule of its primitive ops.
-  float x2 = x * x;
-  float t = tanhf(0.7978846f * (x + 0.044715f * (x * x2)));
-  return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * 0.7978846f * (1.0f + 0.134145f * x2);
+// gelu(x) = 0.5 * (x * (1 + tanh(0.7978846 * (x + 0.044715 * (x * (x * x))))))
+// (lib/nn.shf:10-11) and its derivative by the chain rule of those primitive
+// ops, from one tanh: the forward epilogue saves gelu'(u) for the VJP.
+__device__ __forceinline__ void gelu_and_grad(float x, float& g, float& d) {
+  const float x2 = x * x;
+  const float t = tanh_approx(0.7978846f * (x + 0.044715f * (x * x2)));
+  const float hx = 0.5f * x;
+  g = fmaf(hx, t, hx);
+  d = fmaf(0.5f, t, 0.5f) + hx * fmaf(-t, t, 1.0f) * fmaf(0.7978846f * 0.134145f, x2, 0.7978846f);
 }
 
 __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
@@ -255,7 +261,7 @@ __global__ void __launch_bounds__(192, 1)
           stage(v, &tmC, col0, store_y);
         }
       } else {
-        // 64 bf16 columns (128 B) per block: STORE, GELU (two outputs), GELU_BWD
+        // 64 bf16 columns (128 B) per block: STORE, GELU (two outputs), MUL
 #pragma unroll 1
         for (int c = 0; c < BN / 64; ++c) {
           const int col0 = nt * BN + c * 64;
@@ -273,21 +279,23 @@ __global__ void __launch_bounds__(192, 1)
             }
             stage(w, &tmC, col0, store_y);
           } else if (a.epi == EPI_GELU) {
+            // u is the bf16-rounded product, as the module's dot_general result
             uint32_t g[32];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const float u0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[2 * j])));
-              const float u1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[2 * j + 1])));
-              w[j] = pack_bf16x2(u0, u1);
-              g[j] = pack_bf16x2(gelu_fwd(u0), gelu_fwd(u1));
-              const float u2 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[2 * j])));
-              const float u3 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[2 * j + 1])));
-              w[16 + j] = pack_bf16x2(u2, u3);
-              g[16 + j] = pack_bf16x2(gelu_fwd(u2), gelu_fwd(u3));
+              float y0, y1, y2, y3, d0, d1, d2, d3;
+              gelu_and_grad(__bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[2 * j]))), y0, d0);
+              gelu_and_grad(__bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[2 * j + 1]))), y1, d1);
+              gelu_and_grad(__bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[2 * j]))), y2, d2);
+              gelu_and_grad(__bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[2 * j + 1]))), y3, d3);
+              w[j] = pack_bf16x2(y0, y1);
+              w[16 + j] = pack_bf16x2(y2, y3);
+              g[j] = pack_bf16x2(d0, d1);
+              g[16 + j] = pack_bf16x2(d2, d3);
             }
             stage(w, &tmC, col0, store_y);
             stage(g, &tmC2, col0, store_y);
-          } else {  // EPI_GELU_BWD: acc * gelu'(u), u = aux (bf16)
+          } else {  // EPI_MUL: acc * aux (bf16)
             uint32_t uw[32];
             if (row < a.M) {
               const __nv_bfloat16* up =
@@ -315,10 +323,10 @@ __global__ void __launch_bounds__(192, 1)
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              w[j] = pack_bf16x2(__uint_as_float(v0[2 * j]) * gelu_grad(bf16_bits_to_f32(uw[j] & 0xFFFFu)),
-                                 __uint_as_float(v0[2 * j + 1]) * gelu_grad(bf16_bits_to_f32(uw[j] >> 16)));
-              w[16 + j] = pack_bf16x2(__uint_as_float(v1[2 * j]) * gelu_grad(bf16_bits_to_f32(uw[16 + j] & 0xFFFFu)),
-                                      __uint_as_float(v1[2 * j + 1]) * gelu_grad(bf16_bits_to_f32(uw[16 + j] >> 16)));
+              w[j] = pack_bf16x2(__uint_as_float(v0[2 * j]) * bf16_bits_to_f32(uw[j] & 0xFFFFu),
+                                 __uint_as_float(v0[2 * j + 1]) * bf16_bits_to_f32(uw[j] >> 16));
+              w[16 + j] = pack_bf16x2(__uint_as_float(v1[2 * j]) * bf16_bits_to_f32(uw[16 + j] & 0xFFFFu),
+                                      __uint_as_float(v1[2 * j + 1]) * bf16_bits_to_f32(uw[16 + j] >> 16));
             }
             stage(w, &tmC, col0, store_y);
           }
@@ -506,7 +514,7 @@ size_t gemm_workspace_bytes(const GemmDesc& d, bool bf16) {
 int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* err) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0) return 1;
   const bool f32_epi = d.epi == EPI_ADD || (d.epi == EPI_STORE && d.out_f32);
-  if ((d.epi == EPI_ADD && !d.out_f32) || ((d.epi == EPI_GELU || d.epi == EPI_GELU_BWD) && d.out_f32)) return 1;
+  if ((d.epi == EPI_ADD && !d.out_f32) || ((d.epi == EPI_GELU || d.epi == EPI_MUL) && d.out_f32)) return 1;
   Plan p = plan_for(d);
   GemmArgs a{};
   a.M = d.M;

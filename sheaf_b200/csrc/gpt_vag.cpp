@@ -82,7 +82,7 @@ class GptVagModule : public Module {
   float* loss_f32 = nullptr;
   std::vector<float*> xs, xmid, mean1, rstd1, mean2, rstd2, lse;
   float *meanf = nullptr, *rstdf = nullptr;
-  std::vector<void*> h1, h2, qkv, att, u, gact;
+  std::vector<void*> h1, h2, qkv, att, gder, gact;  // gder = gelu'(u) saved for the VJP
   void *hf = nullptr, *logits = nullptr, *dlogits = nullptr;
   float* dres = nullptr;
   void* dres_bf = nullptr;
@@ -252,7 +252,7 @@ class GptVagModule : public Module {
       SB_TRY(dev(nd * es, &q));
       att.push_back(q);
       SB_TRY(dev(4 * nd * es, &q));
-      u.push_back(q);
+      gder.push_back(q);
       SB_TRY(dev(4 * nd * es, &q));
       gact.push_back(q);
     }
@@ -313,9 +313,9 @@ class GptVagModule : public Module {
       }
       SB_K(layernorm_fwd(xmid[l], Pp(b0 + 3), f32, h2[l], f32, mean2[l], rstd2[l], N, D, st));
       {
-        GemmDesc d = desc(h2[l], D, false, Pp(b0 + 4), D, false, N, 4 * D, D, u[l], 4 * D, f32);
+        GemmDesc d = desc(h2[l], D, false, Pp(b0 + 4), D, false, N, 4 * D, D, gact[l], 4 * D, f32);
         d.epi = EPI_GELU;
-        d.out2 = gact[l];
+        d.out2 = gder[l];
         d.ldo2 = 4 * D;
         SB_K(gemm(d, st, err));
       }
@@ -354,8 +354,8 @@ class GptVagModule : public Module {
       SB_K(gemm(desc(opnd, D, true, gact[l], 4 * D, true, D, 4 * D, N, Gp(b0 + 5), 4 * D, f32), st, err));
       {
         GemmDesc d = desc(opnd, D, false, Pp(b0 + 5), 4 * D, true, N, 4 * D, D, du, 4 * D, f32);
-        d.epi = EPI_GELU_BWD;
-        d.aux = u[l];
+        d.epi = EPI_MUL;
+        d.aux = gder[l];
         d.ldaux = 4 * D;
         d.aux_f32 = f32;
         SB_K(gemm(d, st, err));

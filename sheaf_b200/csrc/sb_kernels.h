@@ -11,8 +11,8 @@ namespace sb {
 enum EpiKind : int {
   EPI_STORE = 0,     // out = acc
   EPI_ADD = 1,       // out = acc + aux            (aux may alias out; f32 only)
-  EPI_GELU = 2,      // out = u = acc; out2 = gelu(u)  (bf16 outputs)
-  EPI_GELU_BWD = 3,  // out = acc * gelu'(aux)     (aux = pre-activation u)
+  EPI_GELU = 2,      // u = acc; out = gelu(u); out2 = gelu'(u)  (out2 feeds EPI_MUL in the VJP)
+  EPI_MUL = 3,       // out = acc * aux            (aux = gelu'(u) saved by EPI_GELU)
 };
 
 // C[M,N] = A[M,K] * B[N,K]^T with either operand stored K-major (rows of K)
