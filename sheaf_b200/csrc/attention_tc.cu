@@ -21,7 +21,7 @@
 //   P^T, dS^T = P^T * (dP^T - delta) / sqrt(Hd) written to shared memory;
 //   dV += P^T dO, dK += dS^T Q (accumulated in TMEM across query tiles);
 //   dQ_i = dS K (the dS^T tile read as an MN-major operand), added into an
-//   fp32 dQ buffer with atomics, converted to bf16 at the end.
+//   fp32 dQ buffer with TMA bulk reduce-adds, converted to bf16 at the end.
 // Q/K/V/dO tiles are 128 rows x 64 bf16 (128-byte rows), the same smem tile
 // serving as a K-major operand (rows = M/N) and an MN-major one (rows = K).
 #include <cuda.h>
@@ -54,8 +54,6 @@ struct AttnArgs {
   __nv_bfloat16* dqkv;
   int* err;
 };
-
-__device__ __forceinline__ void named_bar_softmax() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 // Writes 32 bf16 values (columns 32c .. 32c+31 of row r) into a 128-row,
 // 128-column tile stored as two 64-column K-major SW128 atoms of 16 KB.
@@ -187,32 +185,51 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
         break;
       }
       tc_fence_after();
-      const int kbase = j * kT;
-      float mx = -INFINITY;
+      // Causal mask: only the diagonal tile (j == qt) has masked keys. There,
+      // chunk c (keys 32c..32c+31 of the tile) is fully visible to this warp's
+      // rows 32*quarter.. for c < quarter, fully masked for c > quarter, and
+      // masked above the diagonal (t > lane) for c == quarter.
+      const int clast = (j == qt) ? quarter : 3;
+      float mx = -INFINITY;  // over raw scores (sl > 0)
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c <= clast; ++c) {
         uint32_t v[32];
         tmem_ld32(tS + lane_base + c * 32, v);
         tmem_wait_ld();
+        if (j == qt && c == quarter) {
 #pragma unroll
-        for (int t = 0; t < 32; ++t)
-          if (kbase + c * 32 + t <= q) mx = fmaxf(mx, __uint_as_float(v[t]) * sl);
+          for (int t = 0; t < 32; ++t)
+            if (t <= lane) mx = fmaxf(mx, __uint_as_float(v[t]));
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) mx = fmaxf(mx, __uint_as_float(v[t]));
+        }
       }
-      const float mn = fmaxf(m, mx);
-      const float corr = exp2f(m - mn);
+      const float mn = fmaxf(m, mx * sl);
+      const float corr = ex2_approx(m - mn);
       float rs = 0.f;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tS + lane_base + c * 32, v);
-        tmem_wait_ld();
         uint32_t pk[16];
+        if (c > clast) {
 #pragma unroll
-        for (int t = 0; t < 32; t += 2) {
-          const float p0 = (kbase + c * 32 + t <= q) ? exp2f(__uint_as_float(v[t]) * sl - mn) : 0.f;
-          const float p1 = (kbase + c * 32 + t + 1 <= q) ? exp2f(__uint_as_float(v[t + 1]) * sl - mn) : 0.f;
-          rs += p0 + p1;
-          pk[t >> 1] = pack_bf16x2(p0, p1);
+          for (int t = 0; t < 16; ++t) pk[t] = 0u;
+        } else {
+          uint32_t v[32];
+          tmem_ld32(tS + lane_base + c * 32, v);
+          tmem_wait_ld();
+          const bool part = (j == qt && c == quarter);
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) {
+            float p0 = ex2_approx(fmaf(__uint_as_float(v[t]), sl, -mn));
+            float p1 = ex2_approx(fmaf(__uint_as_float(v[t + 1]), sl, -mn));
+            if (part) {
+              p0 = (t <= lane) ? p0 : 0.f;
+              p1 = (t + 1 <= lane) ? p1 : 0.f;
+            }
+            rs += p0 + p1;
+            pk[t >> 1] = pack_bf16x2(p0, p1);
+          }
         }
         store_row32(p_addr, r, c, pk);
       }
@@ -298,7 +315,8 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
   uint64_t* dq_full = bars + 7;
   uint64_t* dq_empty = bars + 8;
   uint64_t* acc_full = bars + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* stats_full = bars + 10;  // [2]: the 4 softmax warps wrote lse / delta of a query tile
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -319,6 +337,8 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 4);
     mbar_init(acc_full, 1);
+    mbar_init(&stats_full[0], 4);
+    mbar_init(&stats_full[1], 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -404,63 +424,82 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl = a.scale * kLog2e;
     const uint32_t pt_addr = smem_u32(sPT), dst_addr = smem_u32(sdST);
-    bool ok = true;
-    for (int it = 0; it < nq; ++it) {
-      const int s = it & 1, i = kt + it;
-      {
-        // per query row of tile i: lse (log2 units) and delta = rowsum(dO * O)
-        const int q = i * kT + tid;
-        float dl = 0.f;
-        if (q < a.T) {
-          const long off = static_cast<long>(row0 + q) * a.D + h * kHd;
+    // Per query row of tile i into buffer s: lse (log2 units) and
+    // delta * scale, delta = rowsum(dO * O). Issued one tile ahead so that the
+    // global loads overlap the previous tile's UMMAs.
+    auto load_row_stats = [&](int i, int s) {
+      const int q = i * kT + tid;
+      float dl = 0.f;
+      if (q < a.T) {
+        const long off = static_cast<long>(row0 + q) * a.D + h * kHd;
 #pragma unroll
-          for (int u = 0; u < kHd; u += 8) {
-            const uint4 ov = *reinterpret_cast<const uint4*>(a.o + off + u);
-            const uint4 dv = *reinterpret_cast<const uint4*>(a.dout + off + u);
-            const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+        for (int u = 0; u < kHd; u += 8) {
+          const uint4 ov = *reinterpret_cast<const uint4*>(a.o + off + u);
+          const uint4 dv = *reinterpret_cast<const uint4*>(a.dout + off + u);
+          const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              dl += bf16_bits_to_f32(static_cast<uint16_t>(ow[k] & 0xFFFFu)) *
-                    bf16_bits_to_f32(static_cast<uint16_t>(dw[k] & 0xFFFFu));
-              dl += bf16_bits_to_f32(static_cast<uint16_t>(ow[k] >> 16)) *
-                    bf16_bits_to_f32(static_cast<uint16_t>(dw[k] >> 16));
-            }
+          for (int k = 0; k < 4; ++k) {
+            dl += bf16_bits_to_f32(static_cast<uint16_t>(ow[k] & 0xFFFFu)) *
+                  bf16_bits_to_f32(static_cast<uint16_t>(dw[k] & 0xFFFFu));
+            dl += bf16_bits_to_f32(static_cast<uint16_t>(ow[k] >> 16)) *
+                  bf16_bits_to_f32(static_cast<uint16_t>(dw[k] >> 16));
           }
         }
-        sLse[s * kT + tid] = (q < a.T) ? a.lse[static_cast<long>(bh) * a.T + q] * kLog2e : INFINITY;
-        sDel[s * kT + tid] = dl;
       }
-      named_bar_softmax();
-      if (!mbar_wait(st_full, it & 1, a.err, abort_flag)) {
+      sLse[s * kT + tid] = (q < a.T) ? a.lse[static_cast<long>(bh) * a.T + q] * kLog2e : INFINITY;
+      sDel[s * kT + tid] = dl * a.scale;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&stats_full[s]);
+    };
+    // Buffer s is rewritten for tile it+2 only after this thread passed
+    // st_full(it+1), which the MMA warp commits after every warp's p_full(it):
+    // no reader of the tile-it values is left by then.
+    bool ok = true;
+    load_row_stats(kt, 0);
+    for (int it = 0; it < nq; ++it) {
+      const int s = it & 1, i = kt + it;
+      if (!mbar_wait(st_full, it & 1, a.err, abort_flag) ||
+          !mbar_wait(&stats_full[s], (it >> 1) & 1, a.err, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const float* lse2 = sLse + s * kT;
       const float* del = sDel + s * kT;
+      // Causal mask (key <= query) matters only on the diagonal tile i == kt:
+      // there this warp's keys 32*quarter + lane see query chunk c (queries
+      // 32c..32c+31 of the tile) fully for c > quarter, not at all for
+      // c < quarter (P = dS = 0), and for t >= lane when c == quarter.
+      const int cfirst = (i == kt) ? quarter : 0;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld32(tST + lane_base + c * 32, sv);
-        tmem_ld32(tdPT + lane_base + c * 32, dv);
-        tmem_wait_ld();
         uint32_t pp[16], pd[16];
+        if (c < cfirst) {
 #pragma unroll
-        for (int t = 0; t < 32; t += 4) {
-          const float4 l4 = *reinterpret_cast<const float4*>(lse2 + c * 32 + t);
-          const float4 d4 = *reinterpret_cast<const float4*>(del + c * 32 + t);
-          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dl[4] = {d4.x, d4.y, d4.z, d4.w};
-          float p[4], d[4];
+          for (int t = 0; t < 16; ++t) pp[t] = pd[t] = 0u;
+        } else {
+          uint32_t sv[32], dv[32];
+          tmem_ld32(tST + lane_base + c * 32, sv);
+          tmem_ld32(tdPT + lane_base + c * 32, dv);
+          tmem_wait_ld();
+          const bool part = (i == kt && c == quarter);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int q = i * kT + c * 32 + t + u;
-            p[u] = (key <= q) ? exp2f(__uint_as_float(sv[t + u]) * sl - lv[u]) : 0.f;
-            d[u] = p[u] * (__uint_as_float(dv[t + u]) - dl[u]) * a.scale;
+          for (int t = 0; t < 32; t += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(lse2 + c * 32 + t);
+            const float4 d4 = *reinterpret_cast<const float4*>(del + c * 32 + t);
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dl[4] = {d4.x, d4.y, d4.z, d4.w};
+            float p[4], d[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              p[u] = ex2_approx(fmaf(__uint_as_float(sv[t + u]), sl, -lv[u]));
+              if (part && t + u < lane) p[u] = 0.f;
+              d[u] = p[u] * fmaf(__uint_as_float(dv[t + u]), a.scale, -dl[u]);
+            }
+            pp[t >> 1] = pack_bf16x2(p[0], p[1]);
+            pp[(t >> 1) + 1] = pack_bf16x2(p[2], p[3]);
+            pd[t >> 1] = pack_bf16x2(d[0], d[1]);
+            pd[(t >> 1) + 1] = pack_bf16x2(d[2], d[3]);
           }
-          pp[t >> 1] = pack_bf16x2(p[0], p[1]);
-          pp[(t >> 1) + 1] = pack_bf16x2(p[2], p[3]);
-          pd[t >> 1] = pack_bf16x2(d[0], d[1]);
-          pd[(t >> 1) + 1] = pack_bf16x2(d[2], d[3]);
         }
         store_row32(pt_addr, tid, c, pp);
         store_row32(dst_addr, tid, c, pd);
@@ -469,6 +508,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      if (it + 1 < nq) load_row_stats(i + 1, s ^ 1);
       // dQ tile partial: TMEM lane = query row of tile i
       if (!mbar_wait(dq_full, it & 1, a.err, abort_flag)) {
         ok = false;

@@ -349,20 +349,48 @@ done:
   }
 }
 
-// Sums split-K partial slices: out[r, c] = sum_s ws[s][r][c] (slice = stride
-// elements between splits).
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, long slice, int M, int N, void* out,
+// Sums split-K partial slices in split order: out[r, c] = sum_s ws[s][r][c]
+// (slice = elements between splits, partial rows of N floats). Four columns
+// per thread; the loads of all splits are issued ahead of the in-order adds.
+__global__ void splitk_reduce_kernel(const float4* __restrict__ ws, int splits, long slice4, int M, int nq, void* out,
                                      long ldo, int out_f32) {
-  const long total = static_cast<long>(M) * N;
+  const long total = static_cast<long>(M) * nq;
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long>(gridDim.x) * blockDim.x) {
-    float acc = 0.f;
-    for (int s = 0; s < splits; ++s) acc += ws[s * slice + i];
-    const long r = i / N, c = i % N;
-    if (out_f32)
-      static_cast<float*>(out)[r * ldo + c] = acc;
-    else
-      static_cast<__nv_bfloat16*>(out)[r * ldo + c] = __float2bfloat16_rn(acc);
+    float4 acc = ws[i];
+#pragma unroll 4
+    for (int s = 1; s < splits; ++s) {
+      const float4 v = ws[s * slice4 + i];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const long r = i / nq;
+    const long c = (i - r * nq) * 4;
+    if (out_f32) {
+      float* o = static_cast<float*>(out) + r * ldo + c;
+      o[0] = acc.x;
+      o[1] = acc.y;
+      o[2] = acc.z;
+      o[3] = acc.w;
+    } else {
+      __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + r * ldo + c;
+      const uint32_t lo = pack_bf16x2(acc.x, acc.y), hi = pack_bf16x2(acc.z, acc.w);
+      const uintptr_t al = reinterpret_cast<uintptr_t>(o);
+      if ((al & 7) == 0) {
+        *reinterpret_cast<uint2*>(o) = make_uint2(lo, hi);
+      } else if ((al & 3) == 0) {
+        reinterpret_cast<uint32_t*>(o)[0] = lo;
+        reinterpret_cast<uint32_t*>(o)[1] = hi;
+      } else {
+        uint16_t* h = reinterpret_cast<uint16_t*>(o);
+        h[0] = static_cast<uint16_t>(lo);
+        h[1] = static_cast<uint16_t>(lo >> 16);
+        h[2] = static_cast<uint16_t>(hi);
+        h[3] = static_cast<uint16_t>(hi >> 16);
+      }
+    }
   }
 }
 
@@ -473,9 +501,10 @@ Plan plan_for(const GemmDesc& d) {
   if (splits <= 0) {
     splits = 1;
     const int sms = num_sms();
-    if (d.epi == EPI_STORE && tiles * 2 <= sms && p.kb_total >= 8) splits = std::min(sms / tiles, p.kb_total / 4);
+    if (d.epi == EPI_STORE && d.N % 4 == 0 && tiles * 2 <= sms && p.kb_total >= 8)
+      splits = std::min(sms / tiles, p.kb_total / 4);
   }
-  if (d.epi != EPI_STORE) splits = 1;
+  if (d.epi != EPI_STORE || d.N % 4 != 0) splits = 1;  // partial rows of N floats must be 16-byte multiples
   splits = std::max(1, std::min(splits, p.kb_total));
   p.kb_per_split = (p.kb_total + splits - 1) / splits;
   p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
@@ -558,11 +587,12 @@ int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaS
   }
   if (rc) return rc;
   if (split) {
-    const long total = static_cast<long>(d.M) * d.N;
+    const long total = static_cast<long>(d.M) * (d.N / 4);
     const int threads = 256;
-    const int blocks = static_cast<int>(std::min<long>((total + threads - 1) / threads, 4L * num_sms()));
-    splitk_reduce_kernel<<<blocks, threads, 0, s>>>(workspace, p.splits, static_cast<long>(p.m_tiles) * kBM * d.N,
-                                                    d.M, d.N, d.out, d.ldo, d.out_f32);
+    const int blocks = static_cast<int>(std::min<long>((total + threads - 1) / threads, 8L * num_sms()));
+    splitk_reduce_kernel<<<blocks, threads, 0, s>>>(reinterpret_cast<const float4*>(workspace), p.splits,
+                                                    static_cast<long>(p.m_tiles) * kBM * d.N / 4, d.M, d.N / 4, d.out,
+                                                    d.ldo, d.out_f32);
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
   }
   return 0;

@@ -78,103 +78,113 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float4 v
 // (lane*4 + j*128). D must be a multiple of 4 and <= VPT*128.
 // ---------------------------------------------------------------------------
 
+// y = (x - mean) * rstd * gamma, rstd = 1 / sqrt(var + 1e-5); one warp per
+// row, two rows per iteration so that both rows' loads are in flight.
+template <int VPT, typename TO>
+__device__ __forceinline__ void ln_fwd_row(const float4 (&v)[VPT], int lane, int D, const void* gamma, int gamma_f32,
+                                           TO* yr, float* mean_out, float* rstd_out, int row) {
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+  const float mean = warp_sum(s) / static_cast<float>(D);
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int c = lane * 4 + j * 128;
+    if (c < D) {
+      const float a = v[j].x - mean, b = v[j].y - mean, cc = v[j].z - mean, d = v[j].w - mean;
+      q += (a * a + b * b) + (cc * cc + d * d);
+    }
+  }
+  const float var = warp_sum(q) / static_cast<float>(D);
+  const float rstd = 1.0f / sqrtf(var + 1e-5f);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int c = lane * 4 + j * 128;
+    if (c < D) {
+      const float4 g = gamma_f32 ? load4(static_cast<const float*>(gamma) + c)
+                                 : load4(static_cast<const __nv_bfloat16*>(gamma) + c);
+      store4(yr + c, make_float4(((v[j].x - mean) * rstd) * g.x, ((v[j].y - mean) * rstd) * g.y,
+                                 ((v[j].z - mean) * rstd) * g.z, ((v[j].w - mean) * rstd) * g.w));
+    }
+  }
+  if (lane == 0) {
+    mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+}
+
 template <int VPT, typename TO>
 __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x, const void* __restrict__ gamma,
                                                      int gamma_f32, TO* __restrict__ y, float* __restrict__ mean_out,
                                                      float* __restrict__ rstd_out, int rows, int D) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x & 31;
-  for (int row = blockIdx.x * warps + threadIdx.x / 32; row < rows; row += gridDim.x * warps) {
-    const float* xr = x + static_cast<long>(row) * D;
-    float4 v[VPT];
-    float s = 0.f;
+  const int stride = gridDim.x * warps;
+  for (int row = blockIdx.x * warps + threadIdx.x / 32; row < rows; row += 2 * stride) {
+    const int row2 = row + stride;
+    const bool two = row2 < rows;
+    float4 v[VPT], w[VPT];
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int c = lane * 4 + j * 128;
-      v[j] = (c < D) ? load4(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+      v[j] = (c < D) ? load4(x + static_cast<long>(row) * D + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      w[j] = (c < D && two) ? load4(x + static_cast<long>(row2) * D + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const float mean = warp_sum(s) / static_cast<float>(D);
-    float q = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int c = lane * 4 + j * 128;
-      if (c < D) {
-        const float a = v[j].x - mean, b = v[j].y - mean, cc = v[j].z - mean, d = v[j].w - mean;
-        q += (a * a + b * b) + (cc * cc + d * d);
-      }
-    }
-    const float var = warp_sum(q) / static_cast<float>(D);
-    const float sd = sqrtf(var + 1e-5f);
-    const float rstd = 1.0f / sd;
-    TO* yr = y + static_cast<long>(row) * D;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int c = lane * 4 + j * 128;
-      if (c < D) {
-        float4 g;
-        if (gamma_f32)
-          g = load4(static_cast<const float*>(gamma) + c);
-        else
-          g = load4(static_cast<const __nv_bfloat16*>(gamma) + c);
-        float4 o = make_float4(((v[j].x - mean) / sd) * g.x, ((v[j].y - mean) / sd) * g.y,
-                               ((v[j].z - mean) / sd) * g.z, ((v[j].w - mean) / sd) * g.w);
-        store4(yr + c, o);
-      }
-    }
-    if (lane == 0) {
-      mean_out[row] = mean;
-      rstd_out[row] = rstd;
-    }
+    ln_fwd_row<VPT, TO>(v, lane, D, gamma, gamma_f32, y + static_cast<long>(row) * D, mean_out, rstd_out, row);
+    if (two)
+      ln_fwd_row<VPT, TO>(w, lane, D, gamma, gamma_f32, y + static_cast<long>(row2) * D, mean_out, rstd_out, row2);
   }
 }
 
 // dx = rstd * (dxh - mean(dxh) - xhat * mean(dxh * xhat)), dxh = dy * gamma.
 // dres (f32) += dx; optional bf16 copy of the updated dres; per-block partial
 // sums of dgamma = sum_rows dy * xhat into dgamma_part[blockIdx.x][D].
+// x, dy and dres of a row are loaded together (the dres read does not wait
+// for the row reductions); gamma is re-read from L1 per row to keep the
+// register count at three resident blocks per SM.
 template <int VPT, typename TI>
-__global__ void __launch_bounds__(256) ln_bwd_kernel(const TI* __restrict__ dy, const float* __restrict__ x,
-                                                     const float* __restrict__ mean_in,
-                                                     const float* __restrict__ rstd_in, const void* __restrict__ gamma,
-                                                     int gamma_f32, float* __restrict__ dres,
-                                                     __nv_bfloat16* __restrict__ dres_bf,
-                                                     float* __restrict__ dgamma_part, int rows, int D) {
+__global__ void __launch_bounds__(256, VPT <= 3 ? 3 : (VPT <= 4 ? 2 : 1)) ln_bwd_kernel(const TI* __restrict__ dy, const float* __restrict__ x,
+                                                        const float* __restrict__ mean_in,
+                                                        const float* __restrict__ rstd_in,
+                                                        const void* __restrict__ gamma, int gamma_f32,
+                                                        float* __restrict__ dres, __nv_bfloat16* __restrict__ dres_bf,
+                                                        float* __restrict__ dgamma_part, int rows, int D) {
   extern __shared__ float sm_dg[];  // [warps][D]
   const int warps = blockDim.x / 32;
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  float4 g[VPT], dg[VPT];
+  float4 dg[VPT];
 #pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int c = lane * 4 + j * 128;
-    if (c < D)
-      g[j] = gamma_f32 ? load4(static_cast<const float*>(gamma) + c)
-                       : load4(static_cast<const __nv_bfloat16*>(gamma) + c);
-    else
-      g[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    dg[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+  for (int j = 0; j < VPT; ++j) dg[j] = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int row = blockIdx.x * warps + warp; row < rows; row += gridDim.x * warps) {
     const long off = static_cast<long>(row) * D;
     const float mean = mean_in[row], rstd = rstd_in[row];
-    float4 xh[VPT], dxh[VPT];
+    float4 xh[VPT], dxh[VPT], r[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = lane * 4 + j * 128;
+      const bool in = c < D;
+      xh[j] = in ? load4(x + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      dxh[j] = in ? load4(dy + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      r[j] = in ? load4(dres + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int c = lane * 4 + j * 128;
       if (c < D) {
-        const float4 xv = load4(x + off + c);
-        const float4 dv = load4(dy + off + c);
-        xh[j] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd, (xv.w - mean) * rstd);
-        dxh[j] = make_float4(dv.x * g[j].x, dv.y * g[j].y, dv.z * g[j].z, dv.w * g[j].w);
-        dg[j].x += dv.x * xh[j].x;
-        dg[j].y += dv.y * xh[j].y;
-        dg[j].z += dv.z * xh[j].z;
-        dg[j].w += dv.w * xh[j].w;
+        const float4 g = gamma_f32 ? load4(static_cast<const float*>(gamma) + c)
+                                   : load4(static_cast<const __nv_bfloat16*>(gamma) + c);
+        xh[j] = make_float4((xh[j].x - mean) * rstd, (xh[j].y - mean) * rstd, (xh[j].z - mean) * rstd,
+                            (xh[j].w - mean) * rstd);
+        dg[j].x += dxh[j].x * xh[j].x;
+        dg[j].y += dxh[j].y * xh[j].y;
+        dg[j].z += dxh[j].z * xh[j].z;
+        dg[j].w += dxh[j].w * xh[j].w;
+        dxh[j] = make_float4(dxh[j].x * g.x, dxh[j].y * g.y, dxh[j].z * g.z, dxh[j].w * g.w);
         s1 += (dxh[j].x + dxh[j].y) + (dxh[j].z + dxh[j].w);
         s2 += (dxh[j].x * xh[j].x + dxh[j].y * xh[j].y) + (dxh[j].z * xh[j].z + dxh[j].w * xh[j].w);
-      } else {
-        xh[j] = dxh[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
     const float c1 = warp_sum(s1) / static_cast<float>(D);
@@ -183,13 +193,12 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const TI* __restrict__ dy, 
     for (int j = 0; j < VPT; ++j) {
       const int c = lane * 4 + j * 128;
       if (c < D) {
-        float4 r = load4(dres + off + c);
-        r.x += rstd * (dxh[j].x - c1 - xh[j].x * c2);
-        r.y += rstd * (dxh[j].y - c1 - xh[j].y * c2);
-        r.z += rstd * (dxh[j].z - c1 - xh[j].z * c2);
-        r.w += rstd * (dxh[j].w - c1 - xh[j].w * c2);
-        store4(dres + off + c, r);
-        if (dres_bf) store4(dres_bf + off + c, r);
+        r[j].x += rstd * (dxh[j].x - c1 - xh[j].x * c2);
+        r[j].y += rstd * (dxh[j].y - c1 - xh[j].y * c2);
+        r[j].z += rstd * (dxh[j].z - c1 - xh[j].z * c2);
+        r[j].w += rstd * (dxh[j].w - c1 - xh[j].w * c2);
+        store4(dres + off + c, r[j]);
+        if (dres_bf) store4(dres_bf + off + c, r[j]);
       }
     }
   }
@@ -216,8 +225,10 @@ __global__ void __launch_bounds__(256) column_sum_kernel(const float* __restrict
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long c = static_cast<long>(blockIdx.x) * 32 + lane;
   float acc = 0.f;
-  if (c < D)
+  if (c < D) {
+#pragma unroll 8
     for (int b = warp; b < nparts; b += 8) acc += part[static_cast<long>(b) * D + c];
+  }
   sm[warp][lane] = acc;
   __syncthreads();
   if (warp == 0 && c < D) {
@@ -466,7 +477,7 @@ int layernorm_fwd(const float* x, const void* gamma, bool gamma_f32, void* y, bo
                   int rows, int D, cudaStream_t s) {
   if (rows <= 0 || D <= 0 || (D & 3)) return 1;
   const int warps = 8;
-  const int grid = std::min((rows + warps - 1) / warps, 8 * num_sms_cached());
+  const int grid = std::min((rows + 2 * warps - 1) / (2 * warps), 4 * num_sms_cached());
   if (y_f32)
     SB_LN_DISPATCH((D + 127) / 128, (ln_fwd_kernel<V, float><<<grid, warps * 32, 0, s>>>(
                                         x, gamma, gamma_f32, static_cast<float*>(y), mean, rstd, rows, D)));
@@ -477,7 +488,7 @@ int layernorm_fwd(const float* x, const void* gamma, bool gamma_f32, void* y, bo
 }
 
 size_t layernorm_bwd_workspace_bytes(int rows, int D) {
-  const int grid = std::min((rows + 7) / 8, 2 * num_sms_cached());
+  const int grid = std::min((rows + 7) / 8, 3 * num_sms_cached());
   return static_cast<size_t>(grid) * D * sizeof(float);
 }
 
@@ -486,7 +497,7 @@ int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean
                   int rows, int D, cudaStream_t s) {
   if (rows <= 0 || D <= 0 || (D & 3)) return 1;
   const int warps = 8;
-  const int grid = std::min((rows + warps - 1) / warps, 2 * num_sms_cached());
+  const int grid = std::min((rows + warps - 1) / warps, 3 * num_sms_cached());
   const size_t smem = static_cast<size_t>(warps) * D * sizeof(float);
   if (smem > 200 * 1024) return 1;
   if (dy_f32)

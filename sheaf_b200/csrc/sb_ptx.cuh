@@ -261,6 +261,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// 2^x as the single PTX instruction ex2.approx.ftz.f32 (subnormal results
+// flush to zero; 2^-inf = 0). Used for softmax probabilities that are rounded
+// to bf16 before they reach the tensor cores.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ int elect_one_lane() {
   uint32_t pred = 0;
   asm volatile(

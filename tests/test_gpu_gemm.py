@@ -22,6 +22,7 @@ CASES = [
     (65, 384, 2048, 1, 0, 15, 0),
     (512, 65, 384, 0, 1, 0, 15),
     (640, 96, 192, 1, 1, 0, 0),
+    (96, 66, 4096, 1, 1, 0, 2),  # one tile, long K, N not a multiple of 4: no split-K
 ]
 
 
@@ -80,20 +81,25 @@ def test_matmul_f32(case, cuda):
     assert err <= 1e-5 * scale, (err, scale)
 
 
-def test_matmul_bf16_output(cuda):
-    """bf16 output rounding (RNE) on the tcgen05 epilogue."""
+@pytest.mark.parametrize("M,N,K,ldc", [(512, 256, 256, 256), (200, 200, 4096, 200), (130, 132, 4096, 135)])
+def test_matmul_bf16_output(M, N, K, ldc, cuda):
+    """bf16 output rounding (RNE) on the tcgen05 epilogue, and after the
+    split-K reduction (long K, few tiles; odd output row stride)."""
     import torch
     import sheaf_b200 as sb
 
-    M, N, K = 512, 256, 256
     g = torch.Generator(device="cpu").manual_seed(11)
     a = torch.randn(M, K, generator=g).to(torch.bfloat16).to(cuda)
     b = torch.randn(N, K, generator=g).to(torch.bfloat16).to(cuda)
-    c = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    cbuf = torch.full((M, ldc), float("nan"), dtype=torch.bfloat16, device=cuda)
     L = sb.lib()
-    rc = L.sb_op_matmul(sb.ELEM_BF16, a.data_ptr(), K, 0, b.data_ptr(), K, 1, M, N, K, c.data_ptr(), N,
-                        sb.ELEM_BF16, None, 0, torch.cuda.current_stream().cuda_stream)
+    wsb = L.sb_op_matmul_workspace_size(sb.ELEM_BF16, 0, 1, M, N, K)
+    ws = torch.empty(max(wsb // 4, 1), dtype=torch.float32, device=cuda)
+    rc = L.sb_op_matmul(sb.ELEM_BF16, a.data_ptr(), K, 0, b.data_ptr(), K, 1, M, N, K, cbuf.data_ptr(), ldc,
+                        sb.ELEM_BF16, ws.data_ptr(), wsb, torch.cuda.current_stream().cuda_stream)
     assert rc == 0
+    torch.cuda.synchronize()
+    c = cbuf[:, :N]
     exact = a.double() @ b.double().t()
     ref = exact.to(torch.bfloat16).double()
     diff = (c.double() - ref).abs()
