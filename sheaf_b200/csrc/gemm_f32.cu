@@ -155,7 +155,8 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(F32Args a) {
           a.out2[static_cast<long>(row) * a.ldo2 + col] = dg;
           break;
         }
-        default: a.out[o] = v * a.aux[static_cast<long>(row) * a.ldaux + col]; break;
+        case EPI_ACCUM: a.out[o] += v; break;
+        default: a.out[o] = v * a.aux[static_cast<long>(row) * a.ldaux + col]; break;  // EPI_MUL
       }
     }
   }

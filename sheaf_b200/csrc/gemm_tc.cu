@@ -10,13 +10,16 @@
 // Kernel structure (one CTA per SM, persistent over output tiles):
 //   warp 0     : TMA producer (one lane), STAGES-deep smem ring
 //   warp 1     : TMEM allocator + single-thread UMMA issuer (M=128, N=BN, K=16)
-//   warps 2..5 : epilogue; warp w owns TMEM lanes 32*(w%4)..+31 (32 output
+//   warps 2..3 : idle (keep the epilogue warpgroups aligned)
+//   warps 4..11: two epilogue warpgroups; group g drains TMEM accumulator
+//                buffer g. Warp w owns TMEM lanes 32*(w%4)..+31 (32 output
 //                rows). Each 32-row x 128-byte block of the tile is converted
-//                in registers (fused epilogue), written to a 128B-swizzled
-//                4 KB staging slot and stored with a TMA bulk tensor store;
-//                two slots per warp let conversion overlap the stores.
-// Accumulators are double-buffered in TMEM (2*BN columns) so the epilogue of
-// tile i overlaps the main loop of tile i+1.
+//                in registers (fused epilogue), written to the warp's
+//                128B-swizzled 4 KB staging slot and stored with a TMA bulk
+//                tensor store.
+// Accumulators are double-buffered in TMEM (2*BN columns): the MMA warp fills
+// one buffer while the other group's epilogue drains the other, and the two
+// groups' epilogues (global aux loads, math, stores) overlap each other.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -35,8 +38,13 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr uint32_t kABytes = kBM * kBK * 2;
-constexpr uint32_t kSlotBytes = 32 * 128;          // one 32-row x 128-byte staging block
-constexpr uint32_t kStagingBytes = 4 * 2 * kSlotBytes;  // 4 epilogue warps x 2 slots
+constexpr uint32_t kSlotBytes = 32 * 128;  // one 32-row x 128-byte staging block
+
+// Staging slots per epilogue warp: two (conversion overlaps the previous
+// store) except for the 256-wide tile, whose 4-stage operand ring leaves room
+// for one.
+__host__ __device__ constexpr int staging_slots(int bn) { return bn >= 256 ? 1 : 2; }
+__host__ __device__ constexpr uint32_t staging_bytes(int bn) { return 8u * staging_slots(bn) * kSlotBytes; }
 
 struct GemmArgs {
   int M, N, K;
@@ -75,12 +83,12 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
 
 template <int BN, int STAGES>
 constexpr size_t smem_bytes_for() {
-  return 1024 /*alignment slack*/ + static_cast<size_t>(STAGES) * (kABytes + BN * kBK * 2) + kStagingBytes +
+  return 1024 /*alignment slack*/ + static_cast<size_t>(STAGES) * (kABytes + BN * kBK * 2) + staging_bytes(BN) +
          (2 * STAGES + 4) * sizeof(uint64_t) + 16;
 }
 
 template <int BN, bool A_MN, bool B_MN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(384, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, GemmArgs a) {
   constexpr uint32_t kBBytes = BN * kBK * 2;
@@ -92,7 +100,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * kABytes;
   uint8_t* sStg = sB + STAGES * kBBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sStg + kStagingBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sStg + staging_bytes(BN));
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -197,43 +205,66 @@ __global__ void __launch_bounds__(192, 1)
         umma_commit(&tfull[as]);
       }
     }
-  } else {
+  } else if (warp >= 4) {
+    // Two epilogue warpgroups: group eg drains accumulator buffer eg, i.e.
+    // this CTA's tiles local = eg, eg + 2, ...; warp w reads TMEM lanes
+    // 32*(w%4) .. +31.
     const int q = warp & 3;
-    const uint32_t stg = smem_u32(sStg) + (warp - 2) * 2 * kSlotBytes;
+    const int eg = (warp >> 2) - 1;
+    constexpr int kSlots = staging_slots(BN);
+    const uint32_t stg = smem_u32(sStg) + (warp - 4) * kSlots * kSlotBytes;
     uint32_t cc = 0;  // bulk stores issued by this warp (lane 0 commits them)
-    auto stage = [&](const uint32_t(&w)[32], const CUtensorMap* map, int x, int y) {
-      const uint32_t slot = stg + (cc & 1) * kSlotBytes;
-      if (cc >= 2) {
-        if (lane == 0) bulk_wait_read<1>();
+    // Writes the warp's 32-row x 128-byte block into a swizzled staging slot
+    // and stores it with a bulk tensor store, or, with `accumulate`, adds it
+    // into global memory with a bulk tensor reduce-add (the add runs in L2).
+    auto stage = [&](const uint32_t(&w)[32], const CUtensorMap* map, int x, int y, bool accumulate) {
+      const uint32_t slot = stg + (cc % kSlots) * kSlotBytes;
+      if (cc >= static_cast<uint32_t>(kSlots)) {
+        if (lane == 0) bulk_wait_read<kSlots - 1>();
         __syncwarp();
       }
       st_row128_sw(slot, lane, w);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-                         reinterpret_cast<uint64_t>(map)),
-                     "r"(slot), "r"(x), "r"(y)
-                     : "memory");
+        if (accumulate)
+          asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::
+                           "l"(reinterpret_cast<uint64_t>(map)),
+                       "r"(slot), "r"(x), "r"(y)
+                       : "memory");
+        else
+          asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                           reinterpret_cast<uint64_t>(map)),
+                       "r"(slot), "r"(x), "r"(y)
+                       : "memory");
         bulk_commit();
       }
       ++cc;
     };
-    int local = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+    int local = eg;
+    for (int u = blockIdx.x + eg * gridDim.x; u < units; u += 2 * gridDim.x, local += 2) {
       const int split = u % a.splits;
       const int tile = u / a.splits;
       const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
       const int as = local & 1;
       const uint32_t aph = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[as], aph, a.err, abort_flag)) break;
-      tc_fence_after();
       const int row0 = mt * kBM + q * 32;
       const int row = row0 + lane;
+      if ((a.epi == EPI_ADD || a.epi == EPI_MUL) && row < a.M) {
+        // pull this row's aux segment of the tile towards L2 while the
+        // accumulator is still being computed
+        const int esz = a.epi == EPI_ADD ? 4 : 2;
+        const char* ap = static_cast<const char*>(a.aux) + (static_cast<long>(row) * a.ldaux + nt * BN) * esz;
+        const int bytes = min(BN, a.N - nt * BN) * esz;
+        for (int off = 0; off < bytes; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(ap + off));
+      }
+      if (!mbar_wait(&tfull[as], aph, a.err, abort_flag)) break;
+      tc_fence_after();
       const int store_y = a.partial ? split * a.m_tiles * kBM + row0 : row0;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + as * BN;
       if (a.out_f32) {
-        // 32 f32 columns (128 B) per block: STORE or ADD (residual stream)
+        // 32 f32 columns (128 B) per block: STORE, ADD, or ACCUM (reduce-add
+        // into the residual stream)
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           const int col0 = nt * BN + c * 32;
@@ -258,7 +289,7 @@ __global__ void __launch_bounds__(192, 1)
                 if (col0 + j < a.N) v[j] = __float_as_uint(__uint_as_float(v[j]) + x[j]);
             }
           }
-          stage(v, &tmC, col0, store_y);
+          stage(v, &tmC, col0, store_y, a.epi == EPI_ACCUM);
         }
       } else {
         // 64 bf16 columns (128 B) per block: STORE, GELU (two outputs), MUL
@@ -277,24 +308,28 @@ __global__ void __launch_bounds__(192, 1)
               w[j] = pack_bf16x2(__uint_as_float(v0[2 * j]), __uint_as_float(v0[2 * j + 1]));
               w[16 + j] = pack_bf16x2(__uint_as_float(v1[2 * j]), __uint_as_float(v1[2 * j + 1]));
             }
-            stage(w, &tmC, col0, store_y);
+            stage(w, &tmC, col0, store_y, false);
           } else if (a.epi == EPI_GELU) {
-            // u is the bf16-rounded product, as the module's dot_general result
+            // u is the bf16-rounded product, as the module's dot_general
+            // result (rounded in pairs: the paired conversion keeps the
+            // special-function pipe free for the tanh)
             uint32_t g[32];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               float y0, y1, y2, y3, d0, d1, d2, d3;
-              gelu_and_grad(__bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[2 * j]))), y0, d0);
-              gelu_and_grad(__bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[2 * j + 1]))), y1, d1);
-              gelu_and_grad(__bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[2 * j]))), y2, d2);
-              gelu_and_grad(__bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[2 * j + 1]))), y3, d3);
+              const uint32_t r0 = pack_bf16x2(__uint_as_float(v0[2 * j]), __uint_as_float(v0[2 * j + 1]));
+              const uint32_t r1 = pack_bf16x2(__uint_as_float(v1[2 * j]), __uint_as_float(v1[2 * j + 1]));
+              gelu_and_grad(__uint_as_float(r0 << 16), y0, d0);
+              gelu_and_grad(__uint_as_float(r0 & 0xFFFF0000u), y1, d1);
+              gelu_and_grad(__uint_as_float(r1 << 16), y2, d2);
+              gelu_and_grad(__uint_as_float(r1 & 0xFFFF0000u), y3, d3);
               w[j] = pack_bf16x2(y0, y1);
               w[16 + j] = pack_bf16x2(y2, y3);
               g[j] = pack_bf16x2(d0, d1);
               g[16 + j] = pack_bf16x2(d2, d3);
             }
-            stage(w, &tmC, col0, store_y);
-            stage(g, &tmC2, col0, store_y);
+            stage(w, &tmC, col0, store_y, false);
+            stage(g, &tmC2, col0, store_y, false);
           } else {  // EPI_MUL: acc * aux (bf16)
             uint32_t uw[32];
             if (row < a.M) {
@@ -328,7 +363,7 @@ __global__ void __launch_bounds__(192, 1)
               w[16 + j] = pack_bf16x2(__uint_as_float(v1[2 * j]) * bf16_bits_to_f32(uw[16 + j] & 0xFFFFu),
                                       __uint_as_float(v1[2 * j + 1]) * bf16_bits_to_f32(uw[16 + j] >> 16));
             }
-            stage(w, &tmC, col0, store_y);
+            stage(w, &tmC, col0, store_y, false);
           }
         }
       }
@@ -461,7 +496,7 @@ int launch_tc(const GemmDesc& d, const GemmArgs& args, void* out, long ldo, long
       return 3;
     attr_set = true;
   }
-  gemm_tc_kernel<BN, A_MN, B_MN, STAGES><<<grid, 192, smem, s>>>(ta, tb, tc, tc2, args);
+  gemm_tc_kernel<BN, A_MN, B_MN, STAGES><<<grid, 384, smem, s>>>(ta, tb, tc, tc2, args);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
@@ -481,11 +516,12 @@ Plan plan_for(const GemmDesc& d) {
   Plan p;
   p.bn = d.bn;
   if (p.bn == 0) {
-    // widest tile among {256, 192, 128, 64} with the least column padding
-    // (N = 384 -> 192 x 2, N = 1152 -> 192 x 6, N = 1536 -> 256 x 6)
+    // tile width among {64, 128, 256, 192} with the least column padding,
+    // the later one on ties (N = 384 -> 192 x 2, N = 1152 -> 192 x 6,
+    // N = 1536 -> 192 x 8, N = 8192 -> 256 x 32)
     p.bn = 64;
     long best = (d.N + 63) / 64 * 64L;
-    for (int bn : {128, 192, 256}) {
+    for (int bn : {128, 256, 192}) {
       const long padded = static_cast<long>((d.N + bn - 1) / bn) * bn;
       if (padded <= best) {
         best = padded;
@@ -542,8 +578,10 @@ size_t gemm_workspace_bytes(const GemmDesc& d, bool bf16) {
 
 int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* err) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0) return 1;
-  const bool f32_epi = d.epi == EPI_ADD || (d.epi == EPI_STORE && d.out_f32);
-  if ((d.epi == EPI_ADD && !d.out_f32) || ((d.epi == EPI_GELU || d.epi == EPI_MUL) && d.out_f32)) return 1;
+  const bool f32_epi = d.epi == EPI_ADD || d.epi == EPI_ACCUM || (d.epi == EPI_STORE && d.out_f32);
+  if (((d.epi == EPI_ADD || d.epi == EPI_ACCUM) && !d.out_f32) ||
+      ((d.epi == EPI_GELU || d.epi == EPI_MUL) && d.out_f32))
+    return 1;
   Plan p = plan_for(d);
   GemmArgs a{};
   a.M = d.M;
@@ -581,8 +619,8 @@ int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaS
   switch (p.bn) {
     case 256: rc = dispatch_major<256, 4>(d, a, out, ldo, rows, grid, s); break;
     case 192: rc = dispatch_major<192, 4>(d, a, out, ldo, rows, grid, s); break;
-    case 128: rc = dispatch_major<128, 6>(d, a, out, ldo, rows, grid, s); break;
-    case 64: rc = dispatch_major<64, 8>(d, a, out, ldo, rows, grid, s); break;
+    case 128: rc = dispatch_major<128, 5>(d, a, out, ldo, rows, grid, s); break;
+    case 64: rc = dispatch_major<64, 6>(d, a, out, ldo, rows, grid, s); break;
     default: return 6;
   }
   if (rc) return rc;

@@ -5,8 +5,10 @@
 // (examples/nanogpt/train.shf:26-28, model.shf:85-113, lib/nn.shf:44-50) as a
 // fixed schedule of library kernels instead of IREE dispatches:
 //   forward : embedding gather + wpe slice; per layer LN -> QKV GEMM ->
-//             fused causal attention -> proj GEMM (+residual epilogue) -> LN ->
-//             fc GEMM (+GELU epilogue) -> fc2 GEMM (+residual epilogue);
+//             fused causal attention -> proj GEMM (+residual) -> LN ->
+//             fc GEMM (+GELU epilogue) -> fc2 GEMM (+residual); each LN also
+//             copies its input to the next residual buffer, into which the
+//             residual GEMM accumulates with bulk tensor reduce-adds;
 //             final LN -> head GEMM -> fused cross-entropy fwd+VJP
 //   backward: the `@` VJP GEMMs (dX with K-major / N-major operands, dW
 //             contracted over all tokens with split-K), GELU-VJP fused in the
@@ -300,18 +302,16 @@ class GptVagModule : public Module {
     SB_K(embedding_fwd(ids, Pp(iw), Pp(ip), f32, xs[0], N, T, V, D, st));
     for (int l = 0; l < L; ++l) {
       const int b0 = 1 + 6 * l;
-      SB_K(layernorm_fwd(xs[l], Pp(b0 + 2), f32, h1[l], f32, mean1[l], rstd1[l], N, D, st));
+      // LN1 also copies x into xmid, which the proj GEMM then accumulates into
+      SB_K(layernorm_fwd(xs[l], Pp(b0 + 2), f32, h1[l], f32, mean1[l], rstd1[l], N, D, st, xmid[l]));
       SB_K(gemm(desc(h1[l], D, false, Pp(b0 + 0), D, false, N, 3 * D, D, qkv[l], 3 * D, f32), st, err));
       SB_K(attention_fwd(qkv[l], f32, att[l], lse[l], ash, st));
       {
         GemmDesc d = desc(att[l], D, false, Pp(b0 + 1), D, false, N, D, D, xmid[l], D, true);
-        d.epi = EPI_ADD;
-        d.aux = xs[l];
-        d.ldaux = D;
-        d.aux_f32 = true;
+        d.epi = EPI_ACCUM;  // xmid = x + att @ Wproj^T
         SB_K(gemm(d, st, err));
       }
-      SB_K(layernorm_fwd(xmid[l], Pp(b0 + 3), f32, h2[l], f32, mean2[l], rstd2[l], N, D, st));
+      SB_K(layernorm_fwd(xmid[l], Pp(b0 + 3), f32, h2[l], f32, mean2[l], rstd2[l], N, D, st, xs[l + 1]));
       {
         GemmDesc d = desc(h2[l], D, false, Pp(b0 + 4), D, false, N, 4 * D, D, gact[l], 4 * D, f32);
         d.epi = EPI_GELU;
@@ -321,10 +321,7 @@ class GptVagModule : public Module {
       }
       {
         GemmDesc d = desc(gact[l], 4 * D, false, Pp(b0 + 5), 4 * D, false, N, D, 4 * D, xs[l + 1], D, true);
-        d.epi = EPI_ADD;
-        d.aux = xmid[l];
-        d.ldaux = D;
-        d.aux_f32 = true;
+        d.epi = EPI_ACCUM;  // x' = xmid + gelu(...) @ Wfc2^T
         SB_K(gemm(d, st, err));
       }
     }

@@ -82,7 +82,14 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float4 v
 // row, two rows per iteration so that both rows' loads are in flight.
 template <int VPT, typename TO>
 __device__ __forceinline__ void ln_fwd_row(const float4 (&v)[VPT], int lane, int D, const void* gamma, int gamma_f32,
-                                           TO* yr, float* mean_out, float* rstd_out, int row) {
+                                           TO* yr, float* mean_out, float* rstd_out, int row, float* xc) {
+  if (xc) {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = lane * 4 + j * 128;
+      if (c < D) store4(xc + c, v[j]);
+    }
+  }
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
@@ -117,7 +124,8 @@ __device__ __forceinline__ void ln_fwd_row(const float4 (&v)[VPT], int lane, int
 template <int VPT, typename TO>
 __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x, const void* __restrict__ gamma,
                                                      int gamma_f32, TO* __restrict__ y, float* __restrict__ mean_out,
-                                                     float* __restrict__ rstd_out, int rows, int D) {
+                                                     float* __restrict__ rstd_out, int rows, int D,
+                                                     float* __restrict__ x_copy) {
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x & 31;
   const int stride = gridDim.x * warps;
@@ -131,9 +139,11 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
       v[j] = (c < D) ? load4(x + static_cast<long>(row) * D + c) : make_float4(0.f, 0.f, 0.f, 0.f);
       w[j] = (c < D && two) ? load4(x + static_cast<long>(row2) * D + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    ln_fwd_row<VPT, TO>(v, lane, D, gamma, gamma_f32, y + static_cast<long>(row) * D, mean_out, rstd_out, row);
+    ln_fwd_row<VPT, TO>(v, lane, D, gamma, gamma_f32, y + static_cast<long>(row) * D, mean_out, rstd_out, row,
+                        x_copy ? x_copy + static_cast<long>(row) * D : nullptr);
     if (two)
-      ln_fwd_row<VPT, TO>(w, lane, D, gamma, gamma_f32, y + static_cast<long>(row2) * D, mean_out, rstd_out, row2);
+      ln_fwd_row<VPT, TO>(w, lane, D, gamma, gamma_f32, y + static_cast<long>(row2) * D, mean_out, rstd_out, row2,
+                          x_copy ? x_copy + static_cast<long>(row2) * D : nullptr);
   }
 }
 
@@ -474,16 +484,16 @@ int num_sms_cached() {
   } while (0)
 
 int layernorm_fwd(const float* x, const void* gamma, bool gamma_f32, void* y, bool y_f32, float* mean, float* rstd,
-                  int rows, int D, cudaStream_t s) {
+                  int rows, int D, cudaStream_t s, float* x_copy) {
   if (rows <= 0 || D <= 0 || (D & 3)) return 1;
   const int warps = 8;
   const int grid = std::min((rows + 2 * warps - 1) / (2 * warps), 4 * num_sms_cached());
   if (y_f32)
     SB_LN_DISPATCH((D + 127) / 128, (ln_fwd_kernel<V, float><<<grid, warps * 32, 0, s>>>(
-                                        x, gamma, gamma_f32, static_cast<float*>(y), mean, rstd, rows, D)));
+                                        x, gamma, gamma_f32, static_cast<float*>(y), mean, rstd, rows, D, x_copy)));
   else
     SB_LN_DISPATCH((D + 127) / 128, (ln_fwd_kernel<V, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
-                                        x, gamma, gamma_f32, static_cast<__nv_bfloat16*>(y), mean, rstd, rows, D)));
+                                        x, gamma, gamma_f32, static_cast<__nv_bfloat16*>(y), mean, rstd, rows, D, x_copy)));
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 

@@ -17,8 +17,10 @@ int num_sms_cached();
 int* device_error_word();
 
 // y = (x - mean) / sqrt(var + 1e-5) * gamma over the last dim (rows x D, f32 in).
+// x_copy (optional, f32 [rows, D]) receives a copy of x: the base that a
+// following residual GEMM accumulates into (EPI_ACCUM).
 int layernorm_fwd(const float* x, const void* gamma, bool gamma_f32, void* y, bool y_f32, float* mean, float* rstd,
-                  int rows, int D, cudaStream_t s);
+                  int rows, int D, cudaStream_t s, float* x_copy = nullptr);
 // dres += LN-VJP(dy); dres_bf (optional) = bf16(dres); dgamma = sum_rows dy * xhat.
 size_t layernorm_bwd_workspace_bytes(int rows, int D);
 int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean, const float* rstd, const void* gamma,
