@@ -41,10 +41,12 @@ constexpr uint32_t kABytes = kBM * kBK * 2;
 constexpr uint32_t kSlotBytes = 32 * 128;  // one 32-row x 128-byte staging block
 
 // Staging slots per epilogue warp: two (conversion overlaps the previous
-// store) except for the 256-wide tile, whose 4-stage operand ring leaves room
-// for one.
-__host__ __device__ constexpr int staging_slots(int bn) { return bn >= 256 ? 1 : 2; }
-__host__ __device__ constexpr uint32_t staging_bytes(int bn) { return 8u * staging_slots(bn) * kSlotBytes; }
+// store) except for the single-CTA 256-wide tile, whose 4-stage operand ring
+// leaves room for one.
+__host__ __device__ constexpr int staging_slots(int bn, bool pair) { return (bn >= 256 && !pair) ? 1 : 2; }
+__host__ __device__ constexpr uint32_t staging_bytes(int bn, bool pair) {
+  return 8u * staging_slots(bn, pair) * kSlotBytes;
+}
 
 struct GemmArgs {
   int M, N, K;
@@ -81,26 +83,39 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
   return (2 * bn <= 32) ? 32 : (2 * bn <= 64) ? 64 : (2 * bn <= 128) ? 128 : (2 * bn <= 256) ? 256 : 512;
 }
 
-template <int BN, int STAGES>
+// Shared memory per CTA: STAGES x (A tile + this CTA's B rows), staging,
+// barriers. A CTA of a pair (PAIR) holds half of the B tile's BN rows.
+template <int BN, int STAGES, bool PAIR>
 constexpr size_t smem_bytes_for() {
-  return 1024 /*alignment slack*/ + static_cast<size_t>(STAGES) * (kABytes + BN * kBK * 2) + staging_bytes(BN) +
-         (2 * STAGES + 4) * sizeof(uint64_t) + 16;
+  return 1024 /*alignment slack*/ + static_cast<size_t>(STAGES) * (kABytes + (PAIR ? BN / 2 : BN) * kBK * 2) +
+         staging_bytes(BN, PAIR) + (2 * STAGES + 4) * sizeof(uint64_t) + 16;
 }
 
-template <int BN, bool A_MN, bool B_MN, int STAGES>
+// PAIR: launched as clusters of two CTAs on two SMs that compute a 256 x BN
+// tile with tcgen05.mma.cta_group::2 (M = 256). CTA rank r loads A rows
+// 256*mt + 128r .. +127 and B rows BN*nt + (BN/2)r .. +BN/2-1 into its own
+// shared memory, the loads of both completing on rank 0's `full` barrier;
+// rank 0 issues the MMAs, whose completion is signalled to the `empty` and
+// `tfull` barriers of both CTAs; each CTA's epilogue drains the 128
+// accumulator rows in its own TMEM and arrives on rank 0's `tempty`. Halving
+// the B bytes per SM leaves room for deeper operand pipelines.
+template <int BN, bool A_MN, bool B_MN, int STAGES, bool PAIR>
 __global__ void __launch_bounds__(384, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2, GemmArgs a) {
-  constexpr uint32_t kBBytes = BN * kBK * 2;
+  constexpr int BH = PAIR ? BN / 2 : BN;  // B rows (N) loaded by this CTA
+  constexpr uint32_t kBBytes = BH * kBK * 2;
   constexpr uint32_t kTmemCols = tmem_cols_for(BN);
+  constexpr int kRowsPerTile = PAIR ? 2 * kBM : kBM;
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "tile width must be 64, 128, 192 or 256");
+  static_assert(!PAIR || (BH % 64 == 0), "pair tiles split B into 64-row multiples");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * kABytes;
   uint8_t* sStg = sB + STAGES * kBBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sStg + staging_bytes(BN));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sStg + staging_bytes(BN, PAIR));
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -109,6 +124,9 @@ __global__ void __launch_bounds__(384, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int cta0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);  // work-unit stride base
+  const int ncta = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -117,7 +135,7 @@ __global__ void __launch_bounds__(384, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], 4);
+      mbar_init(&tempty[s], PAIR ? 8 : 4);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -129,11 +147,19 @@ __global__ void __launch_bounds__(384, 1)
     tma_prefetch_desc(&tmC2);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -142,41 +168,67 @@ __global__ void __launch_bounds__(384, 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      // with PAIR, both CTAs' loads complete on rank 0's full[s], which rank
+      // 0 arms with the bytes of both halves
+      const uint32_t full0 = PAIR ? mapa_shared(smem_u32(full), 0) : smem_u32(full);
       uint32_t it = 0;
-      for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      for (int u = cta0; u < units; u += ncta) {
         const int split = u % a.splits;
         const int tile = u / a.splits;
         const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
+        const int arow = mt * kRowsPerTile + static_cast<int>(rank) * kBM;
+        const int brow = nt * BN + static_cast<int>(rank) * BH;
         const int kb0 = split * a.kb_per_split;
         const int kb1 = min(a.kb_total, kb0 + a.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, a.err, abort_flag)) goto done;
-          mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
           uint8_t* da = sA + s * kABytes;
           uint8_t* db = sB + s * kBBytes;
-          if (!A_MN) {
-            tma_load_2d(da, &tmA, &full[s], kb * kBK, mt * kBM);
-          } else {
-            tma_load_2d(da, &tmA, &full[s], mt * kBM, kb * kBK);
-            tma_load_2d(da + 8192, &tmA, &full[s], mt * kBM + 64, kb * kBK);
-          }
-          if (!B_MN) {
-            tma_load_2d(db, &tmB, &full[s], kb * kBK, nt * BN);
-          } else {
+          if constexpr (PAIR) {
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (kABytes + kBBytes));
+            const uint32_t fb = full0 + s * 8;
+            if (!A_MN) {
+              tma_load_2d_pair(da, &tmA, fb, kb * kBK, arow);
+            } else {
+              tma_load_2d_pair(da, &tmA, fb, arow, kb * kBK);
+              tma_load_2d_pair(da + 8192, &tmA, fb, arow + 64, kb * kBK);
+            }
+            if (!B_MN) {
+              tma_load_2d_pair(db, &tmB, fb, kb * kBK, brow);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(db + j * 8192, &tmB, &full[s], nt * BN + j * 64, kb * kBK);
+              for (int j = 0; j < BH / 64; ++j) tma_load_2d_pair(db + j * 8192, &tmB, fb, brow + j * 64, kb * kBK);
+            }
+          } else {
+            mbar_arrive_expect_tx(&full[s], kABytes + kBBytes);
+            if (!A_MN) {
+              tma_load_2d(da, &tmA, &full[s], kb * kBK, arow);
+            } else {
+              tma_load_2d(da, &tmA, &full[s], arow, kb * kBK);
+              tma_load_2d(da + 8192, &tmA, &full[s], arow + 64, kb * kBK);
+            }
+            if (!B_MN) {
+              tma_load_2d(db, &tmB, &full[s], kb * kBK, brow);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BH / 64; ++j) tma_load_2d(db + j * 8192, &tmB, &full[s], brow + j * 64, kb * kBK);
+            }
           }
         }
       }
+      // wait for the final release of every stage, so that no UMMA commit
+      // can still arrive on this CTA's barriers after it exits
+      for (int i = 0; i < STAGES; ++i, ++it)
+        if (!mbar_wait(&empty[it % STAGES], ((it / STAGES) & 1) ^ 1, a.err, abort_flag)) break;
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(kRowsPerTile, BN, A_MN, B_MN);
       uint32_t it = 0;
       int local = 0;
-      for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      for (int u = cta0; u < units; u += ncta, ++local) {
         const int split = u % a.splits;
         const int kb0 = split * a.kb_per_split;
         const int kb1 = min(a.kb_total, kb0 + a.kb_per_split);
@@ -198,11 +250,26 @@ __global__ void __launch_bounds__(384, 1)
                                      : make_sw128_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? make_sw128_desc(b_addr + kk * 2048, 8192, 1024)
                                      : make_sw128_desc(b_addr + kk * 32, 16, 1024);
-            umma_f16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            if constexpr (PAIR)
+              umma_f16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            else
+              umma_f16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(&empty[s]);
+          if constexpr (PAIR)
+            umma_commit_pair(&empty[s]);
+          else
+            umma_commit(&empty[s]);
         }
-        umma_commit(&tfull[as]);
+        if constexpr (PAIR)
+          umma_commit_pair(&tfull[as]);
+        else
+          umma_commit(&tfull[as]);
+      }
+      if constexpr (PAIR) {
+        // the peer's epilogue arrives remotely on tempty: wait for the
+        // releases of the last two accumulator buffers before leaving
+        for (int i = 0; i < 2; ++i, ++local)
+          if (!mbar_wait(&tempty[local & 1], ((local >> 1) & 1) ^ 1, a.err, abort_flag)) break;
       }
     }
   } else if (warp >= 4) {
@@ -211,7 +278,7 @@ __global__ void __launch_bounds__(384, 1)
     // 32*(w%4) .. +31.
     const int q = warp & 3;
     const int eg = (warp >> 2) - 1;
-    constexpr int kSlots = staging_slots(BN);
+    constexpr int kSlots = staging_slots(BN, PAIR);
     const uint32_t stg = smem_u32(sStg) + (warp - 4) * kSlots * kSlotBytes;
     uint32_t cc = 0;  // bulk stores issued by this warp (lane 0 commits them)
     // Writes the warp's 32-row x 128-byte block into a swizzled staging slot
@@ -242,13 +309,14 @@ __global__ void __launch_bounds__(384, 1)
       ++cc;
     };
     int local = eg;
-    for (int u = blockIdx.x + eg * gridDim.x; u < units; u += 2 * gridDim.x, local += 2) {
+    const uint32_t tempty0 = PAIR ? mapa_shared(smem_u32(tempty), 0) : smem_u32(tempty);
+    for (int u = cta0 + eg * ncta; u < units; u += 2 * ncta, local += 2) {
       const int split = u % a.splits;
       const int tile = u / a.splits;
       const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
       const int as = local & 1;
       const uint32_t aph = (local >> 1) & 1;
-      const int row0 = mt * kBM + q * 32;
+      const int row0 = mt * kRowsPerTile + static_cast<int>(rank) * kBM + q * 32;
       const int row = row0 + lane;
       if ((a.epi == EPI_ADD || a.epi == EPI_MUL) && row < a.M) {
         // pull this row's aux segment of the tile towards L2 while the
@@ -260,7 +328,7 @@ __global__ void __launch_bounds__(384, 1)
       }
       if (!mbar_wait(&tfull[as], aph, a.err, abort_flag)) break;
       tc_fence_after();
-      const int store_y = a.partial ? split * a.m_tiles * kBM + row0 : row0;
+      const int store_y = a.partial ? split * a.m_tiles * kRowsPerTile + row0 : row0;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + as * BN;
       if (a.out_f32) {
         // 32 f32 columns (128 B) per block: STORE, ADD, or ACCUM (reduce-add
@@ -369,18 +437,34 @@ __global__ void __launch_bounds__(384, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[as]);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(tempty0 + as * 8);  // rank 0's tempty[as]
+        else
+          mbar_arrive(&tempty[as]);
+      }
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
   }
 
 done:
+  __syncwarp();
   tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+  if constexpr (PAIR) {
+    // neither CTA frees TMEM or leaves while the pair's MMAs, commits or
+    // remote arrivals may still touch it
+    cluster_sync();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    }
+  } else {
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem_base, kTmemCols);
+    }
   }
 }
 
@@ -463,7 +547,7 @@ bool make_map_bf16(CUtensorMap* map, const void* base, long rows, long cols, lon
   return make_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols, ld, box_cols, box_rows);
 }
 
-template <int BN, bool A_MN, bool B_MN, int STAGES>
+template <int BN, bool A_MN, bool B_MN, int STAGES, bool PAIR>
 int launch_tc(const GemmDesc& d, const GemmArgs& args, void* out, long ldo, long out_rows, int grid, cudaStream_t s) {
   alignas(64) CUtensorMap ta, tb, tc, tc2;
   bool ok;
@@ -473,7 +557,7 @@ int launch_tc(const GemmDesc& d, const GemmArgs& args, void* out, long ldo, long
     ok = make_map_bf16(&ta, d.A, d.K, d.M, d.lda, 64, kBK);
   if (!ok) return 2;
   if (!B_MN)
-    ok = make_map_bf16(&tb, d.B, d.N, d.K, d.ldb, kBK, BN);
+    ok = make_map_bf16(&tb, d.B, d.N, d.K, d.ldb, kBK, PAIR ? BN / 2 : BN);
   else
     ok = make_map_bf16(&tb, d.B, d.K, d.N, d.ldb, 64, kBK);
   if (!ok) return 2;
@@ -487,41 +571,61 @@ int launch_tc(const GemmDesc& d, const GemmArgs& args, void* out, long ldo, long
   } else {
     tc2 = tc;
   }
-  constexpr size_t smem = smem_bytes_for<BN, STAGES>();
+  constexpr size_t smem = smem_bytes_for<BN, STAGES, PAIR>();
   static_assert(smem <= 232448, "shared memory budget");
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, STAGES, PAIR>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel<BN, A_MN, B_MN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+        cudaSuccess)
       return 3;
     attr_set = true;
   }
-  gemm_tc_kernel<BN, A_MN, B_MN, STAGES><<<grid, 384, smem, s>>>(ta, tb, tc, tc2, args);
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(384);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, tc2, args) != cudaSuccess) return 4;
+  } else {
+    kern<<<grid, 384, smem, s>>>(ta, tb, tc, tc2, args);
+  }
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR>
 int dispatch_major(const GemmDesc& d, const GemmArgs& a, void* out, long ldo, long rows, int grid, cudaStream_t s) {
-  if (!d.a_mn && !d.b_mn) return launch_tc<BN, false, false, STAGES>(d, a, out, ldo, rows, grid, s);
-  if (!d.a_mn && d.b_mn) return launch_tc<BN, false, true, STAGES>(d, a, out, ldo, rows, grid, s);
-  if (d.a_mn && d.b_mn) return launch_tc<BN, true, true, STAGES>(d, a, out, ldo, rows, grid, s);
-  return launch_tc<BN, true, false, STAGES>(d, a, out, ldo, rows, grid, s);
+  if (!d.a_mn && !d.b_mn) return launch_tc<BN, false, false, STAGES, PAIR>(d, a, out, ldo, rows, grid, s);
+  if (!d.a_mn && d.b_mn) return launch_tc<BN, false, true, STAGES, PAIR>(d, a, out, ldo, rows, grid, s);
+  if (d.a_mn && d.b_mn) return launch_tc<BN, true, true, STAGES, PAIR>(d, a, out, ldo, rows, grid, s);
+  return launch_tc<BN, true, false, STAGES, PAIR>(d, a, out, ldo, rows, grid, s);
 }
 
 struct Plan {
   int bn, m_tiles, n_tiles, kb_total, splits, kb_per_split;
+  bool pair;          // 256-row tiles on CTA pairs (tcgen05 cta_group::2)
+  int rows_per_tile;  // 128, or 256 for pair tiles
 };
 
 Plan plan_for(const GemmDesc& d) {
   Plan p;
   p.bn = d.bn;
   if (p.bn == 0) {
-    // tile width among {64, 128, 256, 192} with the least column padding,
-    // the later one on ties (N = 384 -> 192 x 2, N = 1152 -> 192 x 6,
-    // N = 1536 -> 192 x 8, N = 8192 -> 256 x 32)
+    // tile width among {64, 128, 192, 256} with the least column padding,
+    // the wider one on ties: a 128 x N x 16 UMMA costs about the same for
+    // every N <= 256, so full-width tiles do the most work per instruction
+    // (N = 384 -> 192 x 2, N = 1152 -> 192 x 6, N = 1536 -> 256 x 6)
     p.bn = 64;
     long best = (d.N + 63) / 64 * 64L;
-    for (int bn : {128, 256, 192}) {
+    for (int bn : {128, 192, 256}) {
       const long padded = static_cast<long>((d.N + bn - 1) / bn) * bn;
       if (padded <= best) {
         best = padded;
@@ -529,16 +633,20 @@ Plan plan_for(const GemmDesc& d) {
       }
     }
   }
-  p.m_tiles = (d.M + kBM - 1) / kBM;
+  // 256-row tiles on CTA pairs whenever the B tile splits into 64-row halves
+  // and there are at least 256 rows
+  p.pair = (p.bn == 256 || p.bn == 128) && d.M >= 2 * kBM && d.pair != 0;
+  p.rows_per_tile = p.pair ? 2 * kBM : kBM;
+  p.m_tiles = (d.M + p.rows_per_tile - 1) / p.rows_per_tile;
   p.n_tiles = (d.N + p.bn - 1) / p.bn;
   p.kb_total = (d.K + kBK - 1) / kBK;
   const int tiles = p.m_tiles * p.n_tiles;
   int splits = d.splits;
   if (splits <= 0) {
     splits = 1;
-    const int sms = num_sms();
-    if (d.epi == EPI_STORE && d.N % 4 == 0 && tiles * 2 <= sms && p.kb_total >= 8)
-      splits = std::min(sms / tiles, p.kb_total / 4);
+    const int slots = p.pair ? num_sms() / 2 : num_sms();  // tiles in flight at once
+    if (d.epi == EPI_STORE && d.N % 4 == 0 && tiles * 2 <= slots && p.kb_total >= 8)
+      splits = std::min(slots / tiles, p.kb_total / 4);
   }
   if (d.epi != EPI_STORE || d.N % 4 != 0) splits = 1;  // partial rows of N floats must be 16-byte multiples
   splits = std::max(1, std::min(splits, p.kb_total));
@@ -573,7 +681,7 @@ size_t gemm_workspace_bytes(const GemmDesc& d, bool bf16) {
   if (!bf16) return gemm_f32_workspace_bytes(d);
   Plan p = plan_for(d);
   if (p.splits <= 1) return 0;
-  return static_cast<size_t>(p.splits) * p.m_tiles * kBM * d.N * sizeof(float);
+  return static_cast<size_t>(p.splits) * p.m_tiles * p.rows_per_tile * d.N * sizeof(float);
 }
 
 int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* err) {
@@ -600,11 +708,11 @@ int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaS
   void* out = d.out;
   long ldo = d.ldo, rows = d.M;
   if (split) {
-    const size_t need = static_cast<size_t>(p.splits) * p.m_tiles * kBM * d.N * sizeof(float);
+    const size_t need = static_cast<size_t>(p.splits) * p.m_tiles * p.rows_per_tile * d.N * sizeof(float);
     if (!workspace || workspace_bytes < need) return 5;
     out = workspace;
     ldo = d.N;
-    rows = static_cast<long>(p.splits) * p.m_tiles * kBM;
+    rows = static_cast<long>(p.splits) * p.m_tiles * p.rows_per_tile;
     a.out_f32 = 1;
     a.partial = 1;
   } else {
@@ -614,13 +722,19 @@ int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaS
   if (d.aux && (((reinterpret_cast<uintptr_t>(d.aux) & 15) != 0) || ((d.ldaux * (d.aux_f32 ? 4 : 2)) & 15) != 0))
     return 2;
   const int units = p.m_tiles * p.n_tiles * p.splits;
-  const int grid = std::min(units, num_sms());
+  const int grid = p.pair ? 2 * std::min(units, num_sms() / 2) : std::min(units, num_sms());
   int rc;
   switch (p.bn) {
-    case 256: rc = dispatch_major<256, 4>(d, a, out, ldo, rows, grid, s); break;
-    case 192: rc = dispatch_major<192, 4>(d, a, out, ldo, rows, grid, s); break;
-    case 128: rc = dispatch_major<128, 5>(d, a, out, ldo, rows, grid, s); break;
-    case 64: rc = dispatch_major<64, 6>(d, a, out, ldo, rows, grid, s); break;
+    case 256:
+      rc = p.pair ? dispatch_major<256, 5, true>(d, a, out, ldo, rows, grid, s)
+                  : dispatch_major<256, 4, false>(d, a, out, ldo, rows, grid, s);
+      break;
+    case 192: rc = dispatch_major<192, 4, false>(d, a, out, ldo, rows, grid, s); break;
+    case 128:
+      rc = p.pair ? dispatch_major<128, 6, true>(d, a, out, ldo, rows, grid, s)
+                  : dispatch_major<128, 5, false>(d, a, out, ldo, rows, grid, s);
+      break;
+    case 64: rc = dispatch_major<64, 6, false>(d, a, out, ldo, rows, grid, s); break;
     default: return 6;
   }
   if (rc) return rc;
@@ -629,7 +743,8 @@ int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaS
     const int threads = 256;
     const int blocks = static_cast<int>(std::min<long>((total + threads - 1) / threads, 8L * num_sms()));
     splitk_reduce_kernel<<<blocks, threads, 0, s>>>(reinterpret_cast<const float4*>(workspace), p.splits,
-                                                    static_cast<long>(p.m_tiles) * kBM * d.N / 4, d.M, d.N / 4, d.out,
+                                                    static_cast<long>(p.m_tiles) * p.rows_per_tile * d.N / 4, d.M,
+                                                    d.N / 4, d.out,
                                                     d.ldo, d.out_f32);
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
   }

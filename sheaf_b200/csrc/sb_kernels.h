@@ -37,6 +37,7 @@ struct GemmDesc {
   long ldo2 = 0;
   int splits = 0;  // 0 = choose; 1 = no split-K (split-K only with EPI_STORE)
   int bn = 0;      // 0 = choose tile width
+  int pair = -1;   // 256-row tiles on CTA pairs: -1 = when the tile allows, 0 = never
 };
 
 // bf16 operands on tcgen05 tensor cores (fp32 accumulation in TMEM).
