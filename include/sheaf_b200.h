@@ -140,6 +140,23 @@ typedef struct sb_gpt_config {
 } sb_gpt_config;
 SB_API sb_status sb_module_create_gpt_vag(sb_session* session, const char* module_name, const sb_gpt_config* config);
 
+/* Registers the fused nanoGPT train-step module: the value_and_grad graph
+ * followed by clip-by-global-norm(g, max_norm) and adamw-step(params, g, m, v,
+ * t, lr, b1, b2, eps, weight_decay) (examples/nanogpt/train.shf:26-33,
+ * lib/optim.shf:19-32,42-51), executed as one CUDA graph. train.shf's
+ * constants are b1 0.9, b2 0.95, eps 1e-8, weight_decay 0.1, max_norm 1.0.
+ * Function "train_step": inputs are the state pytree in sorted-key order --
+ * loss [] (ignored), the m leaves, the parameter leaves, t [] f32, the v
+ * leaves -- then x ids, y ids [batch, seq] (f32) and lr [] f32; m and v have
+ * the parameters' element type. Outputs are the updated state in the same
+ * order: loss, m', params', t + 1, v'. Function "value_and_grad" is also
+ * available, as for sb_module_create_gpt_vag. */
+typedef struct sb_adamw_config {
+  float b1, b2, eps, weight_decay, max_norm; /* max_norm <= 0: no clipping */
+} sb_adamw_config;
+SB_API sb_status sb_module_create_gpt_train(sb_session* session, const char* module_name,
+                                            const sb_gpt_config* config, const sb_adamw_config* adamw);
+
 /* ---- invocation (replaces iree_runtime_session_call_by_name,
  *      iree_session.rs:576-583) ----
  * `qualified_name` is "<module>.<function>" (iree_dispatch.rs:95-104,172).

@@ -130,6 +130,28 @@ SB_API int sb_op_attention_bwd(uint32_t elem, const void* qkv, const void* o, co
                                void* dqkv, void* workspace, size_t workspace_bytes, int32_t b, int32_t t, int32_t h,
                                int32_t hd, void* stream);
 
+/* Optimizer step of nanoGPT's train-step (examples/nanogpt/train.shf:29-32):
+ * clip-by-global-norm(g, max_norm) then adamw-step(params, g, m, v, t, lr, b1,
+ * b2, eps, wd) as sheaf/lib/optim.shf:19-32,42-51 define them, over n_leaves
+ * tensors of element type `elem` (f32 or bf16) at once. The pointer arrays
+ * are host arrays of device pointers; counts[i] is leaf i's element count.
+ * t and lr are device f32 scalars; t_out receives t + 1. params_out / m_out /
+ * v_out may alias params / m / v. max_norm <= 0 disables clipping; norm_out
+ * (device f32, optional) receives the global norm of the unclipped gradients.
+ * Replaces the optimizer part of the compiled train-step module (IREE
+ * dispatches behind iree_runtime_session_call_by_name,
+ * sheaf/src/runtime/iree_session.rs:576-583). */
+SB_API size_t sb_op_adamw_workspace_size(const int64_t* counts, int32_t n_leaves);
+SB_API int sb_op_adamw_step(uint32_t elem, int32_t n_leaves, const int64_t* counts, const void* const* grads,
+                            const void* const* params, const void* const* m, const void* const* v,
+                            void* const* params_out, void* const* m_out, void* const* v_out, const void* t,
+                            void* t_out, const void* lr, float b1, float b2, float eps, float wd, float max_norm,
+                            void* norm_out, void* workspace, size_t workspace_bytes, void* stream);
+/* Global norm sqrt(sum_i sum(g_i^2)) of n_leaves gradient tensors
+ * (sheaf/lib/optim.shf:42-45), f32 accumulation, written to norm_out. */
+SB_API int sb_op_global_norm(uint32_t elem, int32_t n_leaves, const int64_t* counts, const void* const* grads,
+                             void* norm_out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Reads and clears the device error word that bounded waits inside the
  * kernels set (0 = no error, 1 = a barrier wait timed out). Synchronizes
  * the device. */

@@ -25,6 +25,12 @@ class GptConfig(C.Structure):
                 ("vocab_size", C.c_int32), ("batch", C.c_int32), ("seq", C.c_int32), ("elem_type", C.c_uint32)]
 
 
+class AdamwConfig(C.Structure):
+    """sb_adamw_config (include/sheaf_b200.h)."""
+    _fields_ = [("b1", C.c_float), ("b2", C.c_float), ("eps", C.c_float), ("weight_decay", C.c_float),
+                ("max_norm", C.c_float)]
+
+
 class SessionStats(C.Structure):
     """sb_session_stats (include/sheaf_b200.h)."""
     _fields_ = [("calls", C.c_uint64), ("graph_captures", C.c_uint64), ("graph_replays", C.c_uint64),
@@ -56,6 +62,13 @@ SIGNATURES: dict[str, tuple] = {
     "sb_op_attention_bwd_workspace_size": (C.c_size_t, [C.c_uint32, C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
     "sb_op_attention_bwd": (C.c_int, [C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_size_t, C.c_int32, C.c_int32,
                                       C.c_int32, C.c_int32, _P]),
+    "sb_op_adamw_workspace_size": (C.c_size_t, [C.POINTER(C.c_int64), C.c_int32]),
+    "sb_op_adamw_step": (C.c_int, [C.c_uint32, C.c_int32, C.POINTER(C.c_int64), C.POINTER(_P), C.POINTER(_P),
+                                   C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), _P, _P,
+                                   _P, C.c_float, C.c_float, C.c_float, C.c_float, C.c_float, _P, _P, C.c_size_t,
+                                   _P]),
+    "sb_op_global_norm": (C.c_int, [C.c_uint32, C.c_int32, C.POINTER(C.c_int64), C.POINTER(_P), _P, _P, C.c_size_t,
+                                    _P]),
     "sb_op_device_error": (C.c_int, []),
     # sheaf_b200.h
     "sb_status_is_ok": (C.c_bool, [_P]),
@@ -83,6 +96,7 @@ SIGNATURES: dict[str, tuple] = {
     "sb_buffer_device_ptr": (_P, [_P]),
     "sb_module_load_stablehlo": (_P, [_P, C.c_char_p, C.c_size_t, C.POINTER(C.c_char_p)]),
     "sb_module_create_gpt_vag": (_P, [_P, C.c_char_p, C.POINTER(GptConfig)]),
+    "sb_module_create_gpt_train": (_P, [_P, C.c_char_p, C.POINTER(GptConfig), C.POINTER(AdamwConfig)]),
     "sb_module_describe": (_P, [_P, C.c_char_p, C.c_char_p, C.c_size_t]),
     "sb_stablehlo_validate": (_P, [C.c_char_p, C.c_size_t, C.c_char_p, C.c_size_t]),
     "sb_call": (_P, [_P, C.c_char_p, C.POINTER(_P), C.c_size_t, C.POINTER(_P), C.c_size_t, C.POINTER(C.c_size_t)]),

@@ -147,6 +147,32 @@ int sb_op_attention_bwd(uint32_t elem, const void* qkv, const void* o, const voi
                            static_cast<float*>(workspace), sh, static_cast<cudaStream_t>(stream));
 }
 
+size_t sb_op_adamw_workspace_size(const int64_t* counts, int32_t n_leaves) {
+  if (!counts || n_leaves <= 0) return 0;
+  return sb::optimizer_workspace_bytes(counts, n_leaves);
+}
+
+int sb_op_adamw_step(uint32_t elem, int32_t n_leaves, const int64_t* counts, const void* const* grads,
+                     const void* const* params, const void* const* m, const void* const* v, void* const* params_out,
+                     void* const* m_out, void* const* v_out, const void* t, void* t_out, const void* lr, float b1,
+                     float b2, float eps, float wd, float max_norm, void* norm_out, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (!float_elem(elem) || !params || !t || !t_out || !lr) return SB_OPERR_ARGS;
+  return sb::optimizer_step(elem == SB_ELEM_BF16, n_leaves, counts, grads, params, m, v, params_out, m_out, v_out,
+                            static_cast<const float*>(t), static_cast<float*>(t_out), static_cast<const float*>(lr),
+                            b1, b2, eps, wd, max_norm, static_cast<float*>(norm_out), workspace, workspace_bytes,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int sb_op_global_norm(uint32_t elem, int32_t n_leaves, const int64_t* counts, const void* const* grads,
+                      void* norm_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!float_elem(elem) || !norm_out) return SB_OPERR_ARGS;
+  return sb::optimizer_step(elem == SB_ELEM_BF16, n_leaves, counts, grads, nullptr, nullptr, nullptr, nullptr,
+                            nullptr, nullptr, nullptr, nullptr, nullptr, 0.f, 0.f, 0.f, 0.f, 0.f,
+                            static_cast<float*>(norm_out), workspace, workspace_bytes,
+                            static_cast<cudaStream_t>(stream));
+}
+
 int sb_op_device_error(void) {
   int* w = sb::device_error_word();
   if (!w) return -1;

@@ -93,9 +93,25 @@ class GptVagModule : public Module {
   float* ws = nullptr;
   size_t ws_bytes = 0;
 
+  // train-step (with an AdamW configuration): m, v copied in (parameter
+  // layout), t and lr, and the updated state [loss | m | params | t | v]
+  bool train = false;
+  AdamwConfig opt{};
+  char* mbuf = nullptr;
+  char* vbuf = nullptr;
+  float* tl = nullptr;  // tl[0] = t, tl[1] = lr
+  char* state = nullptr;
+  size_t st_m = 0, st_p = 0, st_t = 0, st_v = 0, st_bytes = 0;
+  float* opt_ws = nullptr;
+  size_t opt_ws_bytes = 0;
+
+  // one captured graph per function: [0] value_and_grad, [1] train_step
   cudaGraphExec_t exec = nullptr;
+  cudaGraphExec_t exec_train = nullptr;
   uint64_t kernels_per_step = 0;  // kernel nodes of the captured step graph
+  uint64_t kernels_per_train = 0;
   int eager_runs = 0;
+  int eager_train = 0;
   bool use_graph = true;
   std::vector<cudaEvent_t> bucket_events;
   cudaEvent_t comm_done = nullptr;
@@ -105,6 +121,8 @@ class GptVagModule : public Module {
   void teardown() override {
     if (exec) cudaGraphExecDestroy(exec);
     exec = nullptr;
+    if (exec_train) cudaGraphExecDestroy(exec_train);
+    exec_train = nullptr;
     for (auto e : bucket_events) cudaEventDestroy(e);
     bucket_events.clear();
     if (comm_done) cudaEventDestroy(comm_done);
@@ -113,7 +131,9 @@ class GptVagModule : public Module {
     owned.clear();
   }
 
-  bool has_function(const std::string& fn) const override { return fn == "value_and_grad"; }
+  bool has_function(const std::string& fn) const override {
+    return fn == "value_and_grad" || (train && fn == "train_step");
+  }
 
   void* Pp(int i) const { return params + offs[i]; }
   void* Gp(int i) const { return grads + offs[i]; }
@@ -172,7 +192,7 @@ class GptVagModule : public Module {
     return v;
   }
 
-  sb_status build(const std::string& nm, const GptShape& shape) {
+  sb_status build(const std::string& nm, const GptShape& shape, const AdamwConfig* adamw) {
     name = nm;
     g = shape;
     SB_RETURN_IF(g.elem != SB_ELEM_BF16 && g.elem != SB_ELEM_F32, SB_STATUS_INVALID_ARGUMENT,
@@ -280,12 +300,43 @@ class GptVagModule : public Module {
     w = std::max(w, embedding_bwd_workspace_bytes(V, D));
     ws_bytes = align256(w);
     SB_TRY(devt(ws_bytes / 4 + 64, &ws));
+
+    if (adamw) {
+      train = true;
+      opt = *adamw;
+      SB_TRY(dev(grads_bytes, &v));
+      mbuf = static_cast<char*>(v);
+      SB_TRY(dev(grads_bytes, &v));
+      vbuf = static_cast<char*>(v);
+      SB_TRY(devt(64, &tl));
+      st_m = 256;
+      st_p = st_m + grads_bytes;
+      st_t = st_p + grads_bytes;
+      st_v = st_t + 256;
+      st_bytes = st_v + grads_bytes;
+      SB_TRY(dev(st_bytes, &v));
+      state = static_cast<char*>(v);
+      cudaMemset(state, 0, st_bytes);
+      std::vector<int64_t> cnt = leaf_counts();
+      opt_ws_bytes = align256(optimizer_workspace_bytes(cnt.data(), static_cast<int>(cnt.size())));
+      SB_TRY(devt(opt_ws_bytes / 4 + 64, &opt_ws));
+    }
     return nullptr;
+  }
+
+  std::vector<int64_t> leaf_counts() const {
+    std::vector<int64_t> c;
+    for (auto& sh : shapes) {
+      int64_t n = 1;
+      for (auto d : sh) n *= d;
+      c.push_back(n);
+    }
+    return c;
   }
 
   // Launches the whole fwd+VJP step on `st` (optionally with the gradient
   // all-reduce on the session's comm stream).
-  sb_status enqueue(Session& s, cudaStream_t st) {
+  sb_status enqueue(Session& s, cudaStream_t st, bool train_step) {
     int* err = s.err_word;
     const bool f32 = !bf;
     const bool dp = s.comm != nullptr && s.world > 1;
@@ -378,35 +429,87 @@ class GptVagModule : public Module {
       SB_CUDA_TRY(cudaEventRecord(comm_done, s.comm_stream));
       SB_CUDA_TRY(cudaStreamWaitEvent(st, comm_done, 0));
     }
+    char* loss_dst = train_step ? state : grads + loss_off;
     if (bf)
-      SB_K(convert_f32_to_bf16(loss_f32, reinterpret_cast<__nv_bfloat16*>(grads + loss_off), 1, st));
+      SB_K(convert_f32_to_bf16(loss_f32, reinterpret_cast<__nv_bfloat16*>(loss_dst), 1, st));
     else
-      SB_CUDA_TRY(cudaMemcpyAsync(grads + loss_off, loss_f32, 4, cudaMemcpyDeviceToDevice, st));
+      SB_CUDA_TRY(cudaMemcpyAsync(loss_dst, loss_f32, 4, cudaMemcpyDeviceToDevice, st));
+    if (train_step) {
+      // clip-by-global-norm + adamw-step over the (averaged) gradients
+      // (train.shf:29-32), written into the state block
+      const int n = static_cast<int>(shapes.size());
+      std::vector<int64_t> cnt = leaf_counts();
+      std::vector<const void*> gp(n), pp(n), mp(n), vp(n);
+      std::vector<void*> po(n), mo(n), vo(n);
+      for (int i = 0; i < n; ++i) {
+        gp[i] = Gp(i);
+        pp[i] = Pp(i);
+        mp[i] = mbuf + offs[i];
+        vp[i] = vbuf + offs[i];
+        po[i] = state + st_p + offs[i];
+        mo[i] = state + st_m + offs[i];
+        vo[i] = state + st_v + offs[i];
+      }
+      SB_K(optimizer_step(bf, n, cnt.data(), gp.data(), pp.data(), mp.data(), vp.data(), po.data(), mo.data(),
+                          vo.data(), tl, reinterpret_cast<float*>(state + st_t), tl + 1, opt.b1, opt.b2, opt.eps,
+                          opt.wd, opt.max_norm, nullptr, opt_ws, opt_ws_bytes, st));
+    }
 #undef SB_K
     return nullptr;
   }
 
+  sb_status check_leaf(const Buffer* b, size_t i, const char* what) const {
+    SB_RETURN_IF(b->elem != g.elem, SB_STATUS_INVALID_ARGUMENT, std::string(what) + " " + std::to_string(i) +
+                                                                   ": element type");
+    SB_RETURN_IF(b->shape != shapes[i], SB_STATUS_INVALID_ARGUMENT, std::string(what) + " " + std::to_string(i) +
+                                                                       ": shape");
+    return nullptr;
+  }
+  sb_status check_ids(const Buffer* b) const {
+    SB_RETURN_IF(b->elem != SB_ELEM_F32, SB_STATUS_INVALID_ARGUMENT, "token ids must be f32");
+    SB_RETURN_IF(b->shape != std::vector<int64_t>({B, T}), SB_STATUS_INVALID_ARGUMENT,
+                 "token ids must be [batch, seq]");
+    return nullptr;
+  }
+  sb_status check_f32_scalar(const Buffer* b, const char* what) const {
+    SB_RETURN_IF(b->elem != SB_ELEM_F32 || !b->shape.empty(), SB_STATUS_INVALID_ARGUMENT,
+                 std::string(what) + " must be an f32 scalar");
+    return nullptr;
+  }
+
+  // value_and_grad: leaves..., x, y
   sb_status check_inputs(const std::vector<Buffer*>& in) const {
     const size_t nleaf = shapes.size();
     SB_RETURN_IF(in.size() != nleaf + 2, SB_STATUS_INVALID_ARGUMENT,
                  "value_and_grad expects " + std::to_string(nleaf + 2) + " inputs, got " + std::to_string(in.size()));
-    for (size_t i = 0; i < nleaf; ++i) {
-      SB_RETURN_IF(in[i]->elem != g.elem, SB_STATUS_INVALID_ARGUMENT, "leaf " + std::to_string(i) + ": element type");
-      SB_RETURN_IF(in[i]->shape != shapes[i], SB_STATUS_INVALID_ARGUMENT, "leaf " + std::to_string(i) + ": shape");
-    }
-    for (size_t i = nleaf; i < nleaf + 2; ++i) {
-      SB_RETURN_IF(in[i]->elem != SB_ELEM_F32, SB_STATUS_INVALID_ARGUMENT, "token ids must be f32");
-      SB_RETURN_IF(in[i]->shape != std::vector<int64_t>({B, T}), SB_STATUS_INVALID_ARGUMENT,
-                   "token ids must be [batch, seq]");
-    }
+    for (size_t i = 0; i < nleaf; ++i) SB_TRY(check_leaf(in[i], i, "leaf"));
+    SB_TRY(check_ids(in[nleaf]));
+    SB_TRY(check_ids(in[nleaf + 1]));
     return nullptr;
   }
 
-  sb_status copy_in(Session& s, const std::vector<Buffer*>& in, cudaStream_t st) {
-    std::vector<std::pair<const void*, std::pair<void*, size_t>>> segs;
-    for (size_t i = 0; i < shapes.size(); ++i) segs.push_back({in[i]->data(), {Pp(static_cast<int>(i)), in[i]->bytes()}});
-    segs.push_back({in[shapes.size()]->data(), {ids, static_cast<size_t>(N) * 4}});
-    segs.push_back({in[shapes.size() + 1]->data(), {ids + N, static_cast<size_t>(N) * 4}});
+  // train_step: loss, m..., params..., t, v..., x, y, lr
+  sb_status check_train_inputs(const std::vector<Buffer*>& in) const {
+    const size_t n = shapes.size();
+    SB_RETURN_IF(in.size() != 3 * n + 5, SB_STATUS_INVALID_ARGUMENT,
+                 "train_step expects " + std::to_string(3 * n + 5) + " inputs, got " + std::to_string(in.size()));
+    SB_RETURN_IF(!in[0]->shape.empty(), SB_STATUS_INVALID_ARGUMENT, "state loss must be a scalar");
+    for (size_t i = 0; i < n; ++i) {
+      SB_TRY(check_leaf(in[1 + i], i, "m leaf"));
+      SB_TRY(check_leaf(in[1 + n + i], i, "param leaf"));
+      SB_TRY(check_leaf(in[2 + 2 * n + i], i, "v leaf"));
+    }
+    SB_TRY(check_f32_scalar(in[1 + 2 * n], "t"));
+    SB_TRY(check_ids(in[2 + 3 * n]));
+    SB_TRY(check_ids(in[3 + 3 * n]));
+    SB_TRY(check_f32_scalar(in[4 + 3 * n], "lr"));
+    return nullptr;
+  }
+
+  using Seg = std::pair<const void*, std::pair<void*, size_t>>;
+
+  // Copies every input into its plan-owned slot with batched-copy launches.
+  sb_status copy_segs(Session& s, const std::vector<Seg>& segs, cudaStream_t st) {
     for (size_t base = 0; base < segs.size(); base += kMaxSegs) {
       CopySegs c{};
       c.n = static_cast<int>(std::min<size_t>(kMaxSegs, segs.size() - base));
@@ -425,10 +528,79 @@ class GptVagModule : public Module {
     return nullptr;
   }
 
+  sb_status copy_in(Session& s, const std::vector<Buffer*>& in, cudaStream_t st) {
+    std::vector<Seg> segs;
+    for (size_t i = 0; i < shapes.size(); ++i) segs.push_back({in[i]->data(), {Pp(static_cast<int>(i)), in[i]->bytes()}});
+    segs.push_back({in[shapes.size()]->data(), {ids, static_cast<size_t>(N) * 4}});
+    segs.push_back({in[shapes.size() + 1]->data(), {ids + N, static_cast<size_t>(N) * 4}});
+    return copy_segs(s, segs, st);
+  }
+
+  sb_status copy_in_train(Session& s, const std::vector<Buffer*>& in, cudaStream_t st) {
+    const size_t n = shapes.size();
+    std::vector<Seg> segs;
+    for (size_t i = 0; i < n; ++i) {
+      segs.push_back({in[1 + i]->data(), {mbuf + offs[i], in[1 + i]->bytes()}});
+      segs.push_back({in[1 + n + i]->data(), {Pp(static_cast<int>(i)), in[1 + n + i]->bytes()}});
+      segs.push_back({in[2 + 2 * n + i]->data(), {vbuf + offs[i], in[2 + 2 * n + i]->bytes()}});
+    }
+    segs.push_back({in[1 + 2 * n]->data(), {tl, 4}});
+    segs.push_back({in[4 + 3 * n]->data(), {tl + 1, 4}});
+    segs.push_back({in[2 + 3 * n]->data(), {ids, static_cast<size_t>(N) * 4}});
+    segs.push_back({in[3 + 3 * n]->data(), {ids + N, static_cast<size_t>(N) * 4}});
+    return copy_segs(s, segs, st);
+  }
+
+  // Runs the step: eagerly on the first call of a function, then from the
+  // CUDA graph captured on the second.
+  sb_status run(Session& s, cudaStream_t st, bool train_step) {
+    cudaGraphExec_t& ex = train_step ? exec_train : exec;
+    uint64_t& kernels = train_step ? kernels_per_train : kernels_per_step;
+    int& eager = train_step ? eager_train : eager_runs;
+    const bool dp = s.comm != nullptr && s.world > 1;
+    if (!use_graph || eager < 1) {
+      SB_TRY(enqueue(s, st, train_step));
+      ++eager;
+      return nullptr;
+    }
+    if (!ex) {
+      cudaGraph_t graph = nullptr;
+      SB_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      sb_status e = enqueue(s, st, train_step);
+      cudaError_t ce = cudaStreamEndCapture(st, &graph);
+      if (e) {
+        if (graph) cudaGraphDestroy(graph);
+        return e;
+      }
+      if (ce != cudaSuccess) return make_status(SB_STATUS_INTERNAL, std::string("graph capture: ") + cudaGetErrorString(ce));
+      size_t nnodes = 0;
+      cudaGraphGetNodes(graph, nullptr, &nnodes);
+      std::vector<cudaGraphNode_t> nodes(nnodes);
+      cudaGraphGetNodes(graph, nodes.data(), &nnodes);
+      kernels = 0;
+      for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+      }
+      // NCCL's own kernels (one per bucket all-reduce and one for the loss)
+      // are not library kernels
+      if (dp) kernels -= std::min<uint64_t>(kernels, static_cast<uint64_t>(L) + 3);
+      ce = cudaGraphInstantiate(&ex, graph, 0);
+      cudaGraphDestroy(graph);
+      if (ce != cudaSuccess) return make_status(SB_STATUS_INTERNAL, std::string("graph instantiate: ") + cudaGetErrorString(ce));
+      s.graph_captures++;
+    }
+    SB_CUDA_TRY(cudaGraphLaunch(ex, st));
+    s.graph_replays++;
+    s.kernel_launches += kernels;
+    return nullptr;
+  }
+
   sb_status call(Session& s, const std::string& fn, const std::vector<Buffer*>& in,
                  std::vector<Buffer*>& out) override {
-    SB_RETURN_IF(fn != "value_and_grad", SB_STATUS_NOT_FOUND, "unknown function " + fn);
-    SB_TRY(check_inputs(in));
+    const bool train_step = fn == "train_step";
+    SB_RETURN_IF(fn != "value_and_grad" && !(train && train_step), SB_STATUS_NOT_FOUND, "unknown function " + fn);
+    SB_TRY(train_step ? check_train_inputs(in) : check_inputs(in));
     cudaStream_t st = s.stream;
     const bool dp = s.comm != nullptr && s.world > 1;
     if (dp && bucket_events.empty()) {
@@ -439,58 +611,38 @@ class GptVagModule : public Module {
       }
       SB_CUDA_TRY(cudaEventCreateWithFlags(&comm_done, cudaEventDisableTiming));
     }
-    SB_TRY(copy_in(s, in, st));
-    if (!use_graph || eager_runs < 1) {
-      SB_TRY(enqueue(s, st));
-      ++eager_runs;
-    } else {
-      if (!exec) {
-        cudaGraph_t graph = nullptr;
-        SB_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-        sb_status e = enqueue(s, st);
-        cudaError_t ce = cudaStreamEndCapture(st, &graph);
-        if (e) {
-          if (graph) cudaGraphDestroy(graph);
-          return e;
-        }
-        if (ce != cudaSuccess) return make_status(SB_STATUS_INTERNAL, std::string("graph capture: ") + cudaGetErrorString(ce));
-        size_t nnodes = 0;
-        cudaGraphGetNodes(graph, nullptr, &nnodes);
-        std::vector<cudaGraphNode_t> nodes(nnodes);
-        cudaGraphGetNodes(graph, nodes.data(), &nnodes);
-        kernels_per_step = 0;
-        for (auto n : nodes) {
-          cudaGraphNodeType t;
-          if (cudaGraphNodeGetType(n, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels_per_step;
-        }
-        // NCCL's own kernels (one per bucket all-reduce and one for the loss)
-        // are not library kernels
-        if (dp) kernels_per_step -= std::min<uint64_t>(kernels_per_step, static_cast<uint64_t>(L) + 3);
-        ce = cudaGraphInstantiate(&exec, graph, 0);
-        cudaGraphDestroy(graph);
-        if (ce != cudaSuccess) return make_status(SB_STATUS_INTERNAL, std::string("graph instantiate: ") + cudaGetErrorString(ce));
-        s.graph_captures++;
-      }
-      SB_CUDA_TRY(cudaGraphLaunch(exec, st));
-      s.graph_replays++;
-      s.kernel_launches += kernels_per_step;
-    }
-    // outputs: one pool allocation holds every gradient and the loss
+    SB_TRY(train_step ? copy_in_train(s, in, st) : copy_in(s, in, st));
+    SB_TRY(run(s, st, train_step));
+    const int n = static_cast<int>(shapes.size());
     Allocation* a = nullptr;
-    SB_TRY(session_alloc(s, out_bytes, &a));
-    SB_CUDA_TRY(cudaMemcpyAsync(a->ptr, grads, out_bytes, cudaMemcpyDeviceToDevice, st));
-    a->refs.store(static_cast<int>(shapes.size()) + 1);
-    out.push_back(buffer_new(s, a, loss_off, {}, g.elem));
-    for (size_t i = 0; i < shapes.size(); ++i) out.push_back(buffer_new(s, a, offs[i], shapes[i], g.elem));
+    if (!train_step) {
+      // outputs: one pool allocation holds every gradient and the loss
+      SB_TRY(session_alloc(s, out_bytes, &a));
+      SB_CUDA_TRY(cudaMemcpyAsync(a->ptr, grads, out_bytes, cudaMemcpyDeviceToDevice, st));
+      a->refs.store(n + 1);
+      out.push_back(buffer_new(s, a, loss_off, {}, g.elem));
+      for (int i = 0; i < n; ++i) out.push_back(buffer_new(s, a, offs[i], shapes[i], g.elem));
+      return nullptr;
+    }
+    // the updated state [loss | m | params | t | v] in one pool allocation
+    SB_TRY(session_alloc(s, st_bytes, &a));
+    SB_CUDA_TRY(cudaMemcpyAsync(a->ptr, state, st_bytes, cudaMemcpyDeviceToDevice, st));
+    a->refs.store(3 * n + 2);
+    out.push_back(buffer_new(s, a, 0, {}, g.elem));
+    for (int i = 0; i < n; ++i) out.push_back(buffer_new(s, a, st_m + offs[i], shapes[i], g.elem));
+    for (int i = 0; i < n; ++i) out.push_back(buffer_new(s, a, st_p + offs[i], shapes[i], g.elem));
+    out.push_back(buffer_new(s, a, st_t, {}, SB_ELEM_F32));
+    for (int i = 0; i < n; ++i) out.push_back(buffer_new(s, a, st_v + offs[i], shapes[i], g.elem));
     return nullptr;
   }
 };
 
 }  // namespace
 
-sb_status make_gpt_vag_module(Session& s, const std::string& name, const GptShape& g, std::unique_ptr<Module>* out) {
+sb_status make_gpt_vag_module(Session& s, const std::string& name, const GptShape& g, std::unique_ptr<Module>* out,
+                              const AdamwConfig* adamw) {
   auto m = std::make_unique<GptVagModule>();
-  sb_status st = m->build(name, g);
+  sb_status st = m->build(name, g, adamw);
   if (st) return st;
   *out = std::move(m);
   return nullptr;

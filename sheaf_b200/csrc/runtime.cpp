@@ -290,6 +290,22 @@ sb_status sb_module_create_gpt_vag(sb_session* s, const char* name, const sb_gpt
   return nullptr;
 }
 
+sb_status sb_module_create_gpt_train(sb_session* s, const char* name, const sb_gpt_config* c,
+                                     const sb_adamw_config* o) {
+  SB_RETURN_IF(!s || !name || !c || !o, SB_STATUS_INVALID_ARGUMENT, "null argument");
+  SB_RETURN_IF(!(o->b1 >= 0.f && o->b1 < 1.f && o->b2 >= 0.f && o->b2 < 1.f && o->eps >= 0.f),
+               SB_STATUS_INVALID_ARGUMENT, "adamw: b1, b2 must lie in [0, 1) and eps >= 0");
+  cudaSetDevice(s->device);
+  GptShape g{c->n_layer, c->n_head, c->n_embd, c->block_size, c->vocab_size, c->batch, c->seq, c->elem_type};
+  AdamwConfig a{o->b1, o->b2, o->eps, o->weight_decay, o->max_norm};
+  std::unique_ptr<Module> m;
+  SB_TRY(make_gpt_vag_module(*s, name, g, &m, &a));
+  std::lock_guard<std::mutex> lk(s->mu);
+  if (auto it = s->modules.find(name); it != s->modules.end()) it->second->teardown();
+  s->modules[name] = std::move(m);
+  return nullptr;
+}
+
 sb_status sb_module_load_stablehlo(sb_session* s, const char* text, size_t len, const char** out_name) {
   SB_RETURN_IF(!s || !text, SB_STATUS_INVALID_ARGUMENT, "null argument");
   cudaSetDevice(s->device);

@@ -104,7 +104,13 @@ struct GptShape {
   int n_layer, n_head, n_embd, block_size, vocab, batch, seq;
   uint32_t elem;  // SB_ELEM_BF16 or SB_ELEM_F32 (parameter / compute type)
 };
-sb_status make_gpt_vag_module(Session& s, const std::string& name, const GptShape& g, std::unique_ptr<Module>* out);
+struct AdamwConfig {
+  float b1, b2, eps, wd, max_norm;
+};
+// With `adamw`, the module also runs the train-step function (VAG + clip +
+// AdamW in one graph).
+sb_status make_gpt_vag_module(Session& s, const std::string& name, const GptShape& g, std::unique_ptr<Module>* out,
+                              const AdamwConfig* adamw = nullptr);
 
 // Parses StableHLO text and maps it onto the kernel library (stablehlo.cpp).
 sb_status load_stablehlo_module(Session& s, const char* text, size_t len, std::unique_ptr<Module>* out);

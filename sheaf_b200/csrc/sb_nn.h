@@ -62,4 +62,16 @@ size_t attention_bwd_workspace_bytes(bool f32, const AttnShape& sh);
 int attention_bwd(const void* qkv, const void* o, const void* dout, const float* lse, bool f32, void* dqkv, float* ws,
                   const AttnShape& sh, cudaStream_t s);
 
+// Global gradient norm, and with `params` the clip-by-global-norm + AdamW
+// step of nanoGPT's train-step over n_leaves tensors of one element type
+// (pointer arrays on the host, tensors on the device). t_in, lr: device f32
+// scalars; t_out <- t_in + 1. Outputs may alias inputs. max_norm <= 0: no
+// clipping. norm_out (optional): the global norm of the unclipped gradients.
+size_t optimizer_workspace_bytes(const int64_t* counts, int n_leaves);
+int optimizer_step(bool bf16, int n_leaves, const int64_t* counts, const void* const* grads,
+                   const void* const* params, const void* const* m, const void* const* v, void* const* params_out,
+                   void* const* m_out, void* const* v_out, const float* t_in, float* t_out, const float* lr,
+                   float b1, float b2, float eps, float wd, float max_norm, float* norm_out, void* workspace,
+                   size_t workspace_bytes, cudaStream_t s);
+
 }  // namespace sb

@@ -141,6 +141,15 @@ class Session:
         _check(lib().sb_module_create_gpt_vag(self._h, name.encode(), C.byref(cfg)))
         return name
 
+    def create_gpt_train(self, name: str, *, n_layer, n_head, n_embd, block_size, vocab_size, batch, seq,
+                         elem=ELEM_BF16, b1=0.9, b2=0.95, eps=1e-8, weight_decay=0.1, max_norm=1.0) -> str:
+        """nanoGPT train-step module (value_and_grad + clip-by-global-norm +
+        AdamW); the defaults are examples/nanogpt/train.shf's constants."""
+        cfg = _lib.GptConfig(n_layer, n_head, n_embd, block_size, vocab_size, batch, seq, elem)
+        opt = _lib.AdamwConfig(b1, b2, eps, weight_decay, max_norm)
+        _check(lib().sb_module_create_gpt_train(self._h, name.encode(), C.byref(cfg), C.byref(opt)))
+        return name
+
     def call(self, qualified_name: str, inputs: Sequence["Buffer"], max_outputs: int = 1024) -> list["Buffer"]:
         arr = (C.c_void_p * max(1, len(inputs)))(*[b._h for b in inputs])
         outs = (C.c_void_p * max_outputs)()
