@@ -88,7 +88,7 @@ class GptVagModule : public Module {
   void *hf = nullptr, *logits = nullptr, *dlogits = nullptr;
   float* dres = nullptr;
   void* dres_bf = nullptr;
-  float* dh = nullptr;
+  void* dh = nullptr;  // dy of the layer-norm VJPs, model element type (as the module materialises it)
   void *du = nullptr, *dout = nullptr, *dqkv = nullptr;
   float* ws = nullptr;
   size_t ws_bytes = 0;
@@ -287,7 +287,7 @@ class GptVagModule : public Module {
     cudaMemset(dlogits, 0, static_cast<size_t>(N) * ldl * es);
     SB_TRY(devt(nd, &dres));
     if (bf) SB_TRY(dev(nd * 2, &dres_bf));
-    SB_TRY(devt(nd, &dh));
+    SB_TRY(dev(nd * es, &dh));
     SB_TRY(dev(4 * nd * es, &du));
     SB_TRY(dev(nd * es, &dout));
     SB_TRY(dev(3 * nd * es, &dqkv));
@@ -381,11 +381,11 @@ class GptVagModule : public Module {
     SB_K(cross_entropy_fwd_bwd(logits, f32, ldl, N, V, ids + N, dlogits, ldl, ws, loss_f32, nullptr, st));
 
     // ---- backward
-    SB_K(gemm(desc(dlogits, ldl, false, Pp(0), D, true, N, D, V, dh, D, true), st, err));
+    SB_K(gemm(desc(dlogits, ldl, false, Pp(0), D, true, N, D, V, dh, D, f32), st, err));
     SB_K(gemm(desc(dlogits, ldl, true, hf, D, true, V, D, N, Gp(0), D, f32), st, err));
     if (cudaMemsetAsync(dres, 0, static_cast<size_t>(N) * D * sizeof(float), st) != cudaSuccess)
       return make_status(SB_STATUS_INTERNAL, "memset failed");
-    SB_K(layernorm_bwd(dh, true, xs[L], meanf, rstdf, Pp(ilnf), f32, dres, static_cast<__nv_bfloat16*>(dres_bf),
+    SB_K(layernorm_bwd(dh, f32, xs[L], meanf, rstdf, Pp(ilnf), f32, dres, static_cast<__nv_bfloat16*>(dres_bf),
                        Gp(ilnf), f32, ws, N, D, st));
     int bucket = 0;
     auto launch_bucket = [&](size_t lo_off, size_t hi_off) -> sb_status {
@@ -409,15 +409,15 @@ class GptVagModule : public Module {
         SB_K(gemm(d, st, err));
       }
       SB_K(gemm(desc(du, 4 * D, true, h2[l], D, true, 4 * D, D, N, Gp(b0 + 4), D, f32), st, err));
-      SB_K(gemm(desc(du, 4 * D, false, Pp(b0 + 4), D, true, N, D, 4 * D, dh, D, true), st, err));
-      SB_K(layernorm_bwd(dh, true, xmid[l], mean2[l], rstd2[l], Pp(b0 + 3), f32, dres,
+      SB_K(gemm(desc(du, 4 * D, false, Pp(b0 + 4), D, true, N, D, 4 * D, dh, D, f32), st, err));
+      SB_K(layernorm_bwd(dh, f32, xmid[l], mean2[l], rstd2[l], Pp(b0 + 3), f32, dres,
                          static_cast<__nv_bfloat16*>(dres_bf), Gp(b0 + 3), f32, ws, N, D, st));
       SB_K(gemm(desc(opnd, D, true, att[l], D, true, D, D, N, Gp(b0 + 1), D, f32), st, err));
       SB_K(gemm(desc(opnd, D, false, Pp(b0 + 1), D, true, N, D, D, dout, D, f32), st, err));
       SB_K(attention_bwd(qkv[l], att[l], dout, lse[l], f32, dqkv, ws, ash, st));
       SB_K(gemm(desc(dqkv, 3 * D, true, h1[l], D, true, 3 * D, D, N, Gp(b0 + 0), D, f32), st, err));
-      SB_K(gemm(desc(dqkv, 3 * D, false, Pp(b0 + 0), D, true, N, D, 3 * D, dh, D, true), st, err));
-      SB_K(layernorm_bwd(dh, true, xs[l], mean1[l], rstd1[l], Pp(b0 + 2), f32, dres,
+      SB_K(gemm(desc(dqkv, 3 * D, false, Pp(b0 + 0), D, true, N, D, 3 * D, dh, D, f32), st, err));
+      SB_K(layernorm_bwd(dh, f32, xs[l], mean1[l], rstd1[l], Pp(b0 + 2), f32, dres,
                          static_cast<__nv_bfloat16*>(dres_bf), Gp(b0 + 2), f32, ws, N, D, st));
       // layer l's six gradients (plus ln_f after the last layer) are final
       SB_TRY(launch_bucket(offs[b0], l == L - 1 ? offs[ip] : offs[b0 + 6]));

@@ -152,9 +152,13 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
 // sums of dgamma = sum_rows dy * xhat into dgamma_part[blockIdx.x][D].
 // x, dy and dres of a row are loaded together (the dres read does not wait
 // for the row reductions); gamma is re-read from L1 per row to keep the
-// register count at three resident blocks per SM.
+// register count low. Rows up to 384 wide run 24 warps per block, one block
+// per SM, so there is one dgamma partial row per SM.
+template <int VPT>
+constexpr int ln_bwd_warps() { return VPT <= 3 ? 24 : 8; }
+
 template <int VPT, typename TI>
-__global__ void __launch_bounds__(256, VPT <= 3 ? 3 : (VPT <= 4 ? 2 : 1)) ln_bwd_kernel(const TI* __restrict__ dy, const float* __restrict__ x,
+__global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(const TI* __restrict__ dy, const float* __restrict__ x,
                                                         const float* __restrict__ mean_in,
                                                         const float* __restrict__ rstd_in,
                                                         const void* __restrict__ gamma, int gamma_f32,
@@ -497,17 +501,22 @@ int layernorm_fwd(const float* x, const void* gamma, bool gamma_f32, void* y, bo
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
+namespace {
+// Blocks of the layer-norm VJP: one per SM (fewer for short inputs).
+int ln_bwd_grid(int rows, int warps) { return std::max(1, std::min((rows + warps - 1) / warps, num_sms_cached())); }
+int ln_bwd_warps_for(int D) { return (D + 127) / 128 <= 3 ? 24 : 8; }
+}  // namespace
+
 size_t layernorm_bwd_workspace_bytes(int rows, int D) {
-  const int grid = std::min((rows + 7) / 8, 3 * num_sms_cached());
-  return static_cast<size_t>(grid) * D * sizeof(float);
+  return static_cast<size_t>(ln_bwd_grid(rows, ln_bwd_warps_for(D))) * D * sizeof(float);
 }
 
 int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean, const float* rstd, const void* gamma,
                   bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma, bool dgamma_f32, float* ws,
                   int rows, int D, cudaStream_t s) {
   if (rows <= 0 || D <= 0 || (D & 3)) return 1;
-  const int warps = 8;
-  const int grid = std::min((rows + warps - 1) / warps, 3 * num_sms_cached());
+  const int warps = ln_bwd_warps_for(D);
+  const int grid = ln_bwd_grid(rows, warps);
   const size_t smem = static_cast<size_t>(warps) * D * sizeof(float);
   if (smem > 200 * 1024) return 1;
   if (dy_f32)
