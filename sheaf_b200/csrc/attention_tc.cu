@@ -15,8 +15,8 @@
 //   warps 2-5 softmax: thread = query row; reads its S row from TMEM, keeps
 //             the running max / sum, writes P (bf16, 128B-swizzled K-major)
 //             to shared memory for the P V UMMA, accumulates O_j in registers.
-// Backward, one CTA per (batch, head, 128-key tile), looping over the query
-// tiles at or after it:
+// Backward, persistent (one CTA per SM) over (batch, head, 128-key tile) work
+// items, each looping over the query tiles at or after its key tile:
 //   S^T = K Q^T and dP^T = V dO^T into TMEM (thread = key row);
 //   P^T, dS^T = P^T * (dP^T - delta) / sqrt(Hd) written to shared memory;
 //   dV += P^T dO, dK += dS^T Q (accumulated in TMEM across query tiles);
@@ -281,9 +281,9 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
 // backward
 // ---------------------------------------------------------------------------
 
-constexpr size_t kBwdSmem = 1024 + 2 * kTileBytes /*K,V*/ + 4 * kTileBytes /*Q,dO x2*/ +
-                            4 * kTileBytes /*P^T, dS^T*/ + 2 * kTileBytes /*dQ staging*/ +
-                            4 * kT * 4 /*lse, delta x2*/ + 16 * 8 + 16;
+constexpr size_t kBwdSmem = 1024 + 4 * kTileBytes /*K,V x2*/ + 4 * kTileBytes /*Q,dO x2*/ +
+                            4 * kTileBytes /*P^T, dS^T*/ + kTileBytes /*dQ staging, 4 KB per warp*/ +
+                            4 * kT * 4 /*lse, delta x2*/ + 24 * 8 + 16;
 
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t smem_src, int x, int y) {
   asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
@@ -292,53 +292,74 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32
                : "memory");
 }
 
+// Work item u of the VJP: key tile kt = u / (B*H) (long items first), head
+// bh = u % (B*H); it loops over the query tiles kt .. ntiles-1.
+struct BwdItem {
+  int kt, bh, h, row0, nq, b;
+};
+__device__ __forceinline__ BwdItem bwd_item(const AttnArgs& a, int u) {
+  BwdItem w;
+  const int bhn = a.B * a.H;
+  w.kt = u / bhn;
+  w.bh = u % bhn;
+  w.b = w.bh / a.H;
+  w.h = w.bh % a.H;
+  w.row0 = w.b * a.T;
+  w.nq = a.ntiles - w.kt;
+  return w;
+}
+
+// Persistent VJP: one CTA per SM loops over work items. K/V are double
+// buffered and the Q/dO ring runs across items, so the next item's loads
+// land while the current one computes; lse/delta of the next query tile are
+// loaded one tile ahead; dK/dV leave through swizzled staging and TMA stores.
 __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CUtensorMap tm_qkv,
                                                       const __grid_constant__ CUtensorMap tm_do,
-                                                      const __grid_constant__ CUtensorMap tm_dq, AttnArgs a) {
+                                                      const __grid_constant__ CUtensorMap tm_dq,
+                                                      const __grid_constant__ CUtensorMap tm_dkv, AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = sm;
-  uint8_t* sV = sK + kTileBytes;
-  uint8_t* sQ = sV + kTileBytes;      // [2]
-  uint8_t* sdO = sQ + 2 * kTileBytes;  // [2]
-  uint8_t* sPT = sdO + 2 * kTileBytes;  // 32 KB
-  uint8_t* sdST = sPT + 2 * kTileBytes;  // 32 KB
-  uint8_t* sStg = sdST + 2 * kTileBytes;  // 4 warps x 2 x (32 rows x 128 B) dQ staging
-  float* sLse = reinterpret_cast<float*>(sStg + 2 * kTileBytes);  // [2][128]
-  float* sDel = sLse + 2 * kT;                                     // [2][128]
+  uint8_t* sK = sm;                       // [2]
+  uint8_t* sV = sK + 2 * kTileBytes;      // [2]
+  uint8_t* sQ = sV + 2 * kTileBytes;      // [2]
+  uint8_t* sdO = sQ + 2 * kTileBytes;     // [2]
+  uint8_t* sPT = sdO + 2 * kTileBytes;    // 32 KB; also dK (first atom) / dV (second atom) staging
+  uint8_t* sdST = sPT + 2 * kTileBytes;   // 32 KB
+  uint8_t* sStg = sdST + 2 * kTileBytes;  // 4 warps x 4 KB dQ staging
+  float* sLse = reinterpret_cast<float*>(sStg + kTileBytes);  // [2][128]
+  float* sDel = sLse + 2 * kT;                                // [2][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 2 * kT);
-  uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;   // [2]
-  uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* st_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* dq_full = bars + 7;
-  uint64_t* dq_empty = bars + 8;
-  uint64_t* acc_full = bars + 9;
-  uint64_t* stats_full = bars + 10;  // [2]: the 4 softmax warps wrote lse / delta of a query tile
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* kv_full = bars + 0;     // [2]
+  uint64_t* kv_empty = bars + 2;    // [2]
+  uint64_t* qd_full = bars + 4;     // [2]
+  uint64_t* qd_empty = bars + 6;    // [2]
+  uint64_t* st_full = bars + 8;
+  uint64_t* p_full = bars + 9;
+  uint64_t* dq_full = bars + 10;
+  uint64_t* dq_empty = bars + 11;
+  uint64_t* acc_full = bars + 12;
+  uint64_t* acc_empty = bars + 13;
+  uint64_t* stats_full = bars + 14;  // [2]: the 4 softmax warps wrote lse / delta of a query tile
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = static_cast<int>(blockIdx.x % a.ntiles);  // long columns (kt = 0) first
-  const int bh = blockIdx.x / a.ntiles;
-  const int b = bh / a.H, h = bh % a.H;
-  const int row0 = b * a.T;
-  const int nq = a.ntiles - kt;  // query tiles kt .. ntiles-1
+  const int nitems = a.B * a.H * a.ntiles;
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&qd_full[s], 1);
-      mbar_init(&qd_empty[s], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+      mbar_init(&stats_full[i], 4);
     }
     mbar_init(st_full, 1);
     mbar_init(p_full, 4);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 4);
     mbar_init(acc_full, 1);
-    mbar_init(&stats_full[0], 4);
-    mbar_init(&stats_full[1], 4);
+    mbar_init(acc_empty, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -346,6 +367,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_do);
     tma_prefetch_desc(&tm_dq);
+    tma_prefetch_desc(&tm_dkv);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -359,15 +381,37 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(kv_full, 2 * kTileBytes);
-      tma_load_2d(sK, &tm_qkv, kv_full, a.D + h * kHd, row0 + kt * kT);
-      tma_load_2d(sV, &tm_qkv, kv_full, 2 * a.D + h * kHd, row0 + kt * kT);
-      for (int it = 0; it < nq; ++it) {
-        const int s = it & 1, i = kt + it;
-        if (!mbar_wait(&qd_empty[s], ((it >> 1) & 1) ^ 1, a.err, abort_flag)) break;
-        mbar_arrive_expect_tx(&qd_full[s], 2 * kTileBytes);
-        tma_load_2d(sQ + s * kTileBytes, &tm_qkv, &qd_full[s], h * kHd, row0 + i * kT);
-        tma_load_2d(sdO + s * kTileBytes, &tm_do, &qd_full[s], h * kHd, row0 + i * kT);
+      uint32_t g = 0;  // query tiles loaded by this CTA
+      int j = 0;       // items of this CTA
+      bool ok = true;
+      for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++j) {
+        const BwdItem w = bwd_item(a, u);
+        const int kb = j & 1;
+        if (!mbar_wait(&kv_empty[kb], ((j >> 1) & 1) ^ 1, a.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[kb], 2 * kTileBytes);
+        tma_load_2d(sK + kb * kTileBytes, &tm_qkv, &kv_full[kb], a.D + w.h * kHd, w.row0 + w.kt * kT);
+        tma_load_2d(sV + kb * kTileBytes, &tm_qkv, &kv_full[kb], 2 * a.D + w.h * kHd, w.row0 + w.kt * kT);
+        for (int it = 0; it < w.nq; ++it, ++g) {
+          const int s = g & 1, i = w.kt + it;
+          if (!mbar_wait(&qd_empty[s], ((g >> 1) & 1) ^ 1, a.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&qd_full[s], 2 * kTileBytes);
+          tma_load_2d(sQ + s * kTileBytes, &tm_qkv, &qd_full[s], w.h * kHd, w.row0 + i * kT);
+          tma_load_2d(sdO + s * kTileBytes, &tm_do, &qd_full[s], w.h * kHd, w.row0 + i * kT);
+        }
+      }
+      // wait for the final releases of every buffer, so that no UMMA commit
+      // arrives on this CTA's barriers after it exits
+      if (ok) {
+        for (int i = 0; i < 2; ++i, ++g)
+          if (!mbar_wait(&qd_empty[g & 1], ((g >> 1) & 1) ^ 1, a.err, abort_flag)) break;
+        for (int i = 0; i < 2; ++i, ++j)
+          if (!mbar_wait(&kv_empty[j & 1], ((j >> 1) & 1) ^ 1, a.err, abort_flag)) break;
       }
     }
   } else if (warp == 1) {
@@ -375,63 +419,85 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
       constexpr uint32_t idS = make_idesc_bf16(128, 128, false, false);
       constexpr uint32_t idKV = make_idesc_bf16(128, 64, false, true);
       constexpr uint32_t idQ = make_idesc_bf16(128, 64, true, true);
-      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       const uint32_t pt_addr = smem_u32(sPT), dst_addr = smem_u32(sdST);
-      bool ok = mbar_wait(kv_full, 0, a.err, abort_flag);
-      for (int it = 0; it < nq && ok; ++it) {
-        const int s = it & 1;
-        if (!mbar_wait(&qd_full[s], (it >> 1) & 1, a.err, abort_flag)) {
+      uint32_t g = 0;
+      int j = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++j) {
+        const BwdItem w = bwd_item(a, u);
+        const int kb = j & 1;
+        if (!mbar_wait(&kv_full[kb], (j >> 1) & 1, a.err, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t q_addr = smem_u32(sQ + s * kTileBytes), do_addr = smem_u32(sdO + s * kTileBytes);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_f16(tST, kdesc(k_addr, kk), kdesc(q_addr, kk), idS, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_f16(tdPT, kdesc(v_addr, kk), kdesc(do_addr, kk), idS, kk > 0);
-        umma_commit(st_full);
-        if (!mbar_wait(p_full, it & 1, a.err, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_f16(tdV, kdesc2(pt_addr, kk), mndesc(do_addr, kk, 8192), idKV, (it > 0 || kk > 0));
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_f16(tdK, kdesc2(dst_addr, kk), mndesc(q_addr, kk, 8192), idKV, (it > 0 || kk > 0));
-        if (it > 0) {
-          if (!mbar_wait(dq_empty, (it - 1) & 1, a.err, abort_flag)) {
+        const uint32_t k_addr = smem_u32(sK + kb * kTileBytes), v_addr = smem_u32(sV + kb * kTileBytes);
+        for (int it = 0; it < w.nq; ++it, ++g) {
+          const int s = g & 1;
+          if (!mbar_wait(&qd_full[s], (g >> 1) & 1, a.err, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-        }
+          const uint32_t q_addr = smem_u32(sQ + s * kTileBytes), do_addr = smem_u32(sdO + s * kTileBytes);
+          // S^T, dP^T overwrite what the softmax warps read for tile g-1
+          // (they arrived on p_full(g-1) before this point)
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_f16(tdQ, mndesc(dst_addr, kk, 16384), mndesc(k_addr, kk, 8192), idQ, kk > 0);
-        umma_commit(dq_full);
-        umma_commit(&qd_empty[s]);
+          for (int kk = 0; kk < 4; ++kk) umma_f16(tST, kdesc(k_addr, kk), kdesc(q_addr, kk), idS, kk > 0);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) umma_f16(tdPT, kdesc(v_addr, kk), kdesc(do_addr, kk), idS, kk > 0);
+          umma_commit(st_full);
+          if (!mbar_wait(p_full, g & 1, a.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (it == 0 && j > 0) {  // the previous item's dK / dV have been read out
+            if (!mbar_wait(acc_empty, (j - 1) & 1, a.err, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tdV, kdesc2(pt_addr, kk), mndesc(do_addr, kk, 8192), idKV, (it > 0 || kk > 0));
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tdK, kdesc2(dst_addr, kk), mndesc(q_addr, kk, 8192), idKV, (it > 0 || kk > 0));
+          if (g > 0) {
+            if (!mbar_wait(dq_empty, (g - 1) & 1, a.err, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tdQ, mndesc(dst_addr, kk, 16384), mndesc(k_addr, kk, 8192), idQ, kk > 0);
+          umma_commit(dq_full);
+          umma_commit(&qd_empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(acc_full);
+        umma_commit(&kv_empty[kb]);
       }
-      if (ok) umma_commit(acc_full);
     }
   } else {
     const int quarter = warp & 3;
     const int tid = quarter * 32 + lane;  // 0..127: key row (S^T, dK, dV) / query row (dQ)
-    const int key = kt * kT + tid;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl = a.scale * kLog2e;
     const uint32_t pt_addr = smem_u32(sPT), dst_addr = smem_u32(sdST);
-    // Per query row of tile i into buffer s: lse (log2 units) and
-    // delta * scale, delta = rowsum(dO * O). Issued one tile ahead so that the
-    // global loads overlap the previous tile's UMMAs.
-    auto load_row_stats = [&](int i, int s) {
+    const uint32_t stg = smem_u32(sStg) + (warp - 2) * 4096;
+    // Per query row of tile i of head bh into buffer s: lse (log2 units) and
+    // delta * scale, delta = rowsum(dO * O). Issued one tile ahead so that
+    // the global loads overlap the previous tile's UMMAs.
+    auto load_row_stats = [&](const BwdItem& w, int i, int s) {
       const int q = i * kT + tid;
       float dl = 0.f;
       if (q < a.T) {
-        const long off = static_cast<long>(row0 + q) * a.D + h * kHd;
+        const long off = static_cast<long>(w.row0 + q) * a.D + w.h * kHd;
 #pragma unroll
         for (int u = 0; u < kHd; u += 8) {
           const uint4 ov = *reinterpret_cast<const uint4*>(a.o + off + u);
@@ -446,106 +512,124 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
           }
         }
       }
-      sLse[s * kT + tid] = (q < a.T) ? a.lse[static_cast<long>(bh) * a.T + q] * kLog2e : INFINITY;
+      sLse[s * kT + tid] = (q < a.T) ? a.lse[static_cast<long>(w.bh) * a.T + q] * kLog2e : INFINITY;
       sDel[s * kT + tid] = dl * a.scale;
       __syncwarp();
       if (lane == 0) mbar_arrive(&stats_full[s]);
     };
-    // Buffer s is rewritten for tile it+2 only after this thread passed
-    // st_full(it+1), which the MMA warp commits after every warp's p_full(it):
-    // no reader of the tile-it values is left by then.
+    // Stats buffer s is rewritten for tile g+2 only after this thread passed
+    // st_full(g+1), which the MMA warp commits after every warp's p_full(g):
+    // no reader of the tile-g values is left by then.
     bool ok = true;
-    load_row_stats(kt, 0);
-    for (int it = 0; it < nq; ++it) {
-      const int s = it & 1, i = kt + it;
-      if (!mbar_wait(st_full, it & 1, a.err, abort_flag) ||
-          !mbar_wait(&stats_full[s], (it >> 1) & 1, a.err, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const float* lse2 = sLse + s * kT;
-      const float* del = sDel + s * kT;
-      // Causal mask (key <= query) matters only on the diagonal tile i == kt:
-      // there this warp's keys 32*quarter + lane see query chunk c (queries
-      // 32c..32c+31 of the tile) fully for c > quarter, not at all for
-      // c < quarter (P = dS = 0), and for t >= lane when c == quarter.
-      const int cfirst = (i == kt) ? quarter : 0;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pp[16], pd[16];
-        if (c < cfirst) {
-#pragma unroll
-          for (int t = 0; t < 16; ++t) pp[t] = pd[t] = 0u;
-        } else {
-          uint32_t sv[32], dv[32];
-          tmem_ld32(tST + lane_base + c * 32, sv);
-          tmem_ld32(tdPT + lane_base + c * 32, dv);
-          tmem_wait_ld();
-          const bool part = (i == kt && c == quarter);
-#pragma unroll
-          for (int t = 0; t < 32; t += 4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(lse2 + c * 32 + t);
-            const float4 d4 = *reinterpret_cast<const float4*>(del + c * 32 + t);
-            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dl[4] = {d4.x, d4.y, d4.z, d4.w};
-            float p[4], d[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              p[u] = ex2_approx(fmaf(__uint_as_float(sv[t + u]), sl, -lv[u]));
-              if (part && t + u < lane) p[u] = 0.f;
-              d[u] = p[u] * fmaf(__uint_as_float(dv[t + u]), a.scale, -dl[u]);
-            }
-            pp[t >> 1] = pack_bf16x2(p[0], p[1]);
-            pp[(t >> 1) + 1] = pack_bf16x2(p[2], p[3]);
-            pd[t >> 1] = pack_bf16x2(d[0], d[1]);
-            pd[(t >> 1) + 1] = pack_bf16x2(d[2], d[3]);
-          }
+    uint32_t g = 0;
+    int j = 0;
+    if (static_cast<int>(blockIdx.x) < nitems) {
+      const BwdItem w0 = bwd_item(a, blockIdx.x);
+      load_row_stats(w0, w0.kt, 0);
+    }
+    for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++j) {
+      const BwdItem w = bwd_item(a, u);
+      const int key = w.kt * kT + tid;
+      for (int it = 0; it < w.nq; ++it, ++g) {
+        const int s = g & 1, i = w.kt + it;
+        if (!mbar_wait(st_full, g & 1, a.err, abort_flag) ||
+            !mbar_wait(&stats_full[s], (g >> 1) & 1, a.err, abort_flag)) {
+          ok = false;
+          break;
         }
-        store_row32(pt_addr, tid, c, pp);
-        store_row32(dst_addr, tid, c, pd);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      if (it + 1 < nq) load_row_stats(i + 1, s ^ 1);
-      // dQ tile partial: TMEM lane = query row of tile i
-      if (!mbar_wait(dq_full, it & 1, a.err, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t q0[32], q1[32];
-      tmem_ld32(tdQ + lane_base, q0);
-      tmem_ld32(tdQ + lane_base + 32, q1);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_empty);
-      // This warp's 32 query rows x 64 columns of dQ are added into the fp32
-      // accumulator with two bulk tensor reduce-adds (32 columns each). Rows
-      // past T hold exact zeros (their P and dS are zero).
-      {
-        const uint32_t slot0 = smem_u32(sStg) + (warp - 2) * 8192, slot1 = slot0 + 4096;
-        if (it > 0) {
+        tc_fence_after();
+        // this warp's rows of sPT held the previous item's dK / dV staging
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+        const float* lse2 = sLse + s * kT;
+        const float* del = sDel + s * kT;
+        // Causal mask (key <= query) matters only on the diagonal tile i == kt:
+        // there this warp's keys 32*quarter + lane see query chunk c (queries
+        // 32c..32c+31 of the tile) fully for c > quarter, not at all for
+        // c < quarter (P = dS = 0), and for t >= lane when c == quarter.
+        const int cfirst = (i == w.kt) ? quarter : 0;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pp[16], pd[16];
+          if (c < cfirst) {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) pp[t] = pd[t] = 0u;
+          } else {
+            uint32_t sv[32], dv[32];
+            tmem_ld32(tST + lane_base + c * 32, sv);
+            tmem_ld32(tdPT + lane_base + c * 32, dv);
+            tmem_wait_ld();
+            const bool part = (i == w.kt && c == quarter);
+#pragma unroll
+            for (int t = 0; t < 32; t += 4) {
+              const float4 l4 = *reinterpret_cast<const float4*>(lse2 + c * 32 + t);
+              const float4 d4 = *reinterpret_cast<const float4*>(del + c * 32 + t);
+              const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dl[4] = {d4.x, d4.y, d4.z, d4.w};
+              float p[4], d[4];
+#pragma unroll
+              for (int uu = 0; uu < 4; ++uu) {
+                p[uu] = ex2_approx(fmaf(__uint_as_float(sv[t + uu]), sl, -lv[uu]));
+                if (part && t + uu < lane) p[uu] = 0.f;
+                d[uu] = p[uu] * fmaf(__uint_as_float(dv[t + uu]), a.scale, -dl[uu]);
+              }
+              pp[t >> 1] = pack_bf16x2(p[0], p[1]);
+              pp[(t >> 1) + 1] = pack_bf16x2(p[2], p[3]);
+              pd[t >> 1] = pack_bf16x2(d[0], d[1]);
+              pd[(t >> 1) + 1] = pack_bf16x2(d[2], d[3]);
+            }
+          }
+          store_row32(pt_addr, tid, c, pp);
+          store_row32(dst_addr, tid, c, pd);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+        // lse / delta of the next query tile (of this item or the next one)
+        if (it + 1 < w.nq) {
+          load_row_stats(w, i + 1, s ^ 1);
+        } else if (u + static_cast<int>(gridDim.x) < nitems) {
+          const BwdItem wn = bwd_item(a, u + gridDim.x);
+          load_row_stats(wn, wn.kt, s ^ 1);
+        }
+        // dQ tile partial: TMEM lane = query row of tile i
+        if (!mbar_wait(dq_full, g & 1, a.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t q0[32], q1[32];
+        tmem_ld32(tdQ + lane_base, q0);
+        tmem_ld32(tdQ + lane_base + 32, q1);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_empty);
+        // This warp's 32 query rows x 64 columns of dQ are added into the fp32
+        // accumulator with two bulk tensor reduce-adds (32 columns each)
+        // through one 4 KB slot. Rows past T hold exact zeros (their P and dS
+        // are zero).
+        const int y = w.row0 + i * kT + quarter * 32;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
           if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
-        }
-        st_row128_sw(slot0, lane, q0);
-        st_row128_sw(slot1, lane, q1);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          const int y = row0 + i * kT + quarter * 32;
-          tma_reduce_add_2d(&tm_dq, slot0, h * kHd, y);
-          tma_reduce_add_2d(&tm_dq, slot1, h * kHd + 32, y);
-          bulk_commit();
+          st_row128_sw(stg, lane, half ? q1 : q0);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_2d(&tm_dq, stg, w.h * kHd + half * 32, y);
+            bulk_commit();
+          }
         }
       }
-    }
-    if (lane == 0) bulk_wait_all();
-    __syncwarp();
-    if (ok && mbar_wait(acc_full, 0, a.err, abort_flag)) {
+      if (!ok) break;
+      // dK / dV of this item: TMEM -> bf16 -> this warp's rows of sPT (dK in
+      // the first 16 KB atom, dV in the second) -> TMA stores clipped at T
+      if (!mbar_wait(acc_full, j & 1, a.err, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       uint32_t k0[32], k1[32], v0[32], v1[32];
       tmem_ld32(tdK + lane_base, k0);
@@ -553,34 +637,31 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
       tmem_ld32(tdV + lane_base, v0);
       tmem_ld32(tdV + lane_base + 32, v1);
       tmem_wait_ld();
-      if (key < a.T) {
-        __nv_bfloat16* dk = a.dqkv + static_cast<long>(row0 + key) * 3 * a.D + a.D + h * kHd;
-        __nv_bfloat16* dvp = dk + a.D;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+      uint32_t wk[32], wv[32];
 #pragma unroll
-        for (int u = 0; u < 32; u += 8) {
-          *reinterpret_cast<uint4*>(dk + u) =
-              make_uint4(pack_bf16x2(__uint_as_float(k0[u]), __uint_as_float(k0[u + 1])),
-                         pack_bf16x2(__uint_as_float(k0[u + 2]), __uint_as_float(k0[u + 3])),
-                         pack_bf16x2(__uint_as_float(k0[u + 4]), __uint_as_float(k0[u + 5])),
-                         pack_bf16x2(__uint_as_float(k0[u + 6]), __uint_as_float(k0[u + 7])));
-          *reinterpret_cast<uint4*>(dk + 32 + u) =
-              make_uint4(pack_bf16x2(__uint_as_float(k1[u]), __uint_as_float(k1[u + 1])),
-                         pack_bf16x2(__uint_as_float(k1[u + 2]), __uint_as_float(k1[u + 3])),
-                         pack_bf16x2(__uint_as_float(k1[u + 4]), __uint_as_float(k1[u + 5])),
-                         pack_bf16x2(__uint_as_float(k1[u + 6]), __uint_as_float(k1[u + 7])));
-          *reinterpret_cast<uint4*>(dvp + u) =
-              make_uint4(pack_bf16x2(__uint_as_float(v0[u]), __uint_as_float(v0[u + 1])),
-                         pack_bf16x2(__uint_as_float(v0[u + 2]), __uint_as_float(v0[u + 3])),
-                         pack_bf16x2(__uint_as_float(v0[u + 4]), __uint_as_float(v0[u + 5])),
-                         pack_bf16x2(__uint_as_float(v0[u + 6]), __uint_as_float(v0[u + 7])));
-          *reinterpret_cast<uint4*>(dvp + 32 + u) =
-              make_uint4(pack_bf16x2(__uint_as_float(v1[u]), __uint_as_float(v1[u + 1])),
-                         pack_bf16x2(__uint_as_float(v1[u + 2]), __uint_as_float(v1[u + 3])),
-                         pack_bf16x2(__uint_as_float(v1[u + 4]), __uint_as_float(v1[u + 5])),
-                         pack_bf16x2(__uint_as_float(v1[u + 6]), __uint_as_float(v1[u + 7])));
-        }
+      for (int t = 0; t < 16; ++t) {
+        wk[t] = pack_bf16x2(__uint_as_float(k0[2 * t]), __uint_as_float(k0[2 * t + 1]));
+        wk[16 + t] = pack_bf16x2(__uint_as_float(k1[2 * t]), __uint_as_float(k1[2 * t + 1]));
+        wv[t] = pack_bf16x2(__uint_as_float(v0[2 * t]), __uint_as_float(v0[2 * t + 1]));
+        wv[16 + t] = pack_bf16x2(__uint_as_float(v1[2 * t]), __uint_as_float(v1[2 * t + 1]));
+      }
+      const uint32_t sk = pt_addr + quarter * 4096, sv = pt_addr + 16384 + quarter * 4096;
+      st_row128_sw(sk, lane, wk);
+      st_row128_sw(sv, lane, wv);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int t0 = w.kt * kT + quarter * 32;
+        tma_store_3d(&tm_dkv, sk, a.D + w.h * kHd, t0, w.b);
+        tma_store_3d(&tm_dkv, sv, 2 * a.D + w.h * kHd, t0, w.b);
+        bulk_commit();
       }
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -642,10 +723,12 @@ int attention_bwd_tc(const void* qkv, const void* o, const void* dout, const flo
   const int D = sh.H * sh.Hd, N = sh.B * sh.T;
   float* dq_acc = ws;
   if (cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(N) * D * sizeof(float), s) != cudaSuccess) return 4;
-  alignas(64) CUtensorMap tq, td, tdq;
+  alignas(64) CUtensorMap tq, td, tdq, tdkv;
   if (!make_tma_2d_bf16(&tq, qkv, N, 3L * D, 3L * D, 64, kT)) return 2;
   if (!make_tma_2d_bf16(&td, dout, N, D, D, 64, kT)) return 2;
   if (!make_tma_2d_f32(&tdq, dq_acc, N, D, D, 32, 32)) return 2;
+  // dK / dV stores through a [B, T, 3D] view, clipped at T per batch element
+  if (!make_tma_3d_bf16(&tdkv, dqkv, 3L * D, sh.T, sh.B, 3L * D, static_cast<long>(sh.T) * 3 * D, 64, 32)) return 2;
   AttnArgs a{};
   a.B = sh.B;
   a.T = sh.T;
@@ -666,7 +749,8 @@ int attention_bwd_tc(const void* qkv, const void* o, const void* dout, const flo
       return 3;
     attr = true;
   }
-  attn_bwd_tc<<<sh.B * sh.H * a.ntiles, 192, kBwdSmem, s>>>(tq, td, tdq, a);
+  const int items = sh.B * sh.H * a.ntiles;
+  attn_bwd_tc<<<std::min(items, num_sms()), 192, kBwdSmem, s>>>(tq, td, tdq, tdkv, a);
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
   const long n = static_cast<long>(N) * D;
   const int blocks = static_cast<int>(std::min<long>((n / 4 + 255) / 256, 8L * num_sms()));

@@ -671,6 +671,24 @@ bool make_tma_2d_bf16(void* map, const void* base, long rows, long cols, long ld
   return make_map_bf16(static_cast<CUtensorMap*>(map), base, rows, cols, ld, box_cols, box_rows);
 }
 
+// 3-D tiled map over a [d2, d1, d0] bf16 tensor (d0 innermost, row strides
+// ld1 and ld2 elements), 128-byte swizzle; coordinates past d1 are clipped,
+// so a per-batch view stops stores at the end of each batch element.
+bool make_tma_3d_bf16(void* map, const void* base, long d0, long d1, long d2, long ld1, long ld2, int box0,
+                      int box1) {
+  auto fn = get_encode_fn();
+  if (!fn || !base) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || ((ld1 * 2) & 15) != 0 || ((ld2 * 2) & 15) != 0) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld1 * 2), static_cast<cuuint64_t>(ld2 * 2)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(static_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool make_tma_2d_f32(void* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows) {
   return make_map(static_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, ld, box_cols,
                   box_rows);

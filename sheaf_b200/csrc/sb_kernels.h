@@ -56,5 +56,7 @@ int num_sms();
 // `map` points at a CUtensorMap (64-byte aligned storage).
 bool make_tma_2d_bf16(void* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows);
 bool make_tma_2d_f32(void* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows);
+bool make_tma_3d_bf16(void* map, const void* base, long d0, long d1, long d2, long ld1, long ld2, int box0,
+                      int box1);
 
 }  // namespace sb
