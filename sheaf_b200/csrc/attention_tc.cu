@@ -7,8 +7,10 @@
 // autodiff/reverse.rs:585-689, 551-583, 1014-1019, 814-828).
 // Masked scores contribute exp(-1e10 - max) == 0, so masked keys are skipped.
 //
-// Forward, one CTA per (batch, head, 128-query tile); 192 threads:
-//   warp 0    TMA: Q tile once, K/V tiles of 128 keys (one slot each)
+// Forward, persistent over (batch, head, 128-query tile) items, two CTAs per
+// SM; 192 threads:
+//   warp 0    TMA: Q tile per item (two slots), K/V tiles of 128 keys (one
+//             slot each)
 //   warp 1    TMEM owner + single-thread UMMA issuer:
 //             S = Q K^T (M=128, N=128, K=64) into TMEM;
 //             O_j = P V (M=128, N=64, K=128) into TMEM
@@ -79,39 +81,49 @@ __device__ __forceinline__ uint64_t mndesc(uint32_t tile, int kk, uint32_t lbo) 
 // forward
 // ---------------------------------------------------------------------------
 
-constexpr size_t kFwdSmem = 1024 + kTileBytes /*Q*/ + kTileBytes /*K*/ + kTileBytes /*V*/ +
+constexpr size_t kFwdSmem = 1024 + 2 * kTileBytes /*Q x2*/ + kTileBytes /*K*/ + kTileBytes /*V*/ +
                             2 * kTileBytes /*P*/ + 16 * 8 + 16;
 
-// ~82 KB of shared memory and 256 TMEM columns: two CTAs per SM, so one CTA's
-// softmax overlaps the other's loads and UMMAs.
+// Forward work item u: query tile qt = ntiles - 1 - u / (B*H) (long rows
+// first), head bh = u % (B*H).
+__device__ __forceinline__ void fwd_item(const AttnArgs& a, int u, int& qt, int& bh, int& h, int& row0) {
+  const int bhn = a.B * a.H;
+  qt = a.ntiles - 1 - u / bhn;
+  bh = u % bhn;
+  h = bh % a.H;
+  row0 = (bh / a.H) * a.T;
+}
+
+// ~98 KB of shared memory and 256 TMEM columns: two CTAs per SM, so one CTA's
+// softmax overlaps the other's loads and UMMAs. Persistent over (batch, head,
+// query-tile) items: Q is double buffered and the K / V slots and every
+// barrier phase continue across items, so the next item's loads overlap the
+// current item's softmax.
 __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = sm;
-  uint8_t* sK = sQ + kTileBytes;
+  uint8_t* sQ = sm;  // [2]
+  uint8_t* sK = sQ + 2 * kTileBytes;
   uint8_t* sV = sK + kTileBytes;
   uint8_t* sP = sV + kTileBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kTileBytes);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 2;
-  uint64_t* v_full = bars + 3;
-  uint64_t* v_empty = bars + 4;
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* o_full = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* q_full = bars + 0;   // [2]
+  uint64_t* q_empty = bars + 2;  // [2]
+  uint64_t* k_full = bars + 4;
+  uint64_t* k_empty = bars + 5;
+  uint64_t* v_full = bars + 6;
+  uint64_t* v_empty = bars + 7;
+  uint64_t* s_full = bars + 8;
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_full = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = a.ntiles - 1 - static_cast<int>(blockIdx.x % a.ntiles);  // long rows first
-  const int bh = blockIdx.x / a.ntiles;
-  const int b = bh / a.H, h = bh % a.H;
-  const int nkv = qt + 1;
-  const int row0 = b * a.T;
+  const int nitems = a.B * a.H * a.ntiles;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 8; ++i) mbar_init(&bars[i], i == 6 ? 4 : 1);
+    for (int i = 0; i < 11; ++i) mbar_init(&bars[i], i == 9 ? 4 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -127,38 +139,74 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
   const uint32_t tS = tmem, tO = tmem + 128;
 
   if (warp == 0) {
-    // K_j is reloaded once S_{j-1} has consumed the single K slot, V_j once
-    // P_{j-1} V_{j-1} has consumed the V slot; both land during softmax.
+    // K_c is reloaded once S_{c-1} has consumed the single K slot, V_c once
+    // P_{c-1} V_{c-1} has consumed the V slot (c counts key tiles across
+    // items); both land during softmax.
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      tma_load_2d(sQ, &tm, q_full, h * kHd, row0 + qt * kT);
-      for (int j = 0; j < nkv; ++j) {
-        const uint32_t ph = (j & 1) ^ 1;
-        if (!mbar_wait(k_empty, ph, a.err, abort_flag)) break;
-        mbar_arrive_expect_tx(k_full, kTileBytes);
-        tma_load_2d(sK, &tm, k_full, a.D + h * kHd, row0 + j * kT);
-        if (!mbar_wait(v_empty, ph, a.err, abort_flag)) break;
-        mbar_arrive_expect_tx(v_full, kTileBytes);
-        tma_load_2d(sV, &tm, v_full, 2 * a.D + h * kHd, row0 + j * kT);
+      uint32_t c = 0;
+      int j = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++j) {
+        int qt, bh, h, row0;
+        fwd_item(a, u, qt, bh, h, row0);
+        const int qb = j & 1;
+        if (!mbar_wait(&q_empty[qb], ((j >> 1) & 1) ^ 1, a.err, abort_flag)) break;
+        mbar_arrive_expect_tx(&q_full[qb], kTileBytes);
+        tma_load_2d(sQ + qb * kTileBytes, &tm, &q_full[qb], h * kHd, row0 + qt * kT);
+        for (int kv = 0; kv <= qt; ++kv, ++c) {
+          const uint32_t ph = (c & 1) ^ 1;
+          if (!mbar_wait(k_empty, ph, a.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(k_full, kTileBytes);
+          tma_load_2d(sK, &tm, k_full, a.D + h * kHd, row0 + kv * kT);
+          if (!mbar_wait(v_empty, ph, a.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(v_full, kTileBytes);
+          tma_load_2d(sV, &tm, v_full, 2 * a.D + h * kHd, row0 + kv * kT);
+        }
+      }
+      // no UMMA commit may arrive on this CTA's barriers after it exits
+      if (ok) {
+        mbar_wait(k_empty, (c & 1) ^ 1, a.err, abort_flag);
+        mbar_wait(v_empty, (c & 1) ^ 1, a.err, abort_flag);
+        for (int i = 0; i < 2; ++i, ++j) mbar_wait(&q_empty[j & 1], ((j >> 1) & 1) ^ 1, a.err, abort_flag);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idS = make_idesc_bf16(128, 128, false, false);
       constexpr uint32_t idO = make_idesc_bf16(128, 64, false, true);
-      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+      const uint32_t p_addr = smem_u32(sP);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      if (mbar_wait(q_full, 0, a.err, abort_flag)) {
-        for (int j = 0; j < nkv; ++j) {
-          const uint32_t ph = j & 1;
-          if (!mbar_wait(k_full, ph, a.err, abort_flag)) break;
+      uint32_t c = 0;
+      int j = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++j) {
+        int qt, bh, h, row0;
+        fwd_item(a, u, qt, bh, h, row0);
+        const int qb = j & 1;
+        if (!mbar_wait(&q_full[qb], (j >> 1) & 1, a.err, abort_flag)) break;
+        const uint32_t q_addr = smem_u32(sQ + qb * kTileBytes);
+        for (int kv = 0; kv <= qt; ++kv, ++c) {
+          const uint32_t ph = c & 1;
+          if (!mbar_wait(k_full, ph, a.err, abort_flag)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) umma_f16(tS, kdesc(q_addr, kk), kdesc(k_addr, kk), idS, kk > 0);
           umma_commit(s_full);
           umma_commit(k_empty);
-          if (!mbar_wait(p_full, ph, a.err, abort_flag)) break;
-          if (!mbar_wait(v_full, ph, a.err, abort_flag)) break;
+          if (kv == qt) umma_commit(&q_empty[qb]);  // the item's last read of Q
+          if (!mbar_wait(p_full, ph, a.err, abort_flag) || !mbar_wait(v_full, ph, a.err, abort_flag)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) umma_f16(tO, kdesc2(p_addr, kk), mndesc(v_addr, kk, 8192), idO, kk > 0);
@@ -170,102 +218,108 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
   } else {
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int q = qt * kT + r;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl = a.scale * kLog2e;  // scores -> log2 units
-    float m = -INFINITY, l = 0.f;
-    float o[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) o[i] = 0.f;
     const uint32_t p_addr = smem_u32(sP);
+    uint32_t c = 0;
     bool ok = true;
-    for (int j = 0; j < nkv && ok; ++j) {
-      if (!mbar_wait(s_full, j & 1, a.err, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // Causal mask: only the diagonal tile (j == qt) has masked keys. There,
-      // chunk c (keys 32c..32c+31 of the tile) is fully visible to this warp's
-      // rows 32*quarter.. for c < quarter, fully masked for c > quarter, and
-      // masked above the diagonal (t > lane) for c == quarter.
-      const int clast = (j == qt) ? quarter : 3;
-      float mx = -INFINITY;  // over raw scores (sl > 0)
-#pragma unroll 1
-      for (int c = 0; c <= clast; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tS + lane_base + c * 32, v);
-        tmem_wait_ld();
-        if (j == qt && c == quarter) {
+    for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x) {
+      int qt, bh, h, row0;
+      fwd_item(a, u, qt, bh, h, row0);
+      const int q = qt * kT + r;
+      float m = -INFINITY, l = 0.f;
+      float o[64];
 #pragma unroll
-          for (int t = 0; t < 32; ++t)
-            if (t <= lane) mx = fmaxf(mx, __uint_as_float(v[t]));
-        } else {
-#pragma unroll
-          for (int t = 0; t < 32; ++t) mx = fmaxf(mx, __uint_as_float(v[t]));
+      for (int i = 0; i < 64; ++i) o[i] = 0.f;
+      for (int j = 0; j <= qt; ++j, ++c) {
+        if (!mbar_wait(s_full, c & 1, a.err, abort_flag)) {
+          ok = false;
+          break;
         }
-      }
-      const float mn = fmaxf(m, mx * sl);
-      const float corr = ex2_approx(m - mn);
-      float rs = 0.f;
+        tc_fence_after();
+        // Causal mask: only the diagonal tile (j == qt) has masked keys. There,
+        // chunk cc (keys 32cc..32cc+31 of the tile) is fully visible to this
+        // warp's rows 32*quarter.. for cc < quarter, fully masked for
+        // cc > quarter, and masked above the diagonal (t > lane) for
+        // cc == quarter.
+        const int clast = (j == qt) ? quarter : 3;
+        float mx = -INFINITY;  // over raw scores (sl > 0)
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-        if (c > clast) {
-#pragma unroll
-          for (int t = 0; t < 16; ++t) pk[t] = 0u;
-        } else {
+        for (int cc = 0; cc <= clast; ++cc) {
           uint32_t v[32];
-          tmem_ld32(tS + lane_base + c * 32, v);
+          tmem_ld32(tS + lane_base + cc * 32, v);
           tmem_wait_ld();
-          const bool part = (j == qt && c == quarter);
+          if (j == qt && cc == quarter) {
 #pragma unroll
-          for (int t = 0; t < 32; t += 2) {
-            float p0 = ex2_approx(fmaf(__uint_as_float(v[t]), sl, -mn));
-            float p1 = ex2_approx(fmaf(__uint_as_float(v[t + 1]), sl, -mn));
-            if (part) {
-              p0 = (t <= lane) ? p0 : 0.f;
-              p1 = (t + 1 <= lane) ? p1 : 0.f;
-            }
-            rs += p0 + p1;
-            pk[t >> 1] = pack_bf16x2(p0, p1);
+            for (int t = 0; t < 32; ++t)
+              if (t <= lane) mx = fmaxf(mx, __uint_as_float(v[t]));
+          } else {
+#pragma unroll
+            for (int t = 0; t < 32; ++t) mx = fmaxf(mx, __uint_as_float(v[t]));
           }
         }
-        store_row32(p_addr, r, c, pk);
-      }
-      l = l * corr + rs;
-      m = mn;
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      if (!mbar_wait(o_full, j & 1, a.err, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t v0[32], v1[32];
-      tmem_ld32(tO + lane_base, v0);
-      tmem_ld32(tO + lane_base + 32, v1);
-      tmem_wait_ld();
+        const float mn = fmaxf(m, mx * sl);
+        const float corr = ex2_approx(m - mn);
+        float rs = 0.f;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t pk[16];
+          if (cc > clast) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        o[i] = o[i] * corr + __uint_as_float(v0[i]);
-        o[32 + i] = o[32 + i] * corr + __uint_as_float(v1[i]);
-      }
-      tc_fence_before();
-    }
-    if (ok && q < a.T) {
-      const float inv = 1.f / l;
-      __nv_bfloat16* orow = a.out + static_cast<long>(row0 + q) * a.D + h * kHd;
+            for (int t = 0; t < 16; ++t) pk[t] = 0u;
+          } else {
+            uint32_t v[32];
+            tmem_ld32(tS + lane_base + cc * 32, v);
+            tmem_wait_ld();
+            const bool part = (j == qt && cc == quarter);
 #pragma unroll
-      for (int i = 0; i < 64; i += 8) {
-        uint4 pk = make_uint4(pack_bf16x2(o[i] * inv, o[i + 1] * inv), pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv),
-                              pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv), pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv));
-        *reinterpret_cast<uint4*>(orow + i) = pk;
+            for (int t = 0; t < 32; t += 2) {
+              float p0 = ex2_approx(fmaf(__uint_as_float(v[t]), sl, -mn));
+              float p1 = ex2_approx(fmaf(__uint_as_float(v[t + 1]), sl, -mn));
+              if (part) {
+                p0 = (t <= lane) ? p0 : 0.f;
+                p1 = (t + 1 <= lane) ? p1 : 0.f;
+              }
+              rs += p0 + p1;
+              pk[t >> 1] = pack_bf16x2(p0, p1);
+            }
+          }
+          store_row32(p_addr, r, cc, pk);
+        }
+        l = l * corr + rs;
+        m = mn;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+        if (!mbar_wait(o_full, c & 1, a.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t v0[32], v1[32];
+        tmem_ld32(tO + lane_base, v0);
+        tmem_ld32(tO + lane_base + 32, v1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          o[i] = o[i] * corr + __uint_as_float(v0[i]);
+          o[32 + i] = o[32 + i] * corr + __uint_as_float(v1[i]);
+        }
+        tc_fence_before();
       }
-      // natural-log log-sum-exp of the scaled scores
-      a.lse[static_cast<long>(bh) * a.T + q] = (m + log2f(l)) / kLog2e;
+      if (ok && q < a.T) {
+        const float inv = 1.f / l;
+        __nv_bfloat16* orow = a.out + static_cast<long>(row0 + q) * a.D + h * kHd;
+#pragma unroll
+        for (int i = 0; i < 64; i += 8) {
+          uint4 pk = make_uint4(pack_bf16x2(o[i] * inv, o[i + 1] * inv), pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv),
+                                pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv), pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv));
+          *reinterpret_cast<uint4*>(orow + i) = pk;
+        }
+        // natural-log log-sum-exp of the scaled scores
+        a.lse[static_cast<long>(bh) * a.T + q] = (m + log2f(l)) / kLog2e;
+      }
     }
   }
 
@@ -710,7 +764,7 @@ int attention_fwd_tc(const void* qkv, void* o, float* lse, const AttnShape& sh, 
       return 3;
     attr = true;
   }
-  attn_fwd_tc<<<sh.B * sh.H * a.ntiles, 192, kFwdSmem, s>>>(tm, a);
+  attn_fwd_tc<<<std::min(sh.B * sh.H * a.ntiles, 2 * num_sms()), 192, kFwdSmem, s>>>(tm, a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 

@@ -142,7 +142,7 @@ def _attn_ref(qkv, B, T, H, Hd):
 
 @pytest.mark.parametrize("kind", ["f32", "bf16"])
 @pytest.mark.parametrize("B,T,H,Hd", [(2, 256, 2, 64), (1, 100, 3, 64), (2, 128, 4, 32), (1, 1024, 2, 64),
-                                     (1, 300, 2, 64), (16, 300, 4, 64)])
+                                     (1, 300, 2, 64), (24, 300, 6, 64)])
 def test_attention(kind, B, T, H, Hd, cuda):
     import torch
     import sheaf_b200 as sb
