@@ -108,8 +108,7 @@ __global__ void __launch_bounds__(384, 1)
   constexpr uint32_t kTmemCols = tmem_cols_for(BN);
   constexpr int kRowsPerTile = PAIR ? 2 * kBM : kBM;
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "tile width must be 64, 128, 192 or 256");
-  static_assert(!PAIR || !B_MN || (BH % 64 == 0), "an MN-major B half is loaded in 64-column boxes");
-  static_assert(!PAIR || (BH % 8 == 0), "a B half covers whole 8-row swizzle atoms");
+  static_assert(!PAIR || (BH % 64 == 0), "pair tiles split B into 64-row halves");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -602,15 +601,6 @@ int launch_tc(const GemmDesc& d, const GemmArgs& args, void* out, long ldo, long
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
-// Pair tiles of width 192 exist for K-major B only (the 96-row B half is one
-// TMA box; an MN-major half would need 64-column boxes).
-template <int STAGES>
-int dispatch_pair192(const GemmDesc& d, const GemmArgs& a, void* out, long ldo, long rows, int grid, cudaStream_t s) {
-  if (d.b_mn) return 6;
-  if (!d.a_mn) return launch_tc<192, false, false, STAGES, true>(d, a, out, ldo, rows, grid, s);
-  return launch_tc<192, true, false, STAGES, true>(d, a, out, ldo, rows, grid, s);
-}
-
 template <int BN, int STAGES, bool PAIR>
 int dispatch_major(const GemmDesc& d, const GemmArgs& a, void* out, long ldo, long rows, int grid, cudaStream_t s) {
   if (!d.a_mn && !d.b_mn) return launch_tc<BN, false, false, STAGES, PAIR>(d, a, out, ldo, rows, grid, s);
@@ -643,9 +633,10 @@ Plan plan_for(const GemmDesc& d) {
       }
     }
   }
-  // 256-row tiles on CTA pairs whenever the B tile splits into halves the
-  // loads can describe and there are at least 256 rows
-  p.pair = (p.bn == 256 || p.bn == 128 || (p.bn == 192 && !d.b_mn)) && d.M >= 2 * kBM && d.pair != 0;
+  // 256-row tiles on CTA pairs for tiles 256 or 128 wide (192-wide pair tiles
+  // measured slower in the step) when padding M to 256 rows wastes little
+  // (M = 384 would run 512 rows: a third more work per SM than 128-row tiles)
+  p.pair = (p.bn == 256 || p.bn == 128) && d.pair != 0 && (d.M % (2 * kBM) == 0 || d.M >= 4096);
   p.rows_per_tile = p.pair ? 2 * kBM : kBM;
   p.m_tiles = (d.M + p.rows_per_tile - 1) / p.rows_per_tile;
   p.n_tiles = (d.N + p.bn - 1) / p.bn;
@@ -757,10 +748,7 @@ int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaS
       rc = p.pair ? dispatch_major<256, 5, true>(d, a, out, ldo, rows, grid, s)
                   : dispatch_major<256, 4, false>(d, a, out, ldo, rows, grid, s);
       break;
-    case 192:
-      rc = p.pair ? dispatch_pair192<5>(d, a, out, ldo, rows, grid, s)
-                  : dispatch_major<192, 4, false>(d, a, out, ldo, rows, grid, s);
-      break;
+    case 192: rc = dispatch_major<192, 4, false>(d, a, out, ldo, rows, grid, s); break;
     case 128:
       rc = p.pair ? dispatch_major<128, 6, true>(d, a, out, ldo, rows, grid, s)
                   : dispatch_major<128, 5, false>(d, a, out, ldo, rows, grid, s);
