@@ -13,7 +13,10 @@ token ids uniform in [0, 65), mirroring init-gpt-params and random-randint.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sheaf_b200|reference]
 
-Prints one JSON line on rank 0.
+Prints one JSON line on rank 0. `--sample` instead times autoregressive
+sampling (generate-token + slide-window, 256 new tokens from a one-token
+prompt, batch 1 and 32, bf16, temperature 1.0 over the whole vocabulary) on
+one GPU and prints one line per batch size.
 """
 from __future__ import annotations
 
@@ -402,15 +405,92 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="primitive op sweep (one JSON line per op)")
     ap.add_argument("--op", default=None, help="run only this op of the sweep (e.g. gemm_bf16_8192)")
+    ap.add_argument("--sample", action="store_true", help="autoregressive sampling tokens/s (1 GPU)")
     args = ap.parse_args()
     if args.sweep or args.op:
         sweep_ops(args.op, reps=args.steps if args.op else 10)
+        return
+    if args.sample:
+        bench_sample(args)
         return
     world, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, world, rank)
         return
     bench_b200(args, world, rank, local)
+
+
+def bench_sample(args, n_new: int = 256):
+    """Generated tokens/s of the sampling module: each call decodes n_new
+    tokens for every sequence, each token one full-window forward (batch x
+    256 positions) plus the on-device top-k / softmax / choice."""
+    import torch
+
+    from sheaf_b200.runtime import Session
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda:0")
+    c = {k: v for k, v in CFG.items() if k not in ("batch", "seq")}
+    leaves, _, _ = synthetic_inputs(1234)
+    steps = max(1, min(args.steps, 10))
+    for batch in (1, 32):
+        s = Session(0)
+        s.create_gpt_sampler("gen", **c, batch=batch, n_new=n_new, top_k=c["vocab_size"], temperature=1.0,
+                             elem=BF16)
+        rng = np.random.default_rng(7)
+        ids = np.zeros((batch, c["block_size"]), np.float32)
+        ids[:, -1] = rng.integers(0, c["vocab_size"], batch)  # encode-prompt of a one-token prompt
+        # (random-key b) for sequence b: words (b, 0) as four 16-bit limbs
+        keys = np.zeros((batch, 4), np.float32)
+        keys[:, 0] = np.arange(batch) & 0xFFFF
+        keys[:, 1] = np.arange(batch) >> 16
+        inputs = [s.upload(l, BF16) for l in leaves] + [s.upload(ids, F32), s.upload(keys, F32)]
+        st = torch.cuda.ExternalStream(s.stream, device=dev)
+        for _ in range(max(args.warmup, 3)):
+            outs = s.call("gen.generate", inputs)
+        del outs
+        s.synchronize()
+        k0 = s.stats()["kernel_launches"]
+        events = []
+        with ClockSampler(0) as clk:
+            with torch.cuda.stream(st):
+                for _ in range(steps):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    outs = s.call("gen.generate", inputs)
+                    e1.record(st)
+                    events.append((e0, e1))
+                    del outs
+                s.synchronize()
+                torch.cuda.synchronize(dev)
+        launches = s.stats()["kernel_launches"] - k0
+        ms = sum(a.elapsed_time(b) for a, b in events)
+        # e2e: prompt window and keys from host, generated tokens back to host
+        pin = torch.from_numpy(ids).pin_memory().numpy()
+        s.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            inputs[-2].write(pin)
+            outs = s.call("gen.generate", inputs)
+            _ = outs[0].to_host()
+            del outs
+        e2e_s = time.perf_counter() - t0
+        gen = batch * n_new * steps
+        line = {
+            "metric": "nanoGPT sampling tokens/sec", "value": gen / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+            "steps": steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / steps, "higher_is_better": True,
+            "scaling": "none", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"nanoGPT-char generate 6L/6H/384 window 256 V=65, batch {batch}, "
+                                   f"{n_new} new tokens from a 1-token prompt, temperature 1.0, top_k = vocab",
+                       "ms_per_token": ms / steps / n_new, "l2": "not flushed (weights stay L2-resident across "
+                                                              "tokens, as in real decoding)"},
+            "clocks": clk.summary(), "gpu_launches": int(launches),
+            "e2e": {"value": gen / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(ids.nbytes),
+                    "d2h_bytes_per_step": batch * n_new * 4},
+        }
+        print(json.dumps(line), flush=True)
+        del inputs
+        s.close()
 
 
 def bench_b200(args, world, rank, local):

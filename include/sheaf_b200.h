@@ -157,6 +157,27 @@ typedef struct sb_adamw_config {
 SB_API sb_status sb_module_create_gpt_train(sb_session* session, const char* module_name,
                                             const sb_gpt_config* config, const sb_adamw_config* adamw);
 
+/* Registers the nanoGPT sampling module: generate-token of
+ * examples/nanogpt/model.shf:116-125 repeated n_new times with the window
+ * update of examples/nanogpt/sample.shf:28-45 (slide-window, key threading).
+ * Each token runs the full-window forward (batch x block_size), takes the last
+ * position's logits / temperature, top_k(min(top_k, vocab)), softmax,
+ * random-split(key) and choice (sheaf/src/lowering/stablehlo/random_ops.rs:
+ * 164-180), then appends the token and drops the oldest id. Sequence b uses
+ * row b of ids and keys; with batch 1 this is the reference's generate.
+ * config->seq must equal config->block_size and vocab_size must be <= 4096.
+ * Function "generate": inputs are the parameter leaves in sorted-key order,
+ * ids [batch, block_size] f32 and keys [batch, 4] f32 (four 16-bit limbs per
+ * key, sheaf/src/core/prng.rs:29-40). Outputs: tokens [batch, n_new], the
+ * final ids, the final keys and the last-position logits of every step
+ * [n_new, batch, vocab] (all f32). */
+typedef struct sb_sampler_config {
+  int32_t n_new, top_k;
+  float temperature;
+} sb_sampler_config;
+SB_API sb_status sb_module_create_gpt_sampler(sb_session* session, const char* module_name,
+                                              const sb_gpt_config* config, const sb_sampler_config* sampler);
+
 /* ---- invocation (replaces iree_runtime_session_call_by_name,
  *      iree_session.rs:576-583) ----
  * `qualified_name` is "<module>.<function>" (iree_dispatch.rs:95-104,172).

@@ -31,6 +31,11 @@ class AdamwConfig(C.Structure):
                 ("max_norm", C.c_float)]
 
 
+class SamplerConfig(C.Structure):
+    """sb_sampler_config (include/sheaf_b200.h)."""
+    _fields_ = [("n_new", C.c_int32), ("top_k", C.c_int32), ("temperature", C.c_float)]
+
+
 class SessionStats(C.Structure):
     """sb_session_stats (include/sheaf_b200.h)."""
     _fields_ = [("calls", C.c_uint64), ("graph_captures", C.c_uint64), ("graph_replays", C.c_uint64),
@@ -97,6 +102,7 @@ SIGNATURES: dict[str, tuple] = {
     "sb_module_load_stablehlo": (_P, [_P, C.c_char_p, C.c_size_t, C.POINTER(C.c_char_p)]),
     "sb_module_create_gpt_vag": (_P, [_P, C.c_char_p, C.POINTER(GptConfig)]),
     "sb_module_create_gpt_train": (_P, [_P, C.c_char_p, C.POINTER(GptConfig), C.POINTER(AdamwConfig)]),
+    "sb_module_create_gpt_sampler": (_P, [_P, C.c_char_p, C.POINTER(GptConfig), C.POINTER(SamplerConfig)]),
     "sb_module_describe": (_P, [_P, C.c_char_p, C.c_char_p, C.c_size_t]),
     "sb_stablehlo_validate": (_P, [C.c_char_p, C.c_size_t, C.c_char_p, C.c_size_t]),
     "sb_call": (_P, [_P, C.c_char_p, C.POINTER(_P), C.c_size_t, C.POINTER(_P), C.c_size_t, C.POINTER(C.c_size_t)]),

@@ -105,13 +105,23 @@ class GptVagModule : public Module {
   float* opt_ws = nullptr;
   size_t opt_ws_bytes = 0;
 
-  // one captured graph per function: [0] value_and_grad, [1] train_step
-  cudaGraphExec_t exec = nullptr;
-  cudaGraphExec_t exec_train = nullptr;
-  uint64_t kernels_per_step = 0;  // kernel nodes of the captured step graph
-  uint64_t kernels_per_train = 0;
-  int eager_runs = 0;
-  int eager_train = 0;
+  // sampling (generate): keys [B, 4], tokens [B, n_new], the device step
+  // counter and the last-position logits of every step [n_new, B, V]
+  bool sampler = false;
+  int n_new = 0, top_k = 0;
+  float temperature = 1.f;
+  float* keys_buf = nullptr;
+  float* tokens_buf = nullptr;
+  int* step_ctr = nullptr;
+  float* step_logits = nullptr;
+  size_t gen_tok = 0, gen_ids = 0, gen_keys = 0, gen_logits = 0, gen_bytes = 0;
+
+  // one captured graph per function (value_and_grad, train_step, one token
+  // of generate), its kernel nodes and the eager runs before the capture
+  enum Mode { kVag, kTrain, kSample, kModes };
+  cudaGraphExec_t exec[kModes] = {};
+  uint64_t kernels[kModes] = {};
+  int eager[kModes] = {};
   bool use_graph = true;
   std::vector<cudaEvent_t> bucket_events;
   cudaEvent_t comm_done = nullptr;
@@ -119,10 +129,10 @@ class GptVagModule : public Module {
   ~GptVagModule() override { teardown(); }
 
   void teardown() override {
-    if (exec) cudaGraphExecDestroy(exec);
-    exec = nullptr;
-    if (exec_train) cudaGraphExecDestroy(exec_train);
-    exec_train = nullptr;
+    for (auto& e : exec) {
+      if (e) cudaGraphExecDestroy(e);
+      e = nullptr;
+    }
     for (auto e : bucket_events) cudaEventDestroy(e);
     bucket_events.clear();
     if (comm_done) cudaEventDestroy(comm_done);
@@ -132,7 +142,7 @@ class GptVagModule : public Module {
   }
 
   bool has_function(const std::string& fn) const override {
-    return fn == "value_and_grad" || (train && fn == "train_step");
+    return fn == "value_and_grad" || (train && fn == "train_step") || (sampler && fn == "generate");
   }
 
   void* Pp(int i) const { return params + offs[i]; }
@@ -192,7 +202,8 @@ class GptVagModule : public Module {
     return v;
   }
 
-  sb_status build(const std::string& nm, const GptShape& shape, const AdamwConfig* adamw) {
+  sb_status build(const std::string& nm, const GptShape& shape, const AdamwConfig* adamw,
+                  const SamplerConfig* smp) {
     name = nm;
     g = shape;
     SB_RETURN_IF(g.elem != SB_ELEM_BF16 && g.elem != SB_ELEM_F32, SB_STATUS_INVALID_ARGUMENT,
@@ -321,6 +332,25 @@ class GptVagModule : public Module {
       opt_ws_bytes = align256(optimizer_workspace_bytes(cnt.data(), static_cast<int>(cnt.size())));
       SB_TRY(devt(opt_ws_bytes / 4 + 64, &opt_ws));
     }
+    if (smp) {
+      SB_RETURN_IF(smp->n_new <= 0 || smp->top_k <= 0 || !(smp->temperature > 0.f), SB_STATUS_INVALID_ARGUMENT,
+                   "sampler: n_new and top_k must be positive, temperature > 0");
+      SB_RETURN_IF(V > kSampleMaxVocab, SB_STATUS_UNIMPLEMENTED, "sampler: vocabulary larger than the on-device sort");
+      sampler = true;
+      n_new = smp->n_new;
+      top_k = smp->top_k;
+      temperature = smp->temperature;
+      SB_TRY(devt(static_cast<size_t>(B) * 4, &keys_buf));
+      SB_TRY(devt(static_cast<size_t>(B) * n_new, &tokens_buf));
+      SB_TRY(devt(64, &step_ctr));
+      SB_TRY(devt(static_cast<size_t>(n_new) * B * V, &step_logits));
+      // outputs of generate: tokens | ids | keys | step logits (all f32)
+      gen_tok = 0;
+      gen_ids = align256(gen_tok + static_cast<size_t>(B) * n_new * 4);
+      gen_keys = align256(gen_ids + static_cast<size_t>(N) * 4);
+      gen_logits = align256(gen_keys + static_cast<size_t>(B) * 16);
+      gen_bytes = align256(gen_logits + static_cast<size_t>(n_new) * B * V * 4);
+    }
     return nullptr;
   }
 
@@ -336,7 +366,8 @@ class GptVagModule : public Module {
 
   // Launches the whole fwd+VJP step on `st` (optionally with the gradient
   // all-reduce on the session's comm stream).
-  sb_status enqueue(Session& s, cudaStream_t st, bool train_step) {
+  sb_status enqueue(Session& s, cudaStream_t st, Mode mode) {
+    const bool train_step = mode == kTrain;
     int* err = s.err_word;
     const bool f32 = !bf;
     const bool dp = s.comm != nullptr && s.world > 1;
@@ -378,6 +409,11 @@ class GptVagModule : public Module {
     }
     SB_K(layernorm_fwd(xs[L], Pp(ilnf), f32, hf, f32, meanf, rstdf, N, D, st));
     SB_K(gemm(desc(hf, D, false, Pp(0), D, false, N, V, D, logits, ldl, f32), st, err));
+    if (mode == kSample) {
+      SB_K(sample_step(logits, f32, ldl, B, T, V, top_k, temperature, ids, keys_buf, tokens_buf, n_new, step_ctr,
+                       step_logits, st));
+      return nullptr;
+    }
     SB_K(cross_entropy_fwd_bwd(logits, f32, ldl, N, V, ids + N, dlogits, ldl, ws, loss_f32, nullptr, st));
 
     // ---- backward
@@ -506,6 +542,18 @@ class GptVagModule : public Module {
     return nullptr;
   }
 
+  // generate: leaves..., ids [batch, block], keys [batch, 4]
+  sb_status check_gen_inputs(const std::vector<Buffer*>& in) const {
+    const size_t n = shapes.size();
+    SB_RETURN_IF(in.size() != n + 2, SB_STATUS_INVALID_ARGUMENT,
+                 "generate expects " + std::to_string(n + 2) + " inputs, got " + std::to_string(in.size()));
+    for (size_t i = 0; i < n; ++i) SB_TRY(check_leaf(in[i], i, "leaf"));
+    SB_TRY(check_ids(in[n]));
+    SB_RETURN_IF(in[n + 1]->elem != SB_ELEM_F32 || in[n + 1]->shape != std::vector<int64_t>({B, 4}),
+                 SB_STATUS_INVALID_ARGUMENT, "keys must be f32 [batch, 4]");
+    return nullptr;
+  }
+
   using Seg = std::pair<const void*, std::pair<void*, size_t>>;
 
   // Copies every input into its plan-owned slot with batched-copy launches.
@@ -551,22 +599,32 @@ class GptVagModule : public Module {
     return copy_segs(s, segs, st);
   }
 
+  sb_status copy_in_gen(Session& s, const std::vector<Buffer*>& in, cudaStream_t st) {
+    const size_t n = shapes.size();
+    std::vector<Seg> segs;
+    for (size_t i = 0; i < n; ++i) segs.push_back({in[i]->data(), {Pp(static_cast<int>(i)), in[i]->bytes()}});
+    segs.push_back({in[n]->data(), {ids, static_cast<size_t>(N) * 4}});
+    segs.push_back({in[n + 1]->data(), {keys_buf, static_cast<size_t>(B) * 16}});
+    SB_TRY(copy_segs(s, segs, st));
+    SB_CUDA_TRY(cudaMemsetAsync(step_ctr, 0, sizeof(int), st));
+    return nullptr;
+  }
+
   // Runs the step: eagerly on the first call of a function, then from the
   // CUDA graph captured on the second.
-  sb_status run(Session& s, cudaStream_t st, bool train_step) {
-    cudaGraphExec_t& ex = train_step ? exec_train : exec;
-    uint64_t& kernels = train_step ? kernels_per_train : kernels_per_step;
-    int& eager = train_step ? eager_train : eager_runs;
-    const bool dp = s.comm != nullptr && s.world > 1;
-    if (!use_graph || eager < 1) {
-      SB_TRY(enqueue(s, st, train_step));
-      ++eager;
+  sb_status run(Session& s, cudaStream_t st, Mode mode) {
+    cudaGraphExec_t& ex = exec[mode];
+    uint64_t& nk = kernels[mode];
+    const bool dp = s.comm != nullptr && s.world > 1 && mode != kSample;
+    if (!use_graph || eager[mode] < 1) {
+      SB_TRY(enqueue(s, st, mode));
+      ++eager[mode];
       return nullptr;
     }
     if (!ex) {
       cudaGraph_t graph = nullptr;
       SB_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-      sb_status e = enqueue(s, st, train_step);
+      sb_status e = enqueue(s, st, mode);
       cudaError_t ce = cudaStreamEndCapture(st, &graph);
       if (e) {
         if (graph) cudaGraphDestroy(graph);
@@ -577,14 +635,14 @@ class GptVagModule : public Module {
       cudaGraphGetNodes(graph, nullptr, &nnodes);
       std::vector<cudaGraphNode_t> nodes(nnodes);
       cudaGraphGetNodes(graph, nodes.data(), &nnodes);
-      kernels = 0;
+      nk = 0;
       for (auto nd : nodes) {
         cudaGraphNodeType t;
-        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++nk;
       }
       // NCCL's own kernels (one per bucket all-reduce and one for the loss)
       // are not library kernels
-      if (dp) kernels -= std::min<uint64_t>(kernels, static_cast<uint64_t>(L) + 3);
+      if (dp) nk -= std::min<uint64_t>(nk, static_cast<uint64_t>(L) + 3);
       ce = cudaGraphInstantiate(&ex, graph, 0);
       cudaGraphDestroy(graph);
       if (ce != cudaSuccess) return make_status(SB_STATUS_INTERNAL, std::string("graph instantiate: ") + cudaGetErrorString(ce));
@@ -592,16 +650,39 @@ class GptVagModule : public Module {
     }
     SB_CUDA_TRY(cudaGraphLaunch(ex, st));
     s.graph_replays++;
-    s.kernel_launches += kernels;
+    s.kernel_launches += nk;
     return nullptr;
   }
 
   sb_status call(Session& s, const std::string& fn, const std::vector<Buffer*>& in,
                  std::vector<Buffer*>& out) override {
-    const bool train_step = fn == "train_step";
-    SB_RETURN_IF(fn != "value_and_grad" && !(train && train_step), SB_STATUS_NOT_FOUND, "unknown function " + fn);
-    SB_TRY(train_step ? check_train_inputs(in) : check_inputs(in));
+    SB_RETURN_IF(!has_function(fn), SB_STATUS_NOT_FOUND, "unknown function " + fn);
     cudaStream_t st = s.stream;
+    const int n = static_cast<int>(shapes.size());
+    Allocation* a = nullptr;
+    if (fn == "generate") {
+      // n_new tokens: the graph of one token (window forward + sampling) is
+      // replayed, the device step counter moving every replay along
+      SB_TRY(check_gen_inputs(in));
+      SB_TRY(copy_in_gen(s, in, st));
+      for (int i = 0; i < n_new; ++i) SB_TRY(run(s, st, kSample));
+      SB_TRY(session_alloc(s, gen_bytes, &a));
+      char* o = static_cast<char*>(a->ptr);
+      SB_CUDA_TRY(cudaMemcpyAsync(o + gen_tok, tokens_buf, static_cast<size_t>(B) * n_new * 4,
+                                  cudaMemcpyDeviceToDevice, st));
+      SB_CUDA_TRY(cudaMemcpyAsync(o + gen_ids, ids, static_cast<size_t>(N) * 4, cudaMemcpyDeviceToDevice, st));
+      SB_CUDA_TRY(cudaMemcpyAsync(o + gen_keys, keys_buf, static_cast<size_t>(B) * 16, cudaMemcpyDeviceToDevice, st));
+      SB_CUDA_TRY(cudaMemcpyAsync(o + gen_logits, step_logits, static_cast<size_t>(n_new) * B * V * 4,
+                                  cudaMemcpyDeviceToDevice, st));
+      a->refs.store(4);
+      out.push_back(buffer_new(s, a, gen_tok, {B, n_new}, SB_ELEM_F32));
+      out.push_back(buffer_new(s, a, gen_ids, {B, T}, SB_ELEM_F32));
+      out.push_back(buffer_new(s, a, gen_keys, {B, 4}, SB_ELEM_F32));
+      out.push_back(buffer_new(s, a, gen_logits, {n_new, B, V}, SB_ELEM_F32));
+      return nullptr;
+    }
+    const bool train_step = fn == "train_step";
+    SB_TRY(train_step ? check_train_inputs(in) : check_inputs(in));
     const bool dp = s.comm != nullptr && s.world > 1;
     if (dp && bucket_events.empty()) {
       for (int i = 0; i < L + 2; ++i) {
@@ -612,9 +693,7 @@ class GptVagModule : public Module {
       SB_CUDA_TRY(cudaEventCreateWithFlags(&comm_done, cudaEventDisableTiming));
     }
     SB_TRY(train_step ? copy_in_train(s, in, st) : copy_in(s, in, st));
-    SB_TRY(run(s, st, train_step));
-    const int n = static_cast<int>(shapes.size());
-    Allocation* a = nullptr;
+    SB_TRY(run(s, st, train_step ? kTrain : kVag));
     if (!train_step) {
       // outputs: one pool allocation holds every gradient and the loss
       SB_TRY(session_alloc(s, out_bytes, &a));
@@ -640,9 +719,9 @@ class GptVagModule : public Module {
 }  // namespace
 
 sb_status make_gpt_vag_module(Session& s, const std::string& name, const GptShape& g, std::unique_ptr<Module>* out,
-                              const AdamwConfig* adamw) {
+                              const AdamwConfig* adamw, const SamplerConfig* sampler) {
   auto m = std::make_unique<GptVagModule>();
-  sb_status st = m->build(name, g, adamw);
+  sb_status st = m->build(name, g, adamw, sampler);
   if (st) return st;
   *out = std::move(m);
   return nullptr;

@@ -306,6 +306,21 @@ sb_status sb_module_create_gpt_train(sb_session* s, const char* name, const sb_g
   return nullptr;
 }
 
+sb_status sb_module_create_gpt_sampler(sb_session* s, const char* name, const sb_gpt_config* c,
+                                       const sb_sampler_config* o) {
+  SB_RETURN_IF(!s || !name || !c || !o, SB_STATUS_INVALID_ARGUMENT, "null argument");
+  SB_RETURN_IF(c->seq != c->block_size, SB_STATUS_INVALID_ARGUMENT, "sampler: seq must equal block_size");
+  cudaSetDevice(s->device);
+  GptShape g{c->n_layer, c->n_head, c->n_embd, c->block_size, c->vocab_size, c->batch, c->seq, c->elem_type};
+  SamplerConfig sc{o->n_new, o->top_k, o->temperature};
+  std::unique_ptr<Module> m;
+  SB_TRY(make_gpt_vag_module(*s, name, g, &m, nullptr, &sc));
+  std::lock_guard<std::mutex> lk(s->mu);
+  if (auto it = s->modules.find(name); it != s->modules.end()) it->second->teardown();
+  s->modules[name] = std::move(m);
+  return nullptr;
+}
+
 sb_status sb_module_load_stablehlo(sb_session* s, const char* text, size_t len, const char** out_name) {
   SB_RETURN_IF(!s || !text, SB_STATUS_INVALID_ARGUMENT, "null argument");
   cudaSetDevice(s->device);

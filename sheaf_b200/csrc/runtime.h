@@ -107,10 +107,15 @@ struct GptShape {
 struct AdamwConfig {
   float b1, b2, eps, wd, max_norm;
 };
+struct SamplerConfig {
+  int n_new, top_k;
+  float temperature;
+};
 // With `adamw`, the module also runs the train-step function (VAG + clip +
-// AdamW in one graph).
+// AdamW in one graph); with `sampler`, the generate function (window forward
+// + top-k sampling per token, one graph replayed per token).
 sb_status make_gpt_vag_module(Session& s, const std::string& name, const GptShape& g, std::unique_ptr<Module>* out,
-                              const AdamwConfig* adamw = nullptr);
+                              const AdamwConfig* adamw = nullptr, const SamplerConfig* sampler = nullptr);
 
 // Parses StableHLO text and maps it onto the kernel library (stablehlo.cpp).
 sb_status load_stablehlo_module(Session& s, const char* text, size_t len, std::unique_ptr<Module>* out);

@@ -62,6 +62,16 @@ size_t attention_bwd_workspace_bytes(bool f32, const AttnShape& sh);
 int attention_bwd(const void* qkv, const void* o, const void* dout, const float* lse, bool f32, void* dqkv, float* ws,
                   const AttnShape& sh, cudaStream_t s);
 
+// One token of nanoGPT's generate-token for B sequences (window T, vocab V
+// at most kSampleMaxVocab): samples from the last position's logits
+// (row b*T + T-1, row stride ld), writes tokens[b * n_new + *step], advances
+// each sequence's key [B, 4] and its id window [B, T] in place, records the
+// raw last-position logits in step_logits [n_new, B, V] (optional) and
+// increments *step.
+constexpr int kSampleMaxVocab = 4096;
+int sample_step(const void* logits, bool logits_f32, long ld, int B, int T, int V, int top_k, float temperature,
+                float* ids, float* keys, float* tokens, int n_new, int* step, float* step_logits, cudaStream_t s);
+
 // Global gradient norm, and with `params` the clip-by-global-norm + AdamW
 // step of nanoGPT's train-step over n_leaves tensors of one element type
 // (pointer arrays on the host, tensors on the device). t_in, lr: device f32

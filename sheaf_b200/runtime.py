@@ -150,6 +150,17 @@ class Session:
         _check(lib().sb_module_create_gpt_train(self._h, name.encode(), C.byref(cfg), C.byref(opt)))
         return name
 
+    def create_gpt_sampler(self, name: str, *, n_layer, n_head, n_embd, block_size, vocab_size, batch,
+                           n_new, top_k=200, temperature=0.8, elem=ELEM_BF16) -> str:
+        """nanoGPT sampling module (generate-token + slide-window repeated
+        n_new times); the defaults are examples/nanogpt/sample.shf's top-k 200
+        and temperature 0.8. Function "generate": leaves, ids [batch,
+        block_size], keys [batch, 4] -> tokens, ids', keys', step logits."""
+        cfg = _lib.GptConfig(n_layer, n_head, n_embd, block_size, vocab_size, batch, block_size, elem)
+        smp = _lib.SamplerConfig(n_new, top_k, temperature)
+        _check(lib().sb_module_create_gpt_sampler(self._h, name.encode(), C.byref(cfg), C.byref(smp)))
+        return name
+
     def call(self, qualified_name: str, inputs: Sequence["Buffer"], max_outputs: int = 1024) -> list["Buffer"]:
         arr = (C.c_void_p * max(1, len(inputs)))(*[b._h for b in inputs])
         outs = (C.c_void_p * max_outputs)()
