@@ -34,6 +34,8 @@
 #include "sb_kernels.h"
 #include "sb_nn.h"
 #include "sb_ptx.cuh"
+#define SB_PDL_FAMILY 2
+#include "sb_launch.cuh"
 
 namespace sb {
 
@@ -128,6 +130,9 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) tma_prefetch_desc(&tm);
+  // inputs come from the preceding kernel: no global access, and no TMEM
+  // allocation, before this
+  pdl_wait();
   if (warp == 1) {
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
@@ -135,6 +140,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_trigger();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tO = tmem + 128;
 
@@ -423,6 +429,9 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
     tma_prefetch_desc(&tm_dq);
     tma_prefetch_desc(&tm_dkv);
   }
+  // inputs come from the preceding kernel: no global access, and no TMEM
+  // allocation, before this
+  pdl_wait();
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -430,6 +439,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_trigger();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tST = tmem, tdPT = tmem + 128, tdV = tmem + 256, tdK = tmem + 320, tdQ = tmem + 384;
 
@@ -728,6 +738,8 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
 
 // dq (bf16, columns [0, D) of dqkv) = dq_acc (f32 [N, D])
 __global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv, long n, int D) {
+  pdl_wait();
+  pdl_trigger();
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n / 4;
        i += static_cast<long>(gridDim.x) * blockDim.x) {
     const long e = i * 4, r = e / D, c = e % D;
@@ -764,7 +776,7 @@ int attention_fwd_tc(const void* qkv, void* o, float* lse, const AttnShape& sh, 
       return 3;
     attr = true;
   }
-  attn_fwd_tc<<<std::min(sh.B * sh.H * a.ntiles, 2 * num_sms()), 192, kFwdSmem, s>>>(tm, a);
+  launch_pdl(attn_fwd_tc, dim3(std::min(sh.B * sh.H * a.ntiles, 2 * num_sms())), dim3(192), kFwdSmem, s, tm, a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
@@ -804,11 +816,11 @@ int attention_bwd_tc(const void* qkv, const void* o, const void* dout, const flo
     attr = true;
   }
   const int items = sh.B * sh.H * a.ntiles;
-  attn_bwd_tc<<<std::min(items, num_sms()), 192, kBwdSmem, s>>>(tq, td, tdq, tdkv, a);
+  launch_pdl(attn_bwd_tc, dim3(std::min(items, num_sms())), dim3(192), kBwdSmem, s, tq, td, tdq, tdkv, a);
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
   const long n = static_cast<long>(N) * D;
   const int blocks = static_cast<int>(std::min<long>((n / 4 + 255) / 256, 8L * num_sms()));
-  dq_convert_kernel<<<blocks, 256, 0, s>>>(dq_acc, static_cast<__nv_bfloat16*>(dqkv), n, D);
+  launch_pdl(dq_convert_kernel, dim3(blocks), dim3(256), 0, s, dq_acc, static_cast<__nv_bfloat16*>(dqkv), n, D);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 

@@ -26,12 +26,24 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "sb_kernels.h"
+#define SB_PDL_FAMILY 0
+#include "sb_launch.cuh"
 #include "sb_ptx.cuh"
 
 namespace sb {
+
+int pdl_mask() {
+  static const int mask = [] {
+    const char* e = std::getenv("SHEAF_B200_PDL");
+    return e ? std::atoi(e) : 0x5;
+  }();
+  return mask;
+}
+
 
 namespace {
 
@@ -146,6 +158,9 @@ __global__ void __launch_bounds__(384, 1)
     tma_prefetch_desc(&tmC);
     tma_prefetch_desc(&tmC2);
   }
+  // operands come from the preceding kernel and the outputs may be its
+  // operands: no global access, and no TMEM allocation, before this
+  pdl_wait();
   if (warp == 1) {
     if constexpr (PAIR) {
       tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -161,6 +176,7 @@ __global__ void __launch_bounds__(384, 1)
   else
     __syncthreads();
   tc_fence_after();
+  pdl_trigger();
   const uint32_t tmem_base = *tmem_slot;
 
   const int tiles = a.m_tiles * a.n_tiles;
@@ -473,6 +489,8 @@ done:
 // per thread; the loads of all splits are issued ahead of the in-order adds.
 __global__ void splitk_reduce_kernel(const float4* __restrict__ ws, int splits, long slice4, int M, int nq, void* out,
                                      long ldo, int out_f32) {
+  pdl_wait();
+  pdl_trigger();
   const long total = static_cast<long>(M) * nq;
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long>(gridDim.x) * blockDim.x) {
@@ -587,16 +605,18 @@ int launch_tc(const GemmDesc& d, const GemmArgs& args, void* out, long ldo, long
     cfg.blockDim = dim3(384);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = pdl_mask() & 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     if (cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, tc2, args) != cudaSuccess) return 4;
   } else {
-    kern<<<grid, 384, smem, s>>>(ta, tb, tc, tc2, args);
+    if (launch_pdl(kern, dim3(grid), dim3(384), smem, s, ta, tb, tc, tc2, args) != cudaSuccess) return 4;
   }
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
@@ -761,11 +781,11 @@ int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaS
     const long total = static_cast<long>(d.M) * (d.N / 4);
     const int threads = 256;
     const int blocks = static_cast<int>(std::min<long>((total + threads - 1) / threads, 8L * num_sms()));
-    splitk_reduce_kernel<<<blocks, threads, 0, s>>>(reinterpret_cast<const float4*>(workspace), p.splits,
-                                                    static_cast<long>(p.m_tiles) * p.rows_per_tile * d.N / 4, d.M,
-                                                    d.N / 4, d.out,
-                                                    d.ldo, d.out_f32);
-    if (cudaPeekAtLastError() != cudaSuccess) return 4;
+    if (launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(threads), 0, s,
+                   reinterpret_cast<const float4*>(workspace), p.splits,
+                   static_cast<long>(p.m_tiles) * p.rows_per_tile * d.N / 4, d.M, d.N / 4, d.out, d.ldo,
+                   static_cast<int>(d.out_f32)) != cudaSuccess)
+      return 4;
   }
   return 0;
 }

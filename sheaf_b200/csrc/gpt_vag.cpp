@@ -126,6 +126,18 @@ class GptVagModule : public Module {
   std::vector<cudaEvent_t> bucket_events;
   cudaEvent_t comm_done = nullptr;
 
+  // bf16 backward: the weight-gradient GEMMs run on a low-priority side
+  // stream beside the critical path (dX GEMMs, layer-norm and attention
+  // VJPs), filling the SMs its tails leave idle. The operands they read are
+  // double-buffered (dres copy by writer, dU and dqkv by layer parity) so the
+  // critical path only waits for a dW GEMM before overwriting its operand.
+  bool dw_side = false;
+  cudaStream_t wst = nullptr;
+  float* ws_w = nullptr;  // split-K workspace of the side stream
+  size_t ws_w_bytes = 0;
+  void *dres_bf2 = nullptr, *du2 = nullptr, *dqkv2 = nullptr;
+  std::vector<cudaEvent_t> xev;
+
   ~GptVagModule() override { teardown(); }
 
   void teardown() override {
@@ -137,6 +149,10 @@ class GptVagModule : public Module {
     bucket_events.clear();
     if (comm_done) cudaEventDestroy(comm_done);
     comm_done = nullptr;
+    for (auto e : xev) cudaEventDestroy(e);
+    xev.clear();
+    if (wst) cudaStreamDestroy(wst);
+    wst = nullptr;
     for (void* p : owned) cudaFree(p);
     owned.clear();
   }
@@ -180,8 +196,10 @@ class GptVagModule : public Module {
     return d;
   }
 
-  int gemm(const GemmDesc& d, cudaStream_t st, int* err) const {
-    return bf ? gemm_bf16(d, ws, ws_bytes, st, err) : gemm_f32(d, ws, ws_bytes, st, err);
+  int gemm(const GemmDesc& d, cudaStream_t st, int* err, bool side = false) const {
+    float* w = side ? ws_w : ws;
+    const size_t wb = side ? ws_w_bytes : ws_bytes;
+    return bf ? gemm_bf16(d, w, wb, st, err) : gemm_f32(d, w, wb, st, err);
   }
 
   // All GEMMs of one step (used for workspace sizing).
@@ -312,6 +330,27 @@ class GptVagModule : public Module {
     ws_bytes = align256(w);
     SB_TRY(devt(ws_bytes / 4 + 64, &ws));
 
+    const char* side_env = std::getenv("SHEAF_B200_DW_STREAM");
+    dw_side = bf && !smp && !(side_env && std::string(side_env) == "0");
+    if (dw_side) {
+      int least = 0, greatest = 0;
+      SB_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+      SB_CUDA_TRY(cudaStreamCreateWithPriority(&wst, cudaStreamNonBlocking, least));
+      size_t w2 = 0;
+      for (auto& d : all_gemms())
+        if (d.K == N) w2 = std::max(w2, gemm_workspace_bytes(d, bf));  // the dW GEMMs contract over tokens
+      ws_w_bytes = align256(w2);
+      SB_TRY(devt(ws_w_bytes / 4 + 64, &ws_w));
+      SB_TRY(dev(nd * 2, &dres_bf2));
+      SB_TRY(dev(4 * nd * es, &du2));
+      SB_TRY(dev(3 * nd * es, &dqkv2));
+      for (int i = 0; i < 8 * L + 8; ++i) {
+        cudaEvent_t e;
+        SB_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        xev.push_back(e);
+      }
+    }
+
     if (adamw) {
       train = true;
       opt = *adamw;
@@ -424,42 +463,89 @@ class GptVagModule : public Module {
     SB_K(layernorm_bwd(dh, f32, xs[L], meanf, rstdf, Pp(ilnf), f32, dres, static_cast<__nv_bfloat16*>(dres_bf),
                        Gp(ilnf), f32, ws, N, D, st));
     int bucket = 0;
-    auto launch_bucket = [&](size_t lo_off, size_t hi_off) -> sb_status {
+    // the all-reduce of a bucket waits for the main stream and, when given,
+    // a side-stream mark
+    auto launch_bucket = [&](size_t lo_off, size_t hi_off, cudaEvent_t side_ev) -> sb_status {
       if (!dp) return nullptr;
       cudaEvent_t ev = bucket_events[bucket++];
       SB_CUDA_TRY(cudaEventRecord(ev, st));
       SB_CUDA_TRY(cudaStreamWaitEvent(s.comm_stream, ev, 0));
+      if (side_ev) SB_CUDA_TRY(cudaStreamWaitEvent(s.comm_stream, side_ev, 0));
       return comm_allreduce_avg(s, grads + lo_off, (hi_off - lo_off) / es, g.elem, s.comm_stream);
     };
-    SB_TRY(launch_bucket(offs[0], offs[1]));
-    const void* opnd = bf ? dres_bf : static_cast<void*>(dres);
+    SB_TRY(launch_bucket(offs[0], offs[1], nullptr));
+
+    // Weight gradients go to the side stream (in line when there is none).
+    cudaStream_t sst = dw_side ? wst : st;
+    int nev = 0;
+    auto fork = [&]() -> sb_status {  // the side stream waits for the main stream's work so far
+      if (!dw_side) return nullptr;
+      cudaEvent_t e = xev[nev++];
+      SB_CUDA_TRY(cudaEventRecord(e, st));
+      SB_CUDA_TRY(cudaStreamWaitEvent(wst, e, 0));
+      return nullptr;
+    };
+    auto mark = [&](cudaEvent_t& e) -> sb_status {  // a point on the side stream
+      if (!dw_side) return nullptr;
+      e = xev[nev++];
+      SB_CUDA_TRY(cudaEventRecord(e, wst));
+      return nullptr;
+    };
+    auto wait = [&](cudaEvent_t e) -> sb_status {  // the main stream waits for a side-stream point
+      if (dw_side && e) SB_CUDA_TRY(cudaStreamWaitEvent(st, e, 0));
+      return nullptr;
+    };
+    // dres operand of the GEMMs: r0 is written by LN_f / LN1 VJPs, r1 by LN2's
+    const void* r0 = bf ? dres_bf : static_cast<void*>(dres);
+    const void* r1 = dw_side ? dres_bf2 : r0;
+    auto bf_out = [&](const void* p) { return bf ? static_cast<__nv_bfloat16*>(const_cast<void*>(p)) : nullptr; };
+    std::vector<cudaEvent_t> ev_fc2(L, nullptr), ev_fc(L, nullptr), ev_proj(L, nullptr), ev_qkv(L, nullptr);
     for (int l = L - 1; l >= 0; --l) {
       const int b0 = 1 + 6 * l;
-      SB_K(gemm(desc(opnd, D, true, gact[l], 4 * D, true, D, 4 * D, N, Gp(b0 + 5), 4 * D, f32), st, err));
+      void* dul = (dw_side && (l & 1)) ? du2 : du;
+      void* dql = (dw_side && (l & 1)) ? dqkv2 : dqkv;
+      SB_TRY(fork());
+      SB_K(gemm(desc(r0, D, true, gact[l], 4 * D, true, D, 4 * D, N, Gp(b0 + 5), 4 * D, f32), sst, err, dw_side));
+      SB_TRY(mark(ev_fc2[l]));
+      if (l + 2 < L) SB_TRY(wait(ev_fc[l + 2]));  // dU buffer last read by dW_fc two layers up
       {
-        GemmDesc d = desc(opnd, D, false, Pp(b0 + 5), 4 * D, true, N, 4 * D, D, du, 4 * D, f32);
+        GemmDesc d = desc(r0, D, false, Pp(b0 + 5), 4 * D, true, N, 4 * D, D, dul, 4 * D, f32);
         d.epi = EPI_MUL;
         d.aux = gder[l];
         d.ldaux = 4 * D;
         d.aux_f32 = f32;
         SB_K(gemm(d, st, err));
       }
-      SB_K(gemm(desc(du, 4 * D, true, h2[l], D, true, 4 * D, D, N, Gp(b0 + 4), D, f32), st, err));
-      SB_K(gemm(desc(du, 4 * D, false, Pp(b0 + 4), D, true, N, D, 4 * D, dh, D, f32), st, err));
-      SB_K(layernorm_bwd(dh, f32, xmid[l], mean2[l], rstd2[l], Pp(b0 + 3), f32, dres,
-                         static_cast<__nv_bfloat16*>(dres_bf), Gp(b0 + 3), f32, ws, N, D, st));
-      SB_K(gemm(desc(opnd, D, true, att[l], D, true, D, D, N, Gp(b0 + 1), D, f32), st, err));
-      SB_K(gemm(desc(opnd, D, false, Pp(b0 + 1), D, true, N, D, D, dout, D, f32), st, err));
-      SB_K(attention_bwd(qkv[l], att[l], dout, lse[l], f32, dqkv, ws, ash, st));
-      SB_K(gemm(desc(dqkv, 3 * D, true, h1[l], D, true, 3 * D, D, N, Gp(b0 + 0), D, f32), st, err));
-      SB_K(gemm(desc(dqkv, 3 * D, false, Pp(b0 + 0), D, true, N, D, 3 * D, dh, D, f32), st, err));
-      SB_K(layernorm_bwd(dh, f32, xs[l], mean1[l], rstd1[l], Pp(b0 + 2), f32, dres,
-                         static_cast<__nv_bfloat16*>(dres_bf), Gp(b0 + 2), f32, ws, N, D, st));
+      SB_TRY(fork());
+      SB_K(gemm(desc(dul, 4 * D, true, h2[l], D, true, 4 * D, D, N, Gp(b0 + 4), D, f32), sst, err, dw_side));
+      SB_TRY(mark(ev_fc[l]));
+      SB_K(gemm(desc(dul, 4 * D, false, Pp(b0 + 4), D, true, N, D, 4 * D, dh, D, f32), st, err));
+      if (l + 1 < L) SB_TRY(wait(ev_proj[l + 1]));  // r1 last read by dW_proj one layer up
+      SB_K(layernorm_bwd(dh, f32, xmid[l], mean2[l], rstd2[l], Pp(b0 + 3), f32, dres, bf_out(r1), Gp(b0 + 3), f32,
+                         ws, N, D, st));
+      SB_TRY(fork());
+      SB_K(gemm(desc(r1, D, true, att[l], D, true, D, D, N, Gp(b0 + 1), D, f32), sst, err, dw_side));
+      SB_TRY(mark(ev_proj[l]));
+      SB_K(gemm(desc(r1, D, false, Pp(b0 + 1), D, true, N, D, D, dout, D, f32), st, err));
+      if (l + 2 < L) SB_TRY(wait(ev_qkv[l + 2]));  // dqkv buffer last read by dW_qkv two layers up
+      SB_K(attention_bwd(qkv[l], att[l], dout, lse[l], f32, dql, ws, ash, st));
+      SB_TRY(fork());
+      SB_K(gemm(desc(dql, 3 * D, true, h1[l], D, true, 3 * D, D, N, Gp(b0 + 0), D, f32), sst, err, dw_side));
+      SB_TRY(mark(ev_qkv[l]));
+      SB_K(gemm(desc(dql, 3 * D, false, Pp(b0 + 0), D, true, N, D, 3 * D, dh, D, f32), st, err));
+      SB_TRY(wait(ev_fc2[l]));  // r0 last read by dW_fc2 of this layer
+      SB_K(layernorm_bwd(dh, f32, xs[l], mean1[l], rstd1[l], Pp(b0 + 2), f32, dres, bf_out(r0), Gp(b0 + 2), f32, ws,
+                         N, D, st));
       // layer l's six gradients (plus ln_f after the last layer) are final
-      SB_TRY(launch_bucket(offs[b0], l == L - 1 ? offs[ip] : offs[b0 + 6]));
+      SB_TRY(launch_bucket(offs[b0], l == L - 1 ? offs[ip] : offs[b0 + 6], ev_qkv[l]));
+    }
+    if (dw_side) {  // join: the main stream waits for every weight gradient
+      cudaEvent_t e = xev[nev++];
+      SB_CUDA_TRY(cudaEventRecord(e, wst));
+      SB_CUDA_TRY(cudaStreamWaitEvent(st, e, 0));
     }
     SB_K(embedding_bwd(ids, dres, B, T, P, V, D, Gp(iw), Gp(ip), f32, ws, st));
-    SB_TRY(launch_bucket(offs[ip], grads_bytes));
+    SB_TRY(launch_bucket(offs[ip], grads_bytes, nullptr));
     if (dp) {
       SB_TRY(comm_allreduce_avg(s, loss_f32, 1, SB_ELEM_F32, s.comm_stream));
       SB_CUDA_TRY(cudaEventRecord(comm_done, s.comm_stream));
@@ -643,7 +729,8 @@ class GptVagModule : public Module {
       // NCCL's own kernels (one per bucket all-reduce and one for the loss)
       // are not library kernels
       if (dp) nk -= std::min<uint64_t>(nk, static_cast<uint64_t>(L) + 3);
-      ce = cudaGraphInstantiate(&ex, graph, 0);
+      // honour the streams' priorities captured into the kernel nodes
+      ce = cudaGraphInstantiate(&ex, graph, cudaGraphInstantiateFlagUseNodePriority);
       cudaGraphDestroy(graph);
       if (ce != cudaSuccess) return make_status(SB_STATUS_INTERNAL, std::string("graph instantiate: ") + cudaGetErrorString(ce));
       s.graph_captures++;

@@ -15,6 +15,8 @@
 #include <cstdint>
 
 #include "sb_nn.h"
+#define SB_PDL_FAMILY 3
+#include "sb_launch.cuh"
 
 namespace sb {
 
@@ -75,6 +77,8 @@ __device__ __forceinline__ int leaf_of(const OptLeaves& t, int c) {
 // thread-strided then a fixed tree over the block).
 template <typename T>
 __global__ void __launch_bounds__(kThreads) sumsq_kernel(OptLeaves t, float* __restrict__ part) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[kThreads];
   const int c0 = t.cstart[0], c1 = t.cstart[t.count];
   for (int c = c0 + static_cast<int>(blockIdx.x); c < c1; c += gridDim.x) {
@@ -104,6 +108,8 @@ __global__ void __launch_bounds__(kThreads) sumsq_kernel(OptLeaves t, float* __r
 __global__ void opt_finish_kernel(const float* __restrict__ part, int nchunks, const float* __restrict__ t_in,
                                   float* __restrict__ t_out, const float* __restrict__ lr, float b1, float b2,
                                   float max_norm, OptScalars* __restrict__ sc, float* __restrict__ norm_out) {
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   double acc = 0.0;
   for (int c = 0; c < nchunks; ++c) acc += static_cast<double>(part[c]);
@@ -126,6 +132,8 @@ __global__ void opt_finish_kernel(const float* __restrict__ part, int nchunks, c
 template <typename T>
 __global__ void __launch_bounds__(kThreads) adamw_kernel(OptLeaves t, const OptScalars* __restrict__ sc, float b1,
                                                          float b2, float eps, float wd) {
+  pdl_wait();
+  pdl_trigger();
   T fac_t;
   st<T>(&fac_t, 0, sc->factor);
   const float fl = ld<T>(&fac_t, 0);  // the clip factor in the leaf's type
@@ -220,13 +228,13 @@ int optimizer_step(bool bf16, int n_leaves, const int64_t* counts, const void* c
     const int nch = t.cstart[cnt] - cbase;
     const int grid = std::min(nch, grid_cap);
     if (bf16)
-      sumsq_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(t, part);
+      launch_pdl((sumsq_kernel<__nv_bfloat16>), dim3(grid), dim3(kThreads), 0, s, t, part);
     else
-      sumsq_kernel<float><<<grid, kThreads, 0, s>>>(t, part);
+      launch_pdl((sumsq_kernel<float>), dim3(grid), dim3(kThreads), 0, s, t, part);
     cbase = t.cstart[cnt];
   }
-  opt_finish_kernel<<<1, 32, 0, s>>>(part, static_cast<int>(total_chunks), t_in, update ? t_out : nullptr, lr, b1,
-                                     b2, max_norm, update ? sc : nullptr, norm_out);
+  launch_pdl(opt_finish_kernel, dim3(1), dim3(32), 0, s, part, static_cast<int>(total_chunks), t_in,
+             update ? t_out : nullptr, lr, b1, b2, max_norm, update ? sc : nullptr, norm_out);
   if (update) {
     cbase = 0;
     for (int first = 0; first < n_leaves; first += kOptLeavesPerLaunch) {
@@ -235,9 +243,9 @@ int optimizer_step(bool bf16, int n_leaves, const int64_t* counts, const void* c
       const int nch = t.cstart[cnt] - cbase;
       const int grid = std::min(nch, grid_cap);
       if (bf16)
-        adamw_kernel<__nv_bfloat16><<<grid, kThreads, 0, s>>>(t, sc, b1, b2, eps, wd);
+        launch_pdl((adamw_kernel<__nv_bfloat16>), dim3(grid), dim3(kThreads), 0, s, t, sc, b1, b2, eps, wd);
       else
-        adamw_kernel<float><<<grid, kThreads, 0, s>>>(t, sc, b1, b2, eps, wd);
+        launch_pdl((adamw_kernel<float>), dim3(grid), dim3(kThreads), 0, s, t, sc, b1, b2, eps, wd);
       cbase = t.cstart[cnt];
     }
   }

@@ -16,6 +16,8 @@
 #include <algorithm>
 
 #include "sb_nn.h"
+#define SB_PDL_FAMILY 1
+#include "sb_launch.cuh"
 
 namespace sb {
 
@@ -126,6 +128,8 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
                                                      int gamma_f32, TO* __restrict__ y, float* __restrict__ mean_out,
                                                      float* __restrict__ rstd_out, int rows, int D,
                                                      float* __restrict__ x_copy) {
+  pdl_wait();
+  pdl_trigger();
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x & 31;
   const int stride = gridDim.x * warps;
@@ -164,6 +168,8 @@ __global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(con
                                                         const void* __restrict__ gamma, int gamma_f32,
                                                         float* __restrict__ dres, __nv_bfloat16* __restrict__ dres_bf,
                                                         float* __restrict__ dgamma_part, int rows, int D) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float sm_dg[];  // [warps][D]
   const int warps = blockDim.x / 32;
   const int warp = threadIdx.x / 32;
@@ -235,6 +241,8 @@ __global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(con
 // column, coalesced), then the 8 warp sums are combined in order.
 __global__ void __launch_bounds__(256) column_sum_kernel(const float* __restrict__ part, int nparts, long D, void* out,
                                                          int out_f32) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sm[8][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long c = static_cast<long>(blockIdx.x) * 32 + lane;
@@ -257,7 +265,8 @@ __global__ void __launch_bounds__(256) column_sum_kernel(const float* __restrict
 }
 
 int column_sum(const float* part, int nparts, long D, void* out, bool out_f32, cudaStream_t s) {
-  column_sum_kernel<<<static_cast<unsigned>((D + 31) / 32), 256, 0, s>>>(part, nparts, D, out, out_f32);
+  launch_pdl(column_sum_kernel, dim3(static_cast<unsigned>((D + 31) / 32)), dim3(256), 0, s, part, nparts, D, out,
+             out_f32);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
@@ -270,6 +279,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) ce_fwd_bwd_kernel(const T* __restrict__ logits, long ld, int rows, int V,
                                                          const float* __restrict__ targets, T* __restrict__ dlogits,
                                                          long ldd, float* __restrict__ row_part, float inv_rows) {
+  pdl_wait();
+  pdl_trigger();
   const int warps = blockDim.x / 32;
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   __shared__ float sm_part[32];
@@ -311,6 +322,8 @@ __global__ void __launch_bounds__(256) ce_fwd_bwd_kernel(const T* __restrict__ l
 // loss = -(sum of block partials) / rows, written as f32 and/or bf16.
 __global__ void ce_finish_kernel(const float* __restrict__ part, int nparts, float inv_rows, float* loss_f32,
                                  __nv_bfloat16* loss_bf16) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sm[256];
   float acc = 0.f;
   for (int i = threadIdx.x; i < nparts; i += blockDim.x) acc += part[i];
@@ -334,6 +347,8 @@ __global__ void ce_finish_kernel(const float* __restrict__ part, int nparts, flo
 template <typename TW>
 __global__ void embed_fwd_kernel(const float* __restrict__ ids, const TW* __restrict__ wte,
                                  const TW* __restrict__ wpe, float* __restrict__ x, int ntok, int T, int V, int D) {
+  pdl_wait();
+  pdl_trigger();
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x & 31;
   for (int n = blockIdx.x * warps + threadIdx.x / 32; n < ntok; n += gridDim.x * warps) {
@@ -355,6 +370,8 @@ __global__ void embed_fwd_kernel(const float* __restrict__ ids, const TW* __rest
 // part[b]; the partials are summed in block order by column_sum.
 __global__ void embed_bwd_priv_kernel(const float* __restrict__ ids, const float* __restrict__ dx, int ntok, int V,
                                       int D, int chunk, float* __restrict__ part) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float acc[];
   const int VD = V * D;
   for (int i = threadIdx.x; i < VD; i += blockDim.x) acc[i] = 0.f;
@@ -384,6 +401,8 @@ constexpr int kEmbedPrivBlocks = 148;
 // dwte for a large vocabulary: fp32 atomics into a zeroed f32 accumulator.
 __global__ void embed_bwd_atomic_kernel(const float* __restrict__ ids, const float* __restrict__ dx, int ntok, int V,
                                         int D, float* __restrict__ acc) {
+  pdl_wait();
+  pdl_trigger();
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x & 31;
   for (int n = blockIdx.x * warps + threadIdx.x / 32; n < ntok; n += gridDim.x * warps) {
@@ -398,6 +417,8 @@ __global__ void embed_bwd_atomic_kernel(const float* __restrict__ ids, const flo
 // dwpe[t, :] = sum_b dx[b*T + t, :] for t < T; rows T..P-1 are zero (pad).
 __global__ void embed_bwd_pos_kernel(const float* __restrict__ dx, int B, int T, int P, int D, void* dwpe,
                                      int out_f32) {
+  pdl_wait();
+  pdl_trigger();
   const long total = static_cast<long>(P) * D;
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long>(gridDim.x) * blockDim.x) {
@@ -426,6 +447,8 @@ __device__ __forceinline__ float gelu_df(float x) {
 
 template <typename T, bool BWD>
 __global__ void gelu_kernel(const T* __restrict__ x, const T* __restrict__ g, T* __restrict__ y, long n) {
+  pdl_wait();
+  pdl_trigger();
   const long n8 = n / 8;
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n8;
        i += static_cast<long>(gridDim.x) * blockDim.x) {
@@ -450,6 +473,8 @@ __global__ void gelu_kernel(const T* __restrict__ x, const T* __restrict__ g, T*
 }
 
 __global__ void convert_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, long n) {
+  pdl_wait();
+  pdl_trigger();
   for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long>(gridDim.x) * blockDim.x)
     out[i] = __float2bfloat16_rn(in[i]);
@@ -493,11 +518,13 @@ int layernorm_fwd(const float* x, const void* gamma, bool gamma_f32, void* y, bo
   const int warps = 8;
   const int grid = std::min((rows + 2 * warps - 1) / (2 * warps), 4 * num_sms_cached());
   if (y_f32)
-    SB_LN_DISPATCH((D + 127) / 128, (ln_fwd_kernel<V, float><<<grid, warps * 32, 0, s>>>(
-                                        x, gamma, gamma_f32, static_cast<float*>(y), mean, rstd, rows, D, x_copy)));
+    SB_LN_DISPATCH((D + 127) / 128, (launch_pdl((ln_fwd_kernel<V, float>), dim3(grid), dim3(warps * 32), 0, s, x,
+                                                gamma, gamma_f32, static_cast<float*>(y), mean, rstd, rows, D,
+                                                x_copy)));
   else
-    SB_LN_DISPATCH((D + 127) / 128, (ln_fwd_kernel<V, __nv_bfloat16><<<grid, warps * 32, 0, s>>>(
-                                        x, gamma, gamma_f32, static_cast<__nv_bfloat16*>(y), mean, rstd, rows, D, x_copy)));
+    SB_LN_DISPATCH((D + 127) / 128, (launch_pdl((ln_fwd_kernel<V, __nv_bfloat16>), dim3(grid), dim3(warps * 32), 0, s,
+                                                x, gamma, gamma_f32, static_cast<__nv_bfloat16*>(y), mean, rstd, rows,
+                                                D, x_copy)));
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
@@ -523,15 +550,15 @@ int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean
     SB_LN_DISPATCH((D + 127) / 128, ({
       auto k = ln_bwd_kernel<V, float>;
       if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      k<<<grid, warps * 32, smem, s>>>(static_cast<const float*>(dy), x, mean, rstd, gamma, gamma_f32, dres, dres_bf,
-                                       ws, rows, D);
+      launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, static_cast<const float*>(dy), x, mean, rstd, gamma,
+                 gamma_f32, dres, dres_bf, ws, rows, D);
     }));
   else
     SB_LN_DISPATCH((D + 127) / 128, ({
       auto k = ln_bwd_kernel<V, __nv_bfloat16>;
       if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      k<<<grid, warps * 32, smem, s>>>(static_cast<const __nv_bfloat16*>(dy), x, mean, rstd, gamma, gamma_f32, dres,
-                                       dres_bf, ws, rows, D);
+      launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, static_cast<const __nv_bfloat16*>(dy), x, mean, rstd,
+                 gamma, gamma_f32, dres, dres_bf, ws, rows, D);
     }));
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
   return column_sum(ws, grid, D, dgamma, dgamma_f32, s);
@@ -550,7 +577,8 @@ int layernorm_bwd_capped(const float* dy, const float* x, const float* mean, con
   SB_LN_DISPATCH((D + 127) / 128, ({
     auto k = ln_bwd_kernel<V, float>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    k<<<grid, warps * 32, smem, s>>>(dy, x, mean, rstd, gamma, gamma_f32, dres, nullptr, scratch, rows, D);
+    launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, dy, x, mean, rstd, gamma, gamma_f32, dres, nullptr, scratch,
+               rows, D);
   }));
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
   return column_sum(scratch, grid, D, dgamma, dgamma_f32, s);
@@ -567,14 +595,14 @@ int cross_entropy_fwd_bwd(const void* logits, bool f32, long ld, int rows, int V
   const int grid = std::min((rows + warps - 1) / warps, 4 * num_sms_cached());
   const float inv = 1.0f / static_cast<float>(rows);
   if (f32)
-    ce_fwd_bwd_kernel<float><<<grid, warps * 32, 0, s>>>(static_cast<const float*>(logits), ld, rows, V, targets,
-                                                         static_cast<float*>(dlogits), ldd, ws, inv);
+    launch_pdl((ce_fwd_bwd_kernel<float>), dim3(grid), dim3(warps * 32), 0, s, static_cast<const float*>(logits), ld,
+               rows, V, targets, static_cast<float*>(dlogits), ldd, ws, inv);
   else
-    ce_fwd_bwd_kernel<__nv_bfloat16><<<grid, warps * 32, 0, s>>>(static_cast<const __nv_bfloat16*>(logits), ld, rows,
-                                                                 V, targets, static_cast<__nv_bfloat16*>(dlogits), ldd,
-                                                                 ws, inv);
+    launch_pdl((ce_fwd_bwd_kernel<__nv_bfloat16>), dim3(grid), dim3(warps * 32), 0, s,
+               static_cast<const __nv_bfloat16*>(logits), ld, rows, V, targets, static_cast<__nv_bfloat16*>(dlogits),
+               ldd, ws, inv);
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
-  ce_finish_kernel<<<1, 256, 0, s>>>(ws, grid, inv, loss_f32, loss_bf16);
+  launch_pdl(ce_finish_kernel, dim3(1), dim3(256), 0, s, ws, grid, inv, loss_f32, loss_bf16);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
@@ -583,11 +611,11 @@ int embedding_fwd(const float* ids, const void* wte, const void* wpe, bool f32, 
   if (ntok <= 0 || (D & 3)) return 1;
   const int grid = std::min((ntok + 7) / 8, 8 * num_sms_cached());
   if (f32)
-    embed_fwd_kernel<float><<<grid, 256, 0, s>>>(ids, static_cast<const float*>(wte), static_cast<const float*>(wpe),
-                                                 x, ntok, T, V, D);
+    launch_pdl((embed_fwd_kernel<float>), dim3(grid), dim3(256), 0, s, ids, static_cast<const float*>(wte),
+               static_cast<const float*>(wpe), x, ntok, T, V, D);
   else
-    embed_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(ids, static_cast<const __nv_bfloat16*>(wte),
-                                                         static_cast<const __nv_bfloat16*>(wpe), x, ntok, T, V, D);
+    launch_pdl((embed_fwd_kernel<__nv_bfloat16>), dim3(grid), dim3(256), 0, s, ids,
+               static_cast<const __nv_bfloat16*>(wte), static_cast<const __nv_bfloat16*>(wpe), x, ntok, T, V, D);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
@@ -607,22 +635,24 @@ int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V,
     const size_t smem = static_cast<size_t>(V) * D * sizeof(float);
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(embed_bwd_priv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    embed_bwd_priv_kernel<<<kEmbedPrivBlocks, (D + 31) / 32 * 32, smem, s>>>(ids, dx, ntok, V, D, chunk, ws);
+    launch_pdl(embed_bwd_priv_kernel, dim3(kEmbedPrivBlocks), dim3((D + 31) / 32 * 32), smem, s, ids, dx, ntok, V, D,
+               chunk, ws);
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
     if (column_sum(ws, kEmbedPrivBlocks, static_cast<long>(V) * D, dwte, out_f32, s)) return 4;
   } else {
     float* acc = out_f32 ? static_cast<float*>(dwte) : ws;
     if (!acc) return 5;
     cudaMemsetAsync(acc, 0, static_cast<size_t>(V) * D * sizeof(float), s);
-    embed_bwd_atomic_kernel<<<std::min((ntok + 7) / 8, 8 * num_sms_cached()), 256, 0, s>>>(ids, dx, ntok, V, D, acc);
+    launch_pdl(embed_bwd_atomic_kernel, dim3(std::min((ntok + 7) / 8, 8 * num_sms_cached())), dim3(256), 0, s, ids,
+               dx, ntok, V, D, acc);
     if (!out_f32) {
       const long n = static_cast<long>(V) * D;
-      convert_kernel<<<grid_for(n, 256), 256, 0, s>>>(acc, static_cast<__nv_bfloat16*>(dwte), n);
+      launch_pdl(convert_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, acc, static_cast<__nv_bfloat16*>(dwte), n);
     }
   }
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
   const long total = static_cast<long>(P) * D;
-  embed_bwd_pos_kernel<<<grid_for(total, 256), 256, 0, s>>>(dx, B, T, P, D, dwpe, out_f32);
+  launch_pdl(embed_bwd_pos_kernel, dim3(grid_for(total, 256)), dim3(256), 0, s, dx, B, T, P, D, dwpe, out_f32);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
@@ -631,24 +661,25 @@ int gelu(const void* x, const void* g, void* y, bool f32, bool bwd, long n, cuda
   const int blocks = grid_for((n + 7) / 8, 256);
   if (f32) {
     if (bwd)
-      gelu_kernel<float, true><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), static_cast<const float*>(g),
-                                                      static_cast<float*>(y), n);
+      launch_pdl((gelu_kernel<float, true>), dim3(blocks), dim3(256), 0, s, static_cast<const float*>(x),
+                 static_cast<const float*>(g), static_cast<float*>(y), n);
     else
-      gelu_kernel<float, false><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), nullptr, static_cast<float*>(y),
-                                                       n);
+      launch_pdl((gelu_kernel<float, false>), dim3(blocks), dim3(256), 0, s, static_cast<const float*>(x), nullptr,
+                 static_cast<float*>(y), n);
   } else {
     using B = __nv_bfloat16;
     if (bwd)
-      gelu_kernel<B, true><<<blocks, 256, 0, s>>>(static_cast<const B*>(x), static_cast<const B*>(g),
-                                                  static_cast<B*>(y), n);
+      launch_pdl((gelu_kernel<B, true>), dim3(blocks), dim3(256), 0, s, static_cast<const B*>(x),
+                 static_cast<const B*>(g), static_cast<B*>(y), n);
     else
-      gelu_kernel<B, false><<<blocks, 256, 0, s>>>(static_cast<const B*>(x), nullptr, static_cast<B*>(y), n);
+      launch_pdl((gelu_kernel<B, false>), dim3(blocks), dim3(256), 0, s, static_cast<const B*>(x), nullptr,
+                 static_cast<B*>(y), n);
   }
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
 int convert_f32_to_bf16(const float* in, __nv_bfloat16* out, long n, cudaStream_t s) {
-  convert_kernel<<<grid_for(n, 256), 256, 0, s>>>(in, out, n);
+  launch_pdl(convert_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, in, out, n);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 

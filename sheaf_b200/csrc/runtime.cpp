@@ -169,8 +169,12 @@ sb_status sb_session_create(int device_ordinal, sb_session** out) {
   SB_CUDA_TRY(cudaSetDevice(device_ordinal));
   auto* s = new sb_session_s();
   s->device = device_ordinal;
-  SB_CUDA_TRY(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
-  SB_CUDA_TRY(cudaStreamCreateWithFlags(&s->comm_stream, cudaStreamNonBlocking));
+  // the session's streams take the highest priority: side streams of a
+  // module (weight gradients) fill the SMs the critical path leaves idle
+  int least = 0, greatest = 0;
+  SB_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+  SB_CUDA_TRY(cudaStreamCreateWithPriority(&s->stream, cudaStreamNonBlocking, greatest));
+  SB_CUDA_TRY(cudaStreamCreateWithPriority(&s->comm_stream, cudaStreamNonBlocking, greatest));
   cudaMemPoolProps props = {};
   props.allocType = cudaMemAllocationTypePinned;
   props.handleTypes = cudaMemHandleTypeNone;

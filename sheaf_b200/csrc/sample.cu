@@ -15,6 +15,8 @@
 #include <cstdint>
 
 #include "sb_nn.h"
+#define SB_PDL_FAMILY 3
+#include "sb_launch.cuh"
 
 namespace sb {
 
@@ -70,6 +72,8 @@ __global__ void __launch_bounds__(256) sample_kernel(const T* __restrict__ logit
                                                     int top_k, float temp, float* __restrict__ ids,
                                                     float* __restrict__ keys, float* __restrict__ tokens, int n_new,
                                                     int* __restrict__ step, float* __restrict__ step_logits) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float sh[];
   float* vals = sh;                                    // [vp2]
   int* idx = reinterpret_cast<int*>(vals + vp2);       // [vp2]
@@ -148,7 +152,11 @@ __global__ void __launch_bounds__(256) sample_kernel(const T* __restrict__ logit
     ids[static_cast<long>(b) * T_ + t] = (t + 1 < T_) ? win[t + 1] : s_token;
 }
 
-__global__ void advance_step_kernel(int* step) { *step += 1; }
+__global__ void advance_step_kernel(int* step) {
+  pdl_wait();
+  pdl_trigger();
+  *step += 1;
+}
 
 }  // namespace
 
@@ -162,16 +170,16 @@ int sample_step(const void* logits, bool logits_f32, long ld, int B, int T, int 
   if (logits_f32) {
     auto k = sample_kernel<float>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    k<<<B, 256, smem, s>>>(static_cast<const float*>(logits), ld, T, V, vp2, top_k, temperature, ids, keys,
-                           tokens, n_new, step, step_logits);
+    launch_pdl(k, dim3(B), dim3(256), smem, s, static_cast<const float*>(logits), ld, T, V, vp2, top_k, temperature,
+               ids, keys, tokens, n_new, step, step_logits);
   } else {
     auto k = sample_kernel<__nv_bfloat16>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    k<<<B, 256, smem, s>>>(static_cast<const __nv_bfloat16*>(logits), ld, T, V, vp2, top_k, temperature, ids,
-                           keys, tokens, n_new, step, step_logits);
+    launch_pdl(k, dim3(B), dim3(256), smem, s, static_cast<const __nv_bfloat16*>(logits), ld, T, V, vp2, top_k,
+               temperature, ids, keys, tokens, n_new, step, step_logits);
   }
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
-  advance_step_kernel<<<1, 1, 0, s>>>(step);
+  launch_pdl(advance_step_kernel, dim3(1), dim3(1), 0, s, step);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
