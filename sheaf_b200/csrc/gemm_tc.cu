@@ -652,6 +652,17 @@ Plan plan_for(const GemmDesc& d) {
         p.bn = bn;
       }
     }
+    // A dependent chain of 128 x N x 16 UMMAs costs about 123 cycles each
+    // for N <= 192 and 129 for N = 256 (measured), so a 256-wide grid with a
+    // half-empty last column of tiles can still win on rounds of tiles:
+    // N = 1152 at M = 16384 runs 5 rounds of 256-wide tiles (5 x 129) instead
+    // of 6 rounds of 192-wide ones (6 x 123).
+    if (p.bn == 192) {
+      const long m128 = (d.M + kBM - 1) / kBM;
+      const long r192 = (m128 * ((d.N + 191) / 192) + num_sms() - 1) / num_sms();
+      const long r256 = (m128 * ((d.N + 255) / 256) + num_sms() - 1) / num_sms();
+      if (r256 * 129 < r192 * 123) p.bn = 256;
+    }
   }
   // 256-row tiles on CTA pairs for tiles 256 or 128 wide (192-wide pair tiles
   // measured slower in the step) when padding M to 256 rows wastes little

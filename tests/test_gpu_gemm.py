@@ -25,6 +25,7 @@ CASES = [
     (96, 66, 4096, 1, 1, 0, 2),  # one tile, long K, N not a multiple of 4: no split-K
     (512, 1536, 4096, 1, 0, 0, 0),  # CTA-pair tiles with split-K
     (4160, 256, 256, 0, 1, 0, 0),  # CTA pairs, the last pair tile half outside M
+    (16384, 1152, 384, 0, 1, 0, 0),  # 256-wide pair tiles, the last column of tiles half outside N
 ]
 
 
