@@ -40,6 +40,9 @@ UNIT = "tokens/s"
 CFG = dict(n_layer=6, n_head=6, n_embd=384, block_size=256, vocab_size=65, batch=64, seq=256)
 BF16 = 0x22000010
 F32 = 0x21000020
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the fc GEMM
+# (13.8 MB + 1.1 MB: A and B read once, the output still in L2 at the end)
+FC_GEMM_DRAM_BYTES = 14.9e6
 
 
 def model_flops_per_token(c=CFG) -> float:
@@ -580,7 +583,9 @@ def bench_b200(args, world, rank, local):
                    "model_flop_per_token": model_flops_per_token(), "loss_at_warmup": loss0},
         "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (fc: 16384x384 @ 384x1536, bf16)",
                      "achieved": achieved_tf, "peak": tc_burst, "unit": "TFLOP/s", "frac": achieved_tf / tc_burst,
-                     "traffic": None, "peak_source": f"{src} bf16_tflops (burst, kernel timed alone)"},
+                     # DRAM read + write per launch, from one ncu capture of this kernel and shape
+                     "traffic": FC_GEMM_DRAM_BYTES, "traffic_unit": "bytes per launch (ncu dram read + write)",
+                     "peak_source": f"{src} bf16_tflops (burst, kernel timed alone)"},
         "clocks": clk.summary(),
         "gpu_launches": int(launches),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(x.nbytes + y.nbytes),
