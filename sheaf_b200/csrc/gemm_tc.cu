@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(384, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], PAIR ? 8 : 4);
+      mbar_init(&tempty[s], PAIR ? 16 : 8);  // every epilogue warp (of both CTAs)
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -289,11 +289,15 @@ __global__ void __launch_bounds__(384, 1)
       }
     }
   } else if (warp >= 4) {
-    // Two epilogue warpgroups: group eg drains accumulator buffer eg, i.e.
-    // this CTA's tiles local = eg, eg + 2, ...; warp w reads TMEM lanes
-    // 32*(w%4) .. +31.
+    // Two epilogue warpgroups drain every tile together, group eg taking one
+    // half of the tile's column blocks, so a tile's drain (the last one's is
+    // not hidden behind a main loop) takes half as long; warp w reads TMEM
+    // lanes 32*(w%4) .. +31.
     const int q = warp & 3;
     const int eg = (warp >> 2) - 1;
+    constexpr int kBlocksBf16 = BN / 64, kBlocksF32 = BN / 32;  // 128-byte column blocks per tile row
+    const int cb16 = eg ? (kBlocksBf16 + 1) / 2 : 0, ce16 = eg ? kBlocksBf16 : (kBlocksBf16 + 1) / 2;
+    const int cb32 = eg ? kBlocksF32 / 2 : 0, ce32 = eg ? kBlocksF32 : kBlocksF32 / 2;
     constexpr int kSlots = staging_slots(BN, PAIR);
     const uint32_t stg = smem_u32(sStg) + (warp - 4) * kSlots * kSlotBytes;
     uint32_t cc = 0;  // bulk stores issued by this warp (lane 0 commits them)
@@ -324,9 +328,9 @@ __global__ void __launch_bounds__(384, 1)
       }
       ++cc;
     };
-    int local = eg;
+    int local = 0;
     const uint32_t tempty0 = PAIR ? mapa_shared(smem_u32(tempty), 0) : smem_u32(tempty);
-    for (int u = cta0 + eg * ncta; u < units; u += 2 * ncta, local += 2) {
+    for (int u = cta0; u < units; u += ncta, ++local) {
       const int split = u % a.splits;
       const int tile = u / a.splits;
       const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
@@ -338,9 +342,10 @@ __global__ void __launch_bounds__(384, 1)
         // pull this row's aux segment of the tile towards L2 while the
         // accumulator is still being computed
         const int esz = a.epi == EPI_ADD ? 4 : 2;
-        const char* ap = static_cast<const char*>(a.aux) + (static_cast<long>(row) * a.ldaux + nt * BN) * esz;
-        const int bytes = min(BN, a.N - nt * BN) * esz;
-        for (int off = 0; off < bytes; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(ap + off));
+        const int c0 = nt * BN + (a.epi == EPI_ADD ? cb32 * 32 : cb16 * 64);
+        const int c1 = min(a.N, nt * BN + (a.epi == EPI_ADD ? ce32 * 32 : ce16 * 64));
+        const char* ap = static_cast<const char*>(a.aux) + static_cast<long>(row) * a.ldaux * esz;
+        for (int off = c0 * esz; off < c1 * esz; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(ap + off));
       }
       if (!mbar_wait(&tfull[as], aph, a.err, abort_flag)) break;
       tc_fence_after();
@@ -350,7 +355,7 @@ __global__ void __launch_bounds__(384, 1)
         // 32 f32 columns (128 B) per block: STORE, ADD, or ACCUM (reduce-add
         // into the residual stream)
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = cb32; c < ce32; ++c) {
           const int col0 = nt * BN + c * 32;
           if (col0 >= a.N) break;
           uint32_t v[32];
@@ -378,7 +383,7 @@ __global__ void __launch_bounds__(384, 1)
       } else {
         // 64 bf16 columns (128 B) per block: STORE, GELU (two outputs), MUL
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = cb16; c < ce16; ++c) {
           const int col0 = nt * BN + c * 64;
           if (col0 >= a.N) break;
           uint32_t v0[32], v1[32];
