@@ -260,6 +260,98 @@ __global__ void gather_rows_kernel(const void* operand, const int32_t* idx, void
   }
 }
 
+// Clamped start of axis k (StableHLO dynamic_slice / dynamic_update_slice).
+__device__ __forceinline__ long dyn_start(const DynSlice& d, int k) {
+  long v = *d.start[k];
+  const long hi = d.shape[k] - d.size[k];
+  return v < 0 ? 0 : (v > hi ? hi : v);
+}
+
+// out[c] = in[start + c] over the slice coordinates c.
+__global__ void dyn_slice_kernel(const void* in, void* out, long n, int esize, DynSlice d) {
+  SB_GRID_LOOP(i, n) {
+    long rem = i, src = 0, stride = 1;
+    for (int k = d.rank - 1; k >= 0; --k) {
+      const long c = rem % d.size[k];
+      rem /= d.size[k];
+      src += (dyn_start(d, k) + c) * stride;
+      stride *= d.shape[k];
+    }
+    const char* sp = static_cast<const char*>(in) + src * esize;
+    char* dp = static_cast<char*>(out) + i * esize;
+    for (int b = 0; b < esize; ++b) dp[b] = sp[b];
+  }
+}
+
+// out[start + c] = upd[c] over the update's coordinates c.
+__global__ void dyn_update_kernel(void* out, const void* upd, long n, int esize, DynSlice d) {
+  SB_GRID_LOOP(i, n) {
+    long rem = i, dst = 0, stride = 1;
+    for (int k = d.rank - 1; k >= 0; --k) {
+      const long c = rem % d.size[k];
+      rem /= d.size[k];
+      dst += (dyn_start(d, k) + c) * stride;
+      stride *= d.shape[k];
+    }
+    const char* sp = static_cast<const char*>(upd) + i * esize;
+    char* dp = static_cast<char*>(out) + dst * esize;
+    for (int b = 0; b < esize; ++b) dp[b] = sp[b];
+  }
+}
+
+// One CTA per row: bitonic sort of (key, position) pairs in shared memory,
+// position breaking ties so the order is stable; padding sorts last.
+__global__ void __launch_bounds__(512) sort_rows_kernel(const void* keys, int key_dt, const int32_t* payload,
+                                                        void* out_keys, int32_t* out_payload, int n, int np2,
+                                                        int descending) {
+  extern __shared__ float sk[];
+  int* pos = reinterpret_cast<int*>(sk + np2);
+  const long row = blockIdx.x;
+  for (int i = threadIdx.x; i < np2; i += blockDim.x) {
+    if (i < n) {
+      const float v = ld(keys, row * n + i, key_dt);
+      sk[i] = descending ? v : -v;  // sort descending on the (possibly negated) key
+      pos[i] = i;
+    } else {
+      sk[i] = -INFINITY;
+      pos[i] = 0x7FFFFFFF;
+    }
+  }
+  __syncthreads();
+  for (int size = 2; size <= np2; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < np2; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const float vi = sk[i], vj = sk[j];
+          const int pi = pos[i], pj = pos[j];
+          // does element j belong before element i?
+          const bool j_first = vj > vi || (vj == vi && pj < pi);
+          const bool i_first = vi > vj || (vi == vj && pi < pj);
+          const bool swap = ((i & size) == 0) ? j_first : i_first;
+          if (swap) {
+            sk[i] = vj;
+            sk[j] = vi;
+            pos[i] = pj;
+            pos[j] = pi;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int p = pos[i];
+    // the key is copied from its source (exact, also for bf16 and -0.0)
+    const long src = row * n + p, dst = row * n + i;
+    if (key_dt == DT_BF16)
+      static_cast<__nv_bfloat16*>(out_keys)[dst] = static_cast<const __nv_bfloat16*>(keys)[src];
+    else
+      static_cast<float*>(out_keys)[dst] = static_cast<const float*>(keys)[src];
+    out_payload[dst] = payload[src];
+  }
+}
+
 int blocks_for(long n) { return static_cast<int>(std::max<long>(1, std::min<long>((n + 255) / 256, 32L * num_sms()))); }
 
 }  // namespace
@@ -335,6 +427,38 @@ int gather_rows(const void* operand, const void* idx, void* out, long rows, long
   if (rows * width == 0) return 0;
   gather_rows_kernel<<<blocks_for(rows * width), 256, 0, s>>>(operand, static_cast<const int32_t*>(idx), out, rows, V,
                                                              width, dt_size(dt));
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+int dynamic_slice(const void* in, void* out, int dt, const DynSlice& d, cudaStream_t s) {
+  long n = 1;
+  for (int k = 0; k < d.rank; ++k) n *= d.size[k];
+  if (n == 0) return 0;
+  dyn_slice_kernel<<<blocks_for(n), 256, 0, s>>>(in, out, n, dt_size(dt), d);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+int dynamic_update(void* out, const void* upd, int dt, const DynSlice& d, cudaStream_t s) {
+  long n = 1;
+  for (int k = 0; k < d.rank; ++k) n *= d.size[k];
+  if (n == 0) return 0;
+  dyn_update_kernel<<<blocks_for(n), 256, 0, s>>>(out, upd, n, dt_size(dt), d);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+int sort_rows(const void* keys, int key_dt, const int32_t* payload, void* out_keys, int32_t* out_payload, long rows,
+              int n, bool descending, cudaStream_t s) {
+  if (rows == 0 || n == 0) return 0;
+  if (n > kSortMaxRow || (key_dt != DT_F32 && key_dt != DT_BF16)) return 1;
+  int np2 = 1;
+  while (np2 < n) np2 <<= 1;
+  const size_t smem = static_cast<size_t>(np2) * 8;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(sort_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+          cudaSuccess)
+    return 3;
+  sort_rows_kernel<<<static_cast<unsigned>(rows), 512, smem, s>>>(keys, key_dt, payload, out_keys, out_payload, n,
+                                                                   np2, descending ? 1 : 0);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 

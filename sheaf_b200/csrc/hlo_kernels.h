@@ -33,6 +33,20 @@ struct IndexMap {
   const void* pad_value = nullptr;  // device pointer to one element
 };
 
+// dynamic_slice / dynamic_update_slice: start indices are device i32
+// scalars, clamped on the device to [0, shape_d - size_d] as StableHLO
+// specifies; `shape` is the operand (slice) or result (update) shape and
+// `size` the slice sizes or the update's shape.
+struct DynSlice {
+  int rank = 0;
+  long shape[kMaxRank] = {};
+  long size[kMaxRank] = {};
+  const int32_t* start[kMaxRank] = {};
+};
+
+// Longest row the sort kernel handles (one CTA sorts a row in shared memory).
+constexpr int kSortMaxRow = 16384;
+
 int dt_size(int dt);
 int unary(const void* a, void* out, long n, int op, int dta, int dto, cudaStream_t s);
 int binary(const void* a, const void* b, void* out, long n, int op, int dt, cudaStream_t s);
@@ -47,6 +61,14 @@ int reduce(const void* in, void* out, long outer, long red, long inner, int op, 
 int bgemm(const void* A, const void* B, void* C, int batch, int M, int N, int K, int dta, int dtb, int dtc,
           cudaStream_t s);
 int gather_rows(const void* operand, const void* idx, void* out, long rows, long V, long width, int dt, cudaStream_t s);
+int dynamic_slice(const void* in, void* out, int dt, const DynSlice& d, cudaStream_t s);
+// Writes `upd` into `out` (already holding the operand) at the clamped starts.
+int dynamic_update(void* out, const void* upd, int dt, const DynSlice& d, cudaStream_t s);
+// Stable sort of `rows` rows of n keys (f32 or bf16) along the last axis,
+// carrying an i32 payload: descending for a GT comparator, ascending for LT;
+// equal keys keep their input order.
+int sort_rows(const void* keys, int key_dt, const int32_t* payload, void* out_keys, int32_t* out_payload, long rows,
+              int n, bool descending, cudaStream_t s);
 
 }  // namespace hlo
 }  // namespace sb

@@ -5,9 +5,10 @@
 // prints (sheaf/src/lowering/stablehlo/emit.rs:240-257 and the op printers in
 // that directory). Three parts:
 //   1. A parser for the op surface of that emitter (elementwise, convert,
-//      clamp, broadcast_in_dim, reshape, transpose, iota, concatenate, slice,
-//      pad, dot_general, reduce, compare, select, constant, generic gather,
-//      return), multi-line generic ops included.
+//      clamp, broadcast_in_dim, reshape, transpose, reverse, iota,
+//      concatenate, slice, pad, dynamic_slice, dynamic_update_slice,
+//      dot_general, reduce, compare, select, constant, generic gather, the
+//      two-result sort of top_k, return), multi-line generic ops included.
 //   2. A generic executor: each op runs as a library kernel in its declared
 //      element type (so bf16 modules round after every op, as the reference
 //      executes them); intermediates live in one device arena planned by
@@ -22,15 +23,30 @@
 //      plan only if every output agrees; otherwise the module stays generic.
 // An op outside the surface returns UNIMPLEMENTED, which the caller treats as
 // a failed compile (jit/compile.rs:119-125).
+//
+// Plan cache: with SHEAF_B200_CACHE_DIR set, the outcome of the first-call
+// check is recorded in <dir>/manifest.json, keyed by a hash of the module
+// text, the function name and the bytes of this library (the counterpart of
+// the reference's __sheaf__/manifest.json of compiled modules,
+// jit/compile.rs:419-478). A later load of the same text by the same build
+// starts from the recorded plan: a verified fused plan runs from the first
+// call, a rejected one is not built.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <dlfcn.h>
+#include <unistd.h>
+
 #include <algorithm>
 #include <cctype>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <fstream>
 #include <map>
+#include <mutex>
 #include <memory>
 #include <sstream>
 #include <string>
@@ -76,6 +92,9 @@ uint32_t elem_of(int dt) {
 struct HOp {
   std::string kind;
   std::string result;
+  std::string result2;  // second result (sort's permuted payload)
+  TType type2;
+  bool descending = true;  // sort: GT comparator
   std::vector<std::string> operands;
   TType type;
   std::vector<TType> operand_types;
@@ -308,7 +327,117 @@ HOp parse_op(const std::string& stmt) {
   HOp op;
   op.text = stmt.size() > 160 ? stmt.substr(0, 160) : stmt;
   op.result = c.value();
+  if (c.accept(",")) op.result2 = c.value();
   c.expect("=");
+  // operands of a quoted op: ( %a, %b, ... )
+  auto paren_values = [&]() {
+    c.expect("(");
+    if (!c.accept(")")) {
+      do op.operands.push_back(c.value());
+      while (c.accept(","));
+      c.expect(")");
+    }
+  };
+  if (c.accept("\"stablehlo.dynamic_slice\"")) {
+    // "stablehlo.dynamic_slice"(%x, %i0, ...) { slice_sizes = array<i64: ...> } : (...) -> R
+    // (indexing_ops.rs:289-318)
+    op.kind = "dynamic_slice";
+    paren_values();
+    c.expect("{");
+    c.expect("slice_sizes");
+    c.expect("=");
+    c.expect("array<i64:");
+    do op.slice_sizes.push_back(c.integer());
+    while (c.accept(","));
+    c.expect(">");
+    c.expect("}");
+    c.expect(":");
+    op.operand_types = c.type_list();
+    c.expect("->");
+    op.type = c.type();
+    return op;
+  }
+  if (c.accept("\"stablehlo.dynamic_update_slice\"")) {
+    // "stablehlo.dynamic_update_slice"(%x, %u, %i0, ...) : (...) -> T (indexing_ops.rs:320-343)
+    op.kind = "dynamic_update_slice";
+    paren_values();
+    c.expect(":");
+    op.operand_types = c.type_list();
+    c.expect("->");
+    op.type = c.type();
+    return op;
+  }
+  if (c.accept("\"stablehlo.sort\"")) {
+    // %v, %i = "stablehlo.sort"(%keys, %payload) ({ ^bb0(...): %p = "stablehlo.compare"(%a, %b)
+    //   {comparison_direction = #stablehlo<comparison_direction GT>} ... "stablehlo.return"(%p) ... })
+    //   {dimension = d : i64, is_stable = true} : (T, I) -> (T, I)   (indexing_ops.rs:486-550)
+    op.kind = "sort";
+    paren_values();
+    c.expect("(");
+    // the comparator region: the block's first two arguments are the key
+    // pair; only a GT or LT compare of that pair is accepted
+    const std::string& s = c.str();
+    size_t p = c.pos();
+    int depth = 1;
+    const size_t body0 = p;
+    while (p < s.size() && depth > 0) {
+      if (s[p] == '(' || s[p] == '{') depth++;
+      if (s[p] == ')' || s[p] == '}') depth--;
+      ++p;
+    }
+    const std::string body = s.substr(body0, p - body0);
+    c.set(p);
+    Cursor rc(body);
+    rc.expect("{");
+    rc.expect("^bb0(");
+    std::vector<std::string> args;
+    do {
+      args.push_back(rc.value());
+      rc.expect(":");
+      rc.type();
+    } while (rc.accept(","));
+    rc.expect(")");
+    rc.expect(":");
+    const std::string pred = rc.value();
+    rc.expect("=");
+    rc.expect("\"stablehlo.compare\"(");
+    const std::string lhs = rc.value();
+    rc.expect(",");
+    const std::string rhs = rc.value();
+    rc.expect(")");
+    rc.expect("{");
+    rc.expect("comparison_direction");
+    rc.expect("=");
+    rc.expect("#stablehlo<comparison_direction");
+    const std::string dir = rc.ident();
+    if (args.size() != 4 || lhs != args[0] || rhs != args[1] || (dir != "GT" && dir != "LT"))
+      c.fail("sort comparator must be a GT or LT compare of the key pair");
+    op.descending = dir == "GT";
+    (void)pred;
+    c.expect("{");
+    while (!c.accept("}")) {
+      const std::string k = c.ident();
+      c.expect("=");
+      if (k == "dimension") {
+        op.dim = c.integer();
+        if (c.accept(":")) c.ident();
+      } else if (k == "is_stable") {
+        c.ident();
+      } else {
+        c.fail("unknown sort attribute " + k);
+      }
+      c.accept(",");
+    }
+    c.expect(":");
+    op.operand_types = c.type_list();
+    c.expect("->");
+    const auto rt = c.type_list();
+    if (rt.size() != 2 || op.result2.empty()) c.fail("sort must return (keys, payload)");
+    op.type = rt[0];
+    op.type2 = rt[1];
+    return op;
+  }
+  if (!op.result2.empty()) c.fail("only stablehlo.sort has two results");
   if (c.accept("\"stablehlo.gather\"")) {
     op.kind = "gather";
     c.expect("(");
@@ -407,6 +536,20 @@ HOp parse_op(const std::string& stmt) {
     c.expect("dims");
     c.expect("=");
     op.dims = c.int_list();
+    ends_with_types(true);
+  } else if (name == "reverse") {
+    // stablehlo.reverse %a, dims = [d] : (T) -> T (indexing_ops.rs:184-205)
+    op.operands.push_back(c.value());
+    c.expect(",");
+    c.expect("dims");
+    c.expect("=");
+    op.dims = c.int_list();
+    ends_with_types(true);
+  } else if (name == "dynamic_update_slice") {
+    // stablehlo.dynamic_update_slice %x, %u, %i0, ... : (T, U, tensor<i32>, ...) -> T
+    // (indexing_ops.rs:207-287)
+    do op.operands.push_back(c.value());
+    while (c.accept(","));
     ends_with_types(true);
   } else if (name == "iota") {
     c.expect("dim");
@@ -602,11 +745,19 @@ HModule parse_module(const char* text, size_t len) {
         while (q < s.size() && (s[q] == ' ' || s[q] == '\t' || s[q] == '\r' || s[q] == '\n')) ++q;
         if (q >= s.size() || s[q] == '}') return true;
         if (s.compare(q, 6, "return") == 0 || s.compare(q, 11, "func.return") == 0) return true;
-        if (s[q] != '%') return false;
-        ++q;
-        while (q < s.size() && (std::isalnum(static_cast<unsigned char>(s[q])) || s[q] == '_' || s[q] == '#')) ++q;
-        while (q < s.size() && s[q] == ' ') ++q;
-        return q < s.size() && s[q] == '=';
+        // "%x =" or "%x, %y =" (multi-result ops)
+        while (true) {
+          if (q >= s.size() || s[q] != '%') return false;
+          ++q;
+          while (q < s.size() && (std::isalnum(static_cast<unsigned char>(s[q])) || s[q] == '_' || s[q] == '#')) ++q;
+          while (q < s.size() && s[q] == ' ') ++q;
+          if (q < s.size() && s[q] == ',') {
+            ++q;
+            while (q < s.size() && s[q] == ' ') ++q;
+            continue;
+          }
+          return q < s.size() && s[q] == '=';
+        }
       };
       while (p < s.size()) {
         const char ch = s[p];
@@ -691,6 +842,7 @@ class GenericFunc {
       }
       check_op(op, types);
       types[op.result] = op.type;
+      if (!op.result2.empty()) types[op.result2] = op.type2;
       if (op.kind == "reshape") root[op.result] = rootof(op.operands[0]);
     }
     for (auto& r : f.ret_names) {
@@ -744,6 +896,7 @@ class GenericFunc {
         loc[op.result] = l;
       } else if (op.kind != "constant") {
         loc[op.result] = ValueLoc{0, alloc(op.type.bytes()), op.type};
+        if (!op.result2.empty()) loc[op.result2] = ValueLoc{0, alloc(op.type2.bytes()), op.type2};
       }
       for (auto& r : frees[i]) {
         auto it = loc.find(r);
@@ -756,7 +909,9 @@ class GenericFunc {
     arena_bytes = scratch_off + scratch_bytes;
   }
 
-  bool op_is_result_root(const HOp& op, const std::string& r) const { return rootof(op.result) == r; }
+  bool op_is_result_root(const HOp& op, const std::string& r) const {
+    return rootof(op.result) == r || (!op.result2.empty() && op.result2 == r);
+  }
 
   static void fill_constant(const HOp& op, char* dst) {
     const int64_t n = op.type.numel();
@@ -922,6 +1077,46 @@ class GenericFunc {
         throw ParseError{"elementwise element type mismatch: " + op.text};
       if (k == "compare" && op.type.dt != DT_I1) throw ParseError{"compare must produce i1: " + op.text};
     }
+    auto i32_scalars_from = [&](size_t first) {
+      for (size_t i = first; i < op.operand_types.size(); ++i)
+        if (op.operand_types[i].dt != DT_I32 || !op.operand_types[i].shape.empty())
+          throw ParseError{"start indices must be i32 scalars: " + op.text};
+    };
+    if (k == "reverse") {
+      for (auto d : op.dims)
+        if (d < 0 || d >= static_cast<int64_t>(op.type.shape.size())) throw ParseError{"reverse dimension: " + op.text};
+      if (!(op.type == op.operand_types[0])) throw ParseError{"reverse type mismatch: " + op.text};
+    } else if (k == "dynamic_slice") {
+      const auto& sh = op.operand_types[0].shape;
+      if (op.operands.size() != 1 + sh.size() || op.slice_sizes.size() != sh.size())
+        throw ParseError{"dynamic_slice needs one start index per dimension: " + op.text};
+      i32_scalars_from(1);
+      for (size_t d = 0; d < sh.size(); ++d)
+        if (op.slice_sizes[d] < 0 || op.slice_sizes[d] > sh[d]) throw ParseError{"dynamic_slice size: " + op.text};
+      if (op.type.shape != op.slice_sizes || op.type.dt != op.operand_types[0].dt)
+        throw ParseError{"dynamic_slice result type: " + op.text};
+    } else if (k == "dynamic_update_slice") {
+      const auto& sh = op.operand_types[0].shape;
+      if (op.operands.size() != 2 + sh.size()) throw ParseError{"dynamic_update_slice arity: " + op.text};
+      const TType& u = op.operand_types[1];
+      if (u.shape.size() != sh.size() || u.dt != op.operand_types[0].dt)
+        throw ParseError{"dynamic_update_slice update type: " + op.text};
+      for (size_t d = 0; d < sh.size(); ++d)
+        if (u.shape[d] > sh[d]) throw ParseError{"dynamic_update_slice update larger than operand: " + op.text};
+      i32_scalars_from(2);
+      if (!(op.type == op.operand_types[0])) throw ParseError{"dynamic_update_slice result type: " + op.text};
+    } else if (k == "sort") {
+      const TType& kt = op.operand_types.at(0);
+      const TType& pt = op.operand_types.at(1);
+      if (op.operands.size() != 2 || kt.shape != pt.shape || kt.shape.empty())
+        throw ParseError{"sort takes keys and a payload of one shape: " + op.text};
+      if ((kt.dt != DT_F32 && kt.dt != DT_BF16) || pt.dt != DT_I32)
+        throw ParseError{"sort keys must be f32 or bf16 and the payload i32: " + op.text};
+      if (op.dim != static_cast<int64_t>(kt.shape.size()) - 1) throw ParseError{"sort along the last axis only: " + op.text};
+      if (kt.shape.back() > kSortMaxRow)
+        throw ParseError{"sort rows longer than " + std::to_string(kSortMaxRow) + ": " + op.text};
+      if (!(op.type == kt) || !(op.type2 == pt)) throw ParseError{"sort result types: " + op.text};
+    }
     if (k == "pad") {
       for (auto v : op.interior)
         if (v != 0) throw ParseError{"interior padding is not supported: " + op.text};
@@ -1046,6 +1241,46 @@ class GenericFunc {
         m.out_shape[0] = 1;
       }
       return remap(P(0), o, n, op.type.dt, m, st);
+    }
+    if (k == "reverse") {
+      const auto& sh = op.type.shape;
+      const auto ist = strides_of(sh);
+      IndexMap m;
+      m.rank = static_cast<int>(sh.size());
+      for (int d = 0; d < m.rank; ++d) {
+        m.out_shape[d] = sh[d];
+        m.stride[d] = ist[d];
+      }
+      for (auto d : op.dims) {
+        m.base += (sh[d] - 1) * ist[d];
+        m.stride[d] = -ist[d];
+      }
+      if (m.rank == 0) {
+        m.rank = 1;
+        m.out_shape[0] = 1;
+      }
+      return remap(P(0), o, n, op.type.dt, m, st);
+    }
+    if (k == "dynamic_slice" || k == "dynamic_update_slice") {
+      const bool upd = k == "dynamic_update_slice";
+      const auto& sh = op.operand_types[0].shape;
+      DynSlice d;
+      d.rank = static_cast<int>(sh.size());
+      for (int a = 0; a < d.rank; ++a) {
+        d.shape[a] = sh[a];
+        d.size[a] = upd ? op.operand_types[1].shape[a] : op.slice_sizes[a];
+        d.start[a] = static_cast<const int32_t*>(P((upd ? 2 : 1) + a));
+      }
+      if (!upd) return dynamic_slice(P(0), o, op.type.dt, d, st);
+      if (o != P(0) && op.type.bytes() &&
+          cudaMemcpyAsync(o, P(0), op.type.bytes(), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return 4;
+      return dynamic_update(o, P(1), op.type.dt, d, st);
+    }
+    if (k == "sort") {
+      const int len = static_cast<int>(op.type.shape.back());
+      return sort_rows(P(0), op.type.dt, static_cast<const int32_t*>(P(1)), o, static_cast<int32_t*>(ptr(op.result2, in)),
+                       len ? n / len : 0, len, op.descending, st);
     }
     if (k == "concatenate") {
       long off = 0;
@@ -1219,6 +1454,143 @@ sb_status outputs_agree(const std::vector<Buffer*>& a, const std::vector<Buffer*
   return nullptr;
 }
 
+// ---------------------------------------------------------------------------
+// Plan cache (manifest of first-call verification outcomes)
+// ---------------------------------------------------------------------------
+
+uint64_t fnv1a(const void* data, size_t n, uint64_t h = 1469598103934665603ull) {
+  const unsigned char* p = static_cast<const unsigned char*>(data);
+  for (size_t i = 0; i < n; ++i) {
+    h ^= p[i];
+    h *= 1099511628211ull;
+  }
+  return h;
+}
+
+std::string hex64(uint64_t v) {
+  char b[17];
+  std::snprintf(b, sizeof b, "%016llx", static_cast<unsigned long long>(v));
+  return b;
+}
+
+// Hash of the loaded library file: any rebuild invalidates recorded plans.
+const std::string& library_id() {
+  static const std::string id = [] {
+    Dl_info info{};
+    if (!dladdr(reinterpret_cast<void*>(&fnv1a), &info) || !info.dli_fname) return std::string("unknown");
+    std::ifstream f(info.dli_fname, std::ios::binary);
+    if (!f) return std::string("unknown");
+    std::string bytes((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+    return hex64(fnv1a(bytes.data(), bytes.size()));
+  }();
+  return id;
+}
+
+std::string plan_cache_dir() {
+  const char* e = std::getenv("SHEAF_B200_CACHE_DIR");
+  return (e && *e) ? std::string(e) : std::string();
+}
+
+struct PlanRecord {
+  std::string hash, plan, note;
+};
+using Manifest = std::map<std::string, PlanRecord>;
+
+std::mutex& manifest_mu() {
+  static std::mutex mu;
+  return mu;
+}
+
+std::string json_escape(const std::string& v) {
+  std::string o;
+  for (char ch : v) {
+    if (ch == '"' || ch == '\\') o += '\\';
+    if (static_cast<unsigned char>(ch) < 0x20) continue;
+    o += ch;
+  }
+  return o;
+}
+
+// Reads the manifest this library writes: {"format": 1, "entries": {"<key>":
+// {"hash": "...", "plan": "...", "note": "..."}, ...}}. Anything else reads as
+// an empty manifest.
+Manifest read_manifest(const std::string& dir) {
+  Manifest m;
+  std::ifstream f(dir + "/manifest.json");
+  if (!f) return m;
+  const std::string t((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+  size_t p = 0;
+  auto ws = [&]() {
+    while (p < t.size() && std::isspace(static_cast<unsigned char>(t[p]))) ++p;
+  };
+  auto str = [&](std::string* out) {
+    ws();
+    if (p >= t.size() || t[p] != '"') return false;
+    ++p;
+    std::string v;
+    while (p < t.size() && t[p] != '"') {
+      if (t[p] == '\\' && p + 1 < t.size()) ++p;
+      v += t[p++];
+    }
+    if (p >= t.size()) return false;
+    ++p;
+    *out = v;
+    return true;
+  };
+  auto lit = [&](char ch) {
+    ws();
+    if (p < t.size() && t[p] == ch) {
+      ++p;
+      return true;
+    }
+    return false;
+  };
+  std::string key;
+  if (!lit('{') || !str(&key) || key != "format" || !lit(':')) return {};
+  ws();
+  while (p < t.size() && std::isdigit(static_cast<unsigned char>(t[p]))) ++p;
+  if (!lit(',') || !str(&key) || key != "entries" || !lit(':') || !lit('{')) return {};
+  if (lit('}')) return m;
+  do {
+    std::string name;
+    PlanRecord r;
+    if (!str(&name) || !lit(':') || !lit('{')) return {};
+    do {
+      std::string k, v;
+      if (!str(&k) || !lit(':') || !str(&v)) return {};
+      if (k == "hash") r.hash = v;
+      else if (k == "plan") r.plan = v;
+      else if (k == "note") r.note = v;
+    } while (lit(','));
+    if (!lit('}')) return {};
+    m[name] = r;
+  } while (lit(','));
+  return m;
+}
+
+// Records one entry (read-modify-write, replaced atomically by rename).
+void record_plan(const std::string& dir, const std::string& name, const PlanRecord& r) {
+  if (dir.empty()) return;
+  std::lock_guard<std::mutex> lk(manifest_mu());
+  Manifest m = read_manifest(dir);
+  m[name] = r;
+  const std::string tmp = dir + "/manifest.json.tmp." + std::to_string(static_cast<long>(getpid()));
+  {
+    std::ofstream f(tmp);
+    if (!f) return;
+    f << "{\"format\": 1, \"entries\": {";
+    bool first = true;
+    for (auto& kv : m) {
+      f << (first ? "\n  " : ",\n  ") << '"' << json_escape(kv.first) << "\": {\"hash\": \"" << json_escape(kv.second.hash)
+        << "\", \"plan\": \"" << json_escape(kv.second.plan) << "\", \"note\": \"" << json_escape(kv.second.note)
+        << "\"}";
+      first = false;
+    }
+    f << "\n}}\n";
+  }
+  std::rename(tmp.c_str(), (dir + "/manifest.json").c_str());
+}
+
 class StableHloModule : public Module {
  public:
   struct Fn {
@@ -1226,7 +1598,9 @@ class StableHloModule : public Module {
     std::unique_ptr<Module> fused;  // the fused plan, when recognised
     int fused_state = 0;            // 0 = unverified, 1 = verified, -1 = rejected
     std::string note;
+    std::string plan_hash;  // key of the plan cache entry
   };
+  std::string cache_dir;
   std::map<std::string, Fn> fns;
 
   bool has_function(const std::string& fn) const override { return fns.count(fn) != 0; }
@@ -1264,6 +1638,8 @@ class StableHloModule : public Module {
         for (Buffer* b : fast) buffer_release(b);
         out = ref;
       }
+      record_plan(cache_dir, name + "." + fn,
+                  PlanRecord{f.plan_hash, f.fused_state == 1 ? "fused-verified" : "fused-rejected", f.note});
       return nullptr;
     }
     return f.generic->run(s, in, out);
@@ -1283,8 +1659,21 @@ sb_status load_stablehlo_module(Session& s, const char* text, size_t len, std::u
   }
   auto m = std::make_unique<StableHloModule>();
   m->name = hm.name;
+  m->cache_dir = plan_cache_dir();
+  Manifest manifest;
+  if (!m->cache_dir.empty()) {
+    std::lock_guard<std::mutex> lk(manifest_mu());
+    manifest = read_manifest(m->cache_dir);
+  }
+  const uint64_t text_hash = fnv1a(text, len);
   for (auto& f : hm.funcs) {
     StableHloModule::Fn fn;
+    {
+      uint64_t h = fnv1a(library_id().data(), library_id().size(), text_hash);
+      fn.plan_hash = hex64(fnv1a(f.name.data(), f.name.size(), h));
+    }
+    const auto rec = manifest.find(hm.name + "." + f.name);
+    const bool cached = rec != manifest.end() && rec->second.hash == fn.plan_hash;
     fn.generic = std::make_unique<GenericFunc>();
     fn.generic->f = f;
     try {
@@ -1295,12 +1684,19 @@ sb_status load_stablehlo_module(Session& s, const char* text, size_t len, std::u
       return make_status(SB_STATUS_INVALID_ARGUMENT, std::string("stablehlo: ") + e.what());
     }
     GptShape g;
-    if (match_gpt_vag(fn.generic->f, &g)) {
+    if (cached && rec->second.plan == "fused-rejected") {
+      fn.note = "generic executor (plan cache: " + rec->second.note + ")";
+    } else if (match_gpt_vag(fn.generic->f, &g)) {
       std::unique_ptr<Module> fused;
       sb_status st = make_gpt_vag_module(s, hm.name + "." + f.name, g, &fused);
       if (!st) {
         fn.fused = std::move(fused);
-        fn.note = "fused nanoGPT plan pending first-call verification";
+        if (cached && rec->second.plan == "fused-verified") {
+          fn.fused_state = 1;
+          fn.note = "fused nanoGPT plan (verified on an earlier load of this text by this build; plan cache)";
+        } else {
+          fn.note = "fused nanoGPT plan pending first-call verification";
+        }
       } else {
         fn.note = std::string("generic executor (fused plan unavailable: ") + sb_status_message(st) + ")";
         sb_status_free(st);

@@ -170,3 +170,88 @@ def test_unimplemented_op_fails_like_a_compile_error(session):
     with pytest.raises(SheafB200Error) as e:
         session.load_stablehlo(text)
     assert e.value.code == 12
+
+
+def test_reverse_and_dynamic_slices(session):
+    """stablehlo.reverse, dynamic_slice and both dynamic_update_slice forms,
+    with start indices inside and outside the operand (clamped to
+    [0, dim - size] as StableHLO specifies)."""
+    from tests.test_stablehlo_parse import INDEXING
+
+    I32 = 0x10000020
+    x = np.arange(24, dtype=np.float32).reshape(4, 6)
+    u = np.array([[100.0, 200.0]], np.float32)
+
+    def clamp(v, hi):
+        return min(max(v, 0), hi)
+
+    for i, j in [(1, 2), (7, -3), (-1, 5), (2, 4)]:
+        _, (rev, ds, dus, dus2) = run(session, INDEXING, [x, np.int32(i).reshape(()), np.int32(j).reshape(()), u],
+                                      [F32, I32, I32, F32])
+        assert np.array_equal(rev, x[:, ::-1])
+        a, b = clamp(i, 2), clamp(j, 3)
+        assert np.array_equal(ds, x[a:a + 2, b:b + 3])
+        e = x.copy()
+        a, b = clamp(i, 3), clamp(j, 4)
+        e[a:a + 1, b:b + 2] = u
+        assert np.array_equal(dus, e)
+        e = x.copy()
+        a, b = clamp(j, 3), clamp(i, 4)
+        e[a:a + 1, b:b + 2] = u
+        assert np.array_equal(dus2, e)
+
+
+@pytest.mark.parametrize("direction,key", [("GT", "f32"), ("LT", "f32"), ("GT", "bf16")])
+def test_top_k_sort(session, direction, key):
+    """top_k through the emitter's sort: stable (ties keep index order), the
+    first k of every row, indices converted to f32; compared bit-exactly with
+    numpy's stable argsort."""
+    from tests.test_stablehlo_parse import top_k_module
+
+    rows, n, k = 5, 1000, 37
+    rng = np.random.default_rng(3)
+    x = rng.integers(-20, 20, (rows, n)).astype(np.float32) * 0.25  # many ties
+    x[0, :7] = 3.5
+    if key == "bf16":
+        x = odt.round_bf16(x)
+    _, (vals, idx) = run(session, top_k_module(rows, n, k, direction, key), [x], [BF16 if key == "bf16" else F32])
+    order = np.argsort(-x if direction == "GT" else x, axis=1, kind="stable")[:, :k]
+    assert np.array_equal(idx, order.astype(np.float32))
+    assert np.array_equal(np.asarray(vals, np.float32), np.take_along_axis(x, order, 1))
+
+
+def test_plan_cache_records_and_reuses_the_verified_plan(cuda, tmp_path, monkeypatch):
+    """With SHEAF_B200_CACHE_DIR set, the first-call check's outcome lands in
+    manifest.json; a new session loading the same text starts on the verified
+    fused plan (no check), a recorded rejection keeps the module generic, and
+    an unreadable manifest is ignored."""
+    from sheaf_b200.runtime import Session
+
+    monkeypatch.setenv("SHEAF_B200_CACHE_DIR", str(tmp_path))
+    cfg = models.GPTConfig(n_layer=1, n_head=2, n_embd=128, block_size=64, vocab_size=65, batch=2, seq=64)
+    leaves, x, y = models.gpt_inputs(cfg)
+    leaves = [odt.round_bf16(l) for l in leaves]
+    text = hlo_emit.gpt_vag_module(cfg, "bf16")
+
+    def load_and_call(expect):
+        s = Session(0)
+        name = s.load_stablehlo(text)
+        assert expect in s.describe(name), s.describe(name)
+        bufs = [s.upload(l, BF16) for l in leaves] + [s.upload(x, F32), s.upload(y, F32)]
+        loss = float(s.call(f"{name}.value_and_grad", bufs)[0].to_host())
+        return s, name, loss
+
+    s1, name, loss1 = load_and_call("pending first-call verification")
+    assert "verified against the generic executor" in s1.describe(name)
+    manifest = json.loads((tmp_path / "manifest.json").read_text())
+    entry = manifest["entries"][f"{name}.value_and_grad"]
+    assert entry["plan"] == "fused-verified" and len(entry["hash"]) == 16
+    s2, _, loss2 = load_and_call("plan cache")
+    assert loss2 == loss1
+    # a recorded rejection: the fused plan is not built
+    manifest["entries"][f"{name}.value_and_grad"]["plan"] = "fused-rejected"
+    (tmp_path / "manifest.json").write_text(json.dumps(manifest))
+    load_and_call("generic executor (plan cache")
+    # an unreadable manifest is ignored
+    (tmp_path / "manifest.json").write_text("{not json")
+    load_and_call("pending first-call verification")

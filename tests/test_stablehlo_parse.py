@@ -69,3 +69,61 @@ def test_type_errors_are_reported():
     undefined = "    %0 = stablehlo.add %arg0, %7 : tensor<4xf32>\n    return %0 : tensor<4xf32>"
     with pytest.raises(SheafB200Error):
         validate_stablehlo(_wrap(undefined))
+
+
+# The emitter's forms for reverse, dynamic slices and top_k's sort
+# (sheaf/src/lowering/stablehlo/indexing_ops.rs:184-343,486-550).
+INDEXING = """module @idx {
+  func.func @f(%arg0: tensor<4x6xf32>, %arg1: tensor<i32>, %arg2: tensor<i32>, %arg3: tensor<1x2xf32>) -> (tensor<4x6xf32>, tensor<2x3xf32>, tensor<4x6xf32>, tensor<4x6xf32>) {
+    %0 = stablehlo.reverse %arg0, dims = [1] : (tensor<4x6xf32>) -> tensor<4x6xf32>
+    %1 = "stablehlo.dynamic_slice"(%arg0, %arg1, %arg2) { slice_sizes = array<i64: 2, 3> } : (tensor<4x6xf32>, tensor<i32>, tensor<i32>) -> tensor<2x3xf32>
+    %2 = "stablehlo.dynamic_update_slice"(%arg0, %arg3, %arg1, %arg2) : (tensor<4x6xf32>, tensor<1x2xf32>, tensor<i32>, tensor<i32>) -> tensor<4x6xf32>
+    %3 = stablehlo.dynamic_update_slice %arg0, %arg3, %arg2, %arg1 : (tensor<4x6xf32>, tensor<1x2xf32>, tensor<i32>, tensor<i32>) -> tensor<4x6xf32>
+    return %0, %1, %2, %3 : tensor<4x6xf32>, tensor<2x3xf32>, tensor<4x6xf32>, tensor<4x6xf32>
+  }
+}
+"""
+
+
+def top_k_module(rows: int, n: int, k: int, direction: str = "GT", key: str = "f32") -> str:
+    """top_k as emit_top_k prints it: iota, the two-operand stable sort with a
+    comparator region, slices of the first k, indices converted to f32."""
+    t = f"tensor<{rows}x{n}x{key}>"
+    ti = f"tensor<{rows}x{n}xi32>"
+    return f"""module @topk {{
+  func.func @top_k(%arg0: {t}) -> (tensor<{rows}x{k}x{key}>, tensor<{rows}x{k}xf32>) {{
+    %0 = stablehlo.iota dim = 1 : {ti}
+    %1, %2 = "stablehlo.sort"(%arg0, %0) ({{
+    ^bb0(%3: tensor<{key}>, %4: tensor<{key}>, %5: tensor<i32>, %6: tensor<i32>):
+      %7 = "stablehlo.compare"(%3, %4) {{comparison_direction = #stablehlo<comparison_direction {direction}>}} : (tensor<{key}>, tensor<{key}>) -> tensor<i1>
+      "stablehlo.return"(%7) : (tensor<i1>) -> ()
+    }}) {{dimension = 1 : i64, is_stable = true}} : ({t}, {ti}) -> ({t}, {ti})
+    %8 = stablehlo.slice %1 [0:{rows}, 0:{k}] : ({t}) -> tensor<{rows}x{k}x{key}>
+    %9 = stablehlo.slice %2 [0:{rows}, 0:{k}] : ({ti}) -> tensor<{rows}x{k}xi32>
+    %10 = stablehlo.convert %9 : (tensor<{rows}x{k}xi32>) -> tensor<{rows}x{k}xf32>
+    return %8, %10 : tensor<{rows}x{k}x{key}>, tensor<{rows}x{k}xf32>
+  }}
+}}
+"""
+
+
+def test_indexing_forms_parse():
+    s = validate_stablehlo(INDEXING)
+    assert "f: 4 ops, 4 args, 4 results" in s
+
+
+def test_top_k_sort_parses():
+    s = validate_stablehlo(top_k_module(3, 65, 5))
+    assert "top_k: 5 ops, 1 args, 2 results" in s
+    validate_stablehlo(top_k_module(1, 50304 // 4, 200, "LT", "bf16"))
+
+
+def test_sort_and_dynamic_slice_rejections():
+    bad_cmp = top_k_module(3, 65, 5).replace('"stablehlo.compare"(%3, %4)', '"stablehlo.compare"(%5, %6)')
+    too_long = top_k_module(1, 20000, 5)
+    eq = top_k_module(3, 65, 5, "EQ")
+    bad_start = INDEXING.replace("%arg1: tensor<i32>", "%arg1: tensor<f32>").replace(
+        "tensor<i32>, tensor<i32>) -> tensor<2x3xf32>", "tensor<f32>, tensor<i32>) -> tensor<2x3xf32>")
+    for text in (bad_cmp, too_long, eq, bad_start):
+        with pytest.raises(SheafB200Error):
+            validate_stablehlo(text)
