@@ -187,6 +187,32 @@ SB_API sb_status sb_module_create_gpt_sampler(sb_session* session, const char* m
 SB_API sb_status sb_call(sb_session* session, const char* qualified_name, sb_buffer* const* inputs, size_t in_count,
                          sb_buffer** outputs, size_t out_capacity, size_t* out_count);
 
+/* ---- checkpoints: safetensors straight from / to device buffers
+ *      (replaces io "save" / io "load" of .safetensors,
+ *      sheaf/src/interpreter/builtins/safetensors.rs:13-81,200-331) ----
+ * sb_safetensors_save writes the buffers under their keys exactly as the
+ * reference's save_safetensors lays a file out (keys sorted, compact header
+ * padded to an 8-byte boundary, raw little-endian data); the element type of
+ * each buffer is its file dtype (F32, BF16, F16, I32). The file is written
+ * under "<path>.tmp" and renamed into place. */
+SB_API sb_status sb_safetensors_save(sb_session* session, const char* path, const char* const* keys,
+                                     sb_buffer* const* buffers, size_t count);
+/* Opens a safetensors file and parses its header (no device work). Entries
+ * are listed in key order; "__metadata__" is skipped. */
+typedef struct sb_safetensors_file_s sb_safetensors_file;
+SB_API sb_status sb_safetensors_open(const char* path, sb_safetensors_file** out);
+SB_API size_t sb_safetensors_count(const sb_safetensors_file* file);
+SB_API const char* sb_safetensors_key(const sb_safetensors_file* file, size_t index);
+/* Element type the entry loads as (F32/F64 -> SB_ELEM_F32, BF16, F16, and
+ * I32/I64/U8/BOOL -> SB_ELEM_I32, following decode_raw) and its shape. */
+SB_API sb_status sb_safetensors_info(const sb_safetensors_file* file, size_t index, uint32_t* elem_type,
+                                     int64_t* shape, size_t shape_capacity, size_t* rank);
+/* Reads entry `index` into a new device buffer (a reference owned by the
+ * caller); the copy is complete when this returns. */
+SB_API sb_status sb_safetensors_read(sb_session* session, const sb_safetensors_file* file, size_t index,
+                                     sb_buffer** out);
+SB_API void sb_safetensors_close(sb_safetensors_file* file);
+
 #ifdef __cplusplus
 }
 #endif

@@ -152,6 +152,17 @@ SB_API int sb_op_adamw_step(uint32_t elem, int32_t n_leaves, const int64_t* coun
 SB_API int sb_op_global_norm(uint32_t elem, int32_t n_leaves, const int64_t* counts, const void* const* grads,
                              void* norm_out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* get-batch of examples/nanogpt/train.shf:15-21 on the device: x, y
+ * [batch, block] f32 token ids, rows starting at random-randint(key, [batch],
+ * 0, n - block - 1) (sheaf/src/core/prng.rs:124-134) in `data` (n f32 ids);
+ * y is x shifted by one. `key` is four f32 limbs (prng.rs:29-40); all
+ * pointers are device memory. Requires 0 < n - block - 1 <= 2^24. */
+SB_API int sb_op_get_batch(const void* data, int64_t n, const void* key, int32_t block, int32_t batch, void* x,
+                           void* y, void* stream);
+/* random-split of `key` into n child keys written as [n, 4] f32 limbs
+ * (child i = threefry(key, [i, 1]), prng.rs:81-84, random_ops.rs:146-162). */
+SB_API int sb_op_random_split(const void* key, int32_t n, void* out, void* stream);
+
 /* Reads and clears the device error word that bounded waits inside the
  * kernels set (0 = no error, 1 = a barrier wait timed out). Synchronizes
  * the device. */

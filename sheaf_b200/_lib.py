@@ -100,6 +100,16 @@ SIGNATURES: dict[str, tuple] = {
     "sb_buffer_byte_length": (C.c_size_t, [_P]),
     "sb_buffer_device_ptr": (_P, [_P]),
     "sb_module_load_stablehlo": (_P, [_P, C.c_char_p, C.c_size_t, C.POINTER(C.c_char_p)]),
+    "sb_op_get_batch": (C.c_int, [_P, C.c_int64, _P, C.c_int32, C.c_int32, _P, _P, _P]),
+    "sb_op_random_split": (C.c_int, [_P, C.c_int32, _P, _P]),
+    "sb_safetensors_save": (_P, [_P, C.c_char_p, C.POINTER(C.c_char_p), C.POINTER(_P), C.c_size_t]),
+    "sb_safetensors_open": (_P, [C.c_char_p, C.POINTER(_P)]),
+    "sb_safetensors_count": (C.c_size_t, [_P]),
+    "sb_safetensors_key": (C.c_char_p, [_P, C.c_size_t]),
+    "sb_safetensors_info": (_P, [_P, C.c_size_t, C.POINTER(C.c_uint32), C.POINTER(C.c_int64), C.c_size_t,
+                                 C.POINTER(C.c_size_t)]),
+    "sb_safetensors_read": (_P, [_P, _P, C.c_size_t, C.POINTER(_P)]),
+    "sb_safetensors_close": (None, [_P]),
     "sb_module_create_gpt_vag": (_P, [_P, C.c_char_p, C.POINTER(GptConfig)]),
     "sb_module_create_gpt_train": (_P, [_P, C.c_char_p, C.POINTER(GptConfig), C.POINTER(AdamwConfig)]),
     "sb_module_create_gpt_sampler": (_P, [_P, C.c_char_p, C.POINTER(GptConfig), C.POINTER(SamplerConfig)]),

@@ -164,6 +164,17 @@ int sb_op_adamw_step(uint32_t elem, int32_t n_leaves, const int64_t* counts, con
                             static_cast<cudaStream_t>(stream));
 }
 
+int sb_op_get_batch(const void* data, int64_t n, const void* key, int32_t block, int32_t batch, void* x, void* y,
+                    void* stream) {
+  return sb::get_batch(static_cast<const float*>(data), n, static_cast<const float*>(key), block, batch,
+                       static_cast<float*>(x), static_cast<float*>(y), static_cast<cudaStream_t>(stream));
+}
+
+int sb_op_random_split(const void* key, int32_t n, void* out, void* stream) {
+  return sb::random_split(static_cast<const float*>(key), n, static_cast<float*>(out),
+                          static_cast<cudaStream_t>(stream));
+}
+
 int sb_op_global_norm(uint32_t elem, int32_t n_leaves, const int64_t* counts, const void* const* grads,
                       void* norm_out, void* workspace, size_t workspace_bytes, void* stream) {
   if (!float_elem(elem) || !norm_out) return SB_OPERR_ARGS;

@@ -15,43 +15,13 @@
 #include <cstdint>
 
 #include "sb_nn.h"
+#include "sb_prng.cuh"
 #define SB_PDL_FAMILY 3
 #include "sb_launch.cuh"
 
 namespace sb {
 
 namespace {
-
-__device__ __forceinline__ uint32_t rotl32(uint32_t x, int r) { return (x << r) | (x >> (32 - r)); }
-
-// Threefry2x32 with 20 rounds (prng.rs:57-79).
-__device__ void threefry2x32(uint32_t k0, uint32_t k1, uint32_t c0, uint32_t c1, uint32_t& x0, uint32_t& x1) {
-  const uint32_t ks[3] = {k0, k1, 0x1BD11BDAu ^ k0 ^ k1};
-  const int rot[8] = {13, 15, 26, 6, 17, 29, 16, 24};
-  x0 = c0 + ks[0];
-  x1 = c1 + ks[1];
-#pragma unroll
-  for (int r = 0; r < 20; ++r) {
-    x0 += x1;
-    x1 = x0 ^ rotl32(x1, rot[r & 7]);
-    if ((r & 3) == 3) {
-      const uint32_t inj = static_cast<uint32_t>((r + 1) / 4);
-      x0 += ks[inj % 3];
-      x1 += ks[(inj + 1) % 3] + inj;
-    }
-  }
-}
-
-__device__ __forceinline__ void key_decode(const float* limbs, uint32_t& w0, uint32_t& w1) {
-  w0 = (static_cast<uint32_t>(limbs[0]) | (static_cast<uint32_t>(limbs[1]) << 16));
-  w1 = (static_cast<uint32_t>(limbs[2]) | (static_cast<uint32_t>(limbs[3]) << 16));
-}
-__device__ __forceinline__ void key_encode(uint32_t w0, uint32_t w1, float* limbs) {
-  limbs[0] = static_cast<float>(w0 & 0xFFFFu);
-  limbs[1] = static_cast<float>(w0 >> 16);
-  limbs[2] = static_cast<float>(w1 & 0xFFFFu);
-  limbs[3] = static_cast<float>(w1 >> 16);
-}
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T x);
@@ -132,7 +102,7 @@ __global__ void __launch_bounds__(256) sample_kernel(const T* __restrict__ logit
     threefry2x32(w0, w1, 0u, 1u, n0, n1);
     threefry2x32(w0, w1, 1u, 1u, u0, u1);
     threefry2x32(u0, u1, 0u, 0u, bits, unused);
-    const float u = static_cast<float>(bits >> 8) * (1.0f / 16777216.0f);
+    const float u = uniform_from_bits(bits);
     // choice: index = min(k - count(cumsum > u), k - 1)
     float c = 0.f;
     int count = 0;

@@ -62,6 +62,14 @@ size_t attention_bwd_workspace_bytes(bool f32, const AttnShape& sh);
 int attention_bwd(const void* qkv, const void* o, const void* dout, const float* lse, bool f32, void* dqkv, float* ws,
                   const AttnShape& sh, cudaStream_t s);
 
+// get-batch of examples/nanogpt/train.shf:15-21 on the device: batch rows
+// of `block` token ids (f32) from `data` (n ids) at starts drawn with
+// random-randint from `key` (four f32 limbs); y is x shifted by one. The
+// start bound n - block - 1 must be positive and at most 2^24 (exact in f32).
+int get_batch(const float* data, long n, const float* key, int block, int batch, float* x, float* y, cudaStream_t s);
+// random-split `key` into n children, written as [n, 4] limbs.
+int random_split(const float* key, int n, float* out, cudaStream_t s);
+
 // One token of nanoGPT's generate-token for B sequences (window T, vocab V
 // at most kSampleMaxVocab): samples from the last position's logits
 // (row b*T + T-1, row stride ld), writes tokens[b * n_new + *step], advances

@@ -161,6 +161,59 @@ class Session:
         _check(lib().sb_module_create_gpt_sampler(self._h, name.encode(), C.byref(cfg), C.byref(smp)))
         return name
 
+    # -- checkpoints (io "save" / io "load", builtins/safetensors.rs) ----------
+    def save_safetensors(self, path: str, tree) -> None:
+        """Writes a pytree of device buffers (dicts, lists, Buffer leaves) as
+        the reference's save_safetensors does: dot-separated keys (dict keys,
+        list indices), sorted; each buffer's bytes go straight to the file."""
+        items = _flatten_tree(tree)
+        for k, v in items:
+            if not isinstance(v, Buffer):
+                raise TypeError(f"checkpoint leaf {k!r} is not a device buffer")
+        n = len(items)
+        keys = (C.c_char_p * max(1, n))(*[k.encode() for k, _ in items])
+        bufs = (C.c_void_p * max(1, n))(*[v._h for _, v in items])
+        _check(lib().sb_safetensors_save(self._h, str(path).encode(), keys, bufs, n))
+
+    def load_safetensors(self, path: str, nested: bool = True):
+        """Reads every tensor of a safetensors file into a device buffer;
+        with `nested`, dot-separated keys become dicts and contiguous numeric
+        siblings lists (load_safetensors's nest_flat_keys)."""
+        f = C.c_void_p()
+        _check(lib().sb_safetensors_open(str(path).encode(), C.byref(f)))
+        flat = {}
+        try:
+            for i in range(lib().sb_safetensors_count(f)):
+                key = lib().sb_safetensors_key(f, i).decode()
+                h = C.c_void_p()
+                _check(lib().sb_safetensors_read(self._h, f, i, C.byref(h)))
+                flat[key] = Buffer(h)
+        finally:
+            lib().sb_safetensors_close(f)
+        return _nest_keys(flat) if nested else flat
+
+    # -- data path (train.shf get-batch, random-split) -----------------------
+    def random_split(self, key: "Buffer", n: int = 2) -> "Buffer":
+        """Child keys [n, 4] of a key buffer [4] (f32 limbs)."""
+        out = self.empty((n, 4), ELEM_F32)
+        rc = lib().sb_op_random_split(C.c_void_p(key.device_ptr), n, C.c_void_p(out.device_ptr),
+                                      C.c_void_p(self.stream))
+        if rc:
+            raise SheafB200Error(3, f"random_split failed ({rc})")
+        return out
+
+    def get_batch(self, data: "Buffer", key: "Buffer", block: int, batch: int) -> tuple["Buffer", "Buffer"]:
+        """get-batch on the device: x, y [batch, block] f32 ids from the f32
+        token array `data` at starts drawn from `key` (train.shf:15-21)."""
+        (n,) = data.shape
+        x = self.empty((batch, block), ELEM_F32)
+        y = self.empty((batch, block), ELEM_F32)
+        rc = lib().sb_op_get_batch(C.c_void_p(data.device_ptr), n, C.c_void_p(key.device_ptr), block, batch,
+                                   C.c_void_p(x.device_ptr), C.c_void_p(y.device_ptr), C.c_void_p(self.stream))
+        if rc:
+            raise SheafB200Error(3, f"get_batch failed ({rc})")
+        return x, y
+
     def call(self, qualified_name: str, inputs: Sequence["Buffer"], max_outputs: int = 1024) -> list["Buffer"]:
         arr = (C.c_void_p * max(1, len(inputs)))(*[b._h for b in inputs])
         outs = (C.c_void_p * max_outputs)()
@@ -176,6 +229,41 @@ def validate_stablehlo(text: str) -> str:
     buf = C.create_string_buffer(8192)
     _check(lib().sb_stablehlo_validate(data, len(data), buf, 8192))
     return buf.value.decode()
+
+
+def _flatten_tree(tree, prefix: str = "") -> list:
+    """(key, leaf) pairs: dict keys in sorted order, list items by index,
+    joined with '.'; a leaf at the root is named 'tensor'."""
+    if isinstance(tree, dict):
+        out = []
+        for k in sorted(tree):
+            out += _flatten_tree(tree[k], f"{prefix}.{k}" if prefix else str(k))
+        return out
+    if isinstance(tree, (list, tuple)):
+        out = []
+        for i, v in enumerate(tree):
+            out += _flatten_tree(v, f"{prefix}.{i}" if prefix else str(i))
+        return out
+    return [(prefix or "tensor", tree)]
+
+
+def _nest_keys(flat: dict):
+    root: dict = {}
+    for key in sorted(flat):
+        node = root
+        segs = key.split(".")
+        for seg in segs[:-1]:
+            node = node.setdefault(seg, {})
+        node[segs[-1]] = flat[key]
+
+    def lists(node):
+        if not isinstance(node, dict):
+            return node
+        node = {k: lists(v) for k, v in node.items()}
+        if node and all(k.isdigit() for k in node) and max(int(k) for k in node) + 1 == len(node):
+            return [node[str(i)] for i in range(len(node))]
+        return node
+    return lists(root)
 
 
 class Buffer:
