@@ -51,6 +51,20 @@ SB_API int sb_op_matmul(uint32_t elem, const void* a, int64_t lda, int trans_a, 
                  int32_t m, int32_t n, int32_t k, void* c, int64_t ldc, uint32_t c_elem, void* workspace,
                  size_t workspace_bytes, void* stream);
 SB_API size_t sb_op_matmul_workspace_size(uint32_t elem, int trans_a, int trans_b, int32_t m, int32_t n, int32_t k);
+/* The matmul fused with the MLP activation, as the nanoGPT plan runs the fc
+ * layer: u = A @ B^T (B stored [N,K]) rounded to the element type, then
+ * y = gelu(u) and dy = gelu'(u) in the epilogue (lib/nn.shf:10-11 and its
+ * derivative through the tanh, reverse.rs:969-975), both [M,N] with row
+ * stride ldc in the element type. No workspace. */
+SB_API int sb_op_matmul_gelu(uint32_t elem, const void* a, int64_t lda, const void* b, int64_t ldb, int32_t m,
+                             int32_t n, int32_t k, void* y, void* dy, int64_t ldc, void* stream);
+/* The matmul with a multiplicative epilogue, as the nanoGPT plan runs the
+ * fc2 VJP through the GELU: C = (op(A) @ op(B)) * aux elementwise (the `*`
+ * VJP rule fused into the dot_general, reverse.rs:551-583), aux [M,N] with
+ * row stride ldaux in the element type; trans_a / trans_b as sb_op_matmul. */
+SB_API int sb_op_matmul_mul(uint32_t elem, const void* a, int64_t lda, int trans_a, const void* b, int64_t ldb,
+                            int trans_b, int32_t m, int32_t n, int32_t k, const void* aux, int64_t ldaux, void* c,
+                            int64_t ldc, void* stream);
 
 /* Layer norm without beta over the last dim (examples/nanogpt/model.shf:11-14:
  * (x - mean) / sqrt(var + 1e-5) * gamma, two-pass population variance as in

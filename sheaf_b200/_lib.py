@@ -48,6 +48,10 @@ SIGNATURES: dict[str, tuple] = {
     # sheaf_b200_ops.h
     "sb_op_matmul": (C.c_int, [C.c_uint32, _P, C.c_int64, C.c_int, _P, C.c_int64, C.c_int, C.c_int32, C.c_int32,
                                C.c_int32, _P, C.c_int64, C.c_uint32, _P, C.c_size_t, _P]),
+    "sb_op_matmul_gelu": (C.c_int, [C.c_uint32, _P, C.c_int64, _P, C.c_int64, C.c_int32, C.c_int32, C.c_int32, _P,
+                                    _P, C.c_int64, _P]),
+    "sb_op_matmul_mul": (C.c_int, [C.c_uint32, _P, C.c_int64, C.c_int, _P, C.c_int64, C.c_int, C.c_int32, C.c_int32,
+                                   C.c_int32, _P, C.c_int64, _P, C.c_int64, _P]),
     "sb_op_matmul_workspace_size": (C.c_size_t, [C.c_uint32, C.c_int, C.c_int, C.c_int32, C.c_int32, C.c_int32]),
     "sb_op_layernorm_fwd": (C.c_int, [C.c_uint32, _P, _P, _P, _P, _P, C.c_int32, C.c_int32, _P]),
     "sb_op_layernorm_bwd_workspace_size": (C.c_size_t, [C.c_int32, C.c_int32]),

@@ -63,6 +63,40 @@ int sb_op_matmul(uint32_t elem, const void* a, int64_t lda, int trans_a, const v
   return sb::gemm_f32(d, static_cast<float*>(workspace), workspace_bytes, s, sb::device_error_word());
 }
 
+int sb_op_matmul_gelu(uint32_t elem, const void* a, int64_t lda, const void* b, int64_t ldb, int32_t m, int32_t n,
+                      int32_t k, void* y, void* dy, int64_t ldc, void* stream) {
+  sb::GemmDesc d;
+  if (!a || !b || !y || !dy) return SB_OPERR_ARGS;
+  if (!sb::fill_matmul_desc(d, elem, a, lda, 0, b, ldb, 1, m, n, k)) return SB_OPERR_ARGS;
+  d.out = y;
+  d.ldo = ldc;
+  d.out_f32 = elem == SB_ELEM_F32;
+  d.epi = sb::EPI_GELU;
+  d.out2 = dy;
+  d.ldo2 = ldc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (elem == SB_ELEM_BF16) return sb::gemm_bf16(d, nullptr, 0, s, sb::device_error_word());
+  return sb::gemm_f32(d, nullptr, 0, s, sb::device_error_word());
+}
+
+int sb_op_matmul_mul(uint32_t elem, const void* a, int64_t lda, int trans_a, const void* b, int64_t ldb, int trans_b,
+                     int32_t m, int32_t n, int32_t k, const void* aux, int64_t ldaux, void* c, int64_t ldc,
+                     void* stream) {
+  sb::GemmDesc d;
+  if (!a || !b || !aux || !c) return SB_OPERR_ARGS;
+  if (!sb::fill_matmul_desc(d, elem, a, lda, trans_a, b, ldb, trans_b, m, n, k)) return SB_OPERR_ARGS;
+  d.out = c;
+  d.ldo = ldc;
+  d.out_f32 = elem == SB_ELEM_F32;
+  d.epi = sb::EPI_MUL;
+  d.aux = aux;
+  d.ldaux = ldaux;
+  d.aux_f32 = elem == SB_ELEM_F32;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (elem == SB_ELEM_BF16) return sb::gemm_bf16(d, nullptr, 0, s, sb::device_error_word());
+  return sb::gemm_f32(d, nullptr, 0, s, sb::device_error_word());
+}
+
 static bool float_elem(uint32_t e) { return e == SB_ELEM_BF16 || e == SB_ELEM_F32; }
 
 int sb_op_layernorm_fwd(uint32_t elem, const void* x, const void* gamma, void* y, void* mean, void* rstd,

@@ -111,3 +111,79 @@ def test_matmul_bf16_output(M, N, K, ldc, cuda):
     # sum |a_k b_k| (it dominates where the dot product cancels)
     acc_err = K * 2.0 ** -24 * (a.double().abs() @ b.double().abs().t())
     assert (diff <= 2.0 ** -8 * (ref.abs() + exact.abs()) + 2 * acc_err).all()
+
+
+@pytest.mark.parametrize("kind,M,N,K", [("bf16", 16384, 1536, 384), ("bf16", 300, 520, 128), ("f32", 300, 520, 128)])
+def test_matmul_gelu(kind, M, N, K, cuda):
+    """The fc layer's fused epilogue (sb_op_matmul_gelu): y = gelu(u) and
+    dy = gelu'(u) for u = A @ B^T, u rounded to bf16 first on the bf16 path
+    (the module's dot_general result type). Oracle: lib/nn.shf:10-11 and its
+    VJP in fp64 (oracle.ops)."""
+    import numpy as np
+    import torch
+    import sheaf_b200 as sb
+
+    from oracle import dtype as odt
+    from oracle import ops
+
+    bf = kind == "bf16"
+    elem = sb.ELEM_BF16 if bf else sb.ELEM_F32
+    dt = torch.bfloat16 if bf else torch.float32
+    g = torch.Generator(device="cpu").manual_seed(M + N + K)
+    a = (torch.randn(M, K, generator=g) * 0.1).to(dt)
+    b = (torch.randn(N, K, generator=g) * 0.1).to(dt)
+    y = torch.full((M, N), float("nan"), dtype=dt, device=cuda)
+    dy = torch.full((M, N), float("nan"), dtype=dt, device=cuda)
+    L = sb.lib()
+    ad, bd = a.to(cuda), b.to(cuda)
+    rc = L.sb_op_matmul_gelu(elem, ad.data_ptr(), K, bd.data_ptr(), K, M, N, K, y.data_ptr(), dy.data_ptr(), N,
+                             torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert L.sb_op_device_error() == 0
+    u = a.double().numpy() @ b.double().numpy().T
+    if bf:
+        u = odt.round_bf16(u.astype(np.float32)).astype(np.float64)
+    ey = ops.gelu(u)
+    edy = ops.gelu_vjp(u, np.ones_like(u))
+    tol = 2e-2 if bf else 1e-5
+    for got, ref, nm in ((y, ey, "gelu"), (dy, edy, "gelu'")):
+        gg = got.float().cpu().double().numpy()
+        assert np.isfinite(gg).all(), nm
+        err = np.abs(gg - ref)
+        assert err.max() <= tol * np.abs(ref).max(), (nm, err.max())
+        assert (err <= tol * (1 + np.abs(ref))).all(), nm
+
+
+@pytest.mark.parametrize("kind,M,N,K,tb", [("bf16", 16384, 1536, 384, 0), ("bf16", 300, 520, 128, 1),
+                                           ("f32", 300, 520, 128, 0)])
+def test_matmul_mul(kind, M, N, K, tb, cuda):
+    """C = (A @ op(B)) * aux (sb_op_matmul_mul), the fc2 VJP through gelu'
+    of the nanoGPT plan: the product rounded once, on the bf16 path, after
+    the multiply in f32."""
+    import numpy as np
+    import torch
+    import sheaf_b200 as sb
+
+    bf = kind == "bf16"
+    elem = sb.ELEM_BF16 if bf else sb.ELEM_F32
+    dt = torch.bfloat16 if bf else torch.float32
+    g = torch.Generator(device="cpu").manual_seed(M + 3 * N + K)
+    a = (torch.randn(M, K, generator=g) * 0.1).to(dt)
+    b_log = (torch.randn(K, N, generator=g) * 0.1).to(dt)
+    b = b_log.t().contiguous() if tb else b_log
+    aux = torch.randn(M, N, generator=g).to(dt)
+    c = torch.full((M, N), float("nan"), dtype=dt, device=cuda)
+    L = sb.lib()
+    ad, bd, xd = a.to(cuda), b.to(cuda), aux.to(cuda)
+    rc = L.sb_op_matmul_mul(elem, ad.data_ptr(), K, 0, bd.data_ptr(), bd.stride(0), tb, M, N, K, xd.data_ptr(), N,
+                            c.data_ptr(), N, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert L.sb_op_device_error() == 0
+    ref = (a.double().numpy() @ b_log.double().numpy()) * aux.double().numpy()
+    got = c.float().cpu().double().numpy()
+    tol = 2e-2 if bf else 1e-5
+    err = np.abs(got - ref)
+    assert np.isfinite(got).all() and err.max() <= tol * np.abs(ref).max()
+    assert (err <= tol * (1 + np.abs(ref))).all()
