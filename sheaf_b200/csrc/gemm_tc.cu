@@ -304,7 +304,12 @@ __global__ void __launch_bounds__(384, 1)
     // Writes the warp's 32-row x 128-byte block into a swizzled staging slot
     // and stores it with a bulk tensor store, or, with `accumulate`, adds it
     // into global memory with a bulk tensor reduce-add (the add runs in L2).
-    auto stage = [&](const uint32_t(&w)[32], const CUtensorMap* map, int x, int y, bool accumulate) {
+    // L2 policy for outputs nothing reads soon (gelu'(u), read by the VJP
+    // only): evict first, so they do not push the next kernel's operands out
+    uint64_t evict_first_policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(evict_first_policy));
+    auto stage = [&](const uint32_t(&w)[32], const CUtensorMap* map, int x, int y, bool accumulate,
+                     bool evict_first = false) {
       const uint32_t slot = stg + (cc % kSlots) * kSlotBytes;
       if (cc >= static_cast<uint32_t>(kSlots)) {
         if (lane == 0) bulk_wait_read<kSlots - 1>();
@@ -319,6 +324,12 @@ __global__ void __launch_bounds__(384, 1)
                            "l"(reinterpret_cast<uint64_t>(map)),
                        "r"(slot), "r"(x), "r"(y)
                        : "memory");
+        else if (evict_first)
+          asm volatile(
+              "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+                  reinterpret_cast<uint64_t>(map)),
+              "r"(slot), "r"(x), "r"(y), "l"(evict_first_policy)
+              : "memory");
         else
           asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                            reinterpret_cast<uint64_t>(map)),
@@ -418,7 +429,7 @@ __global__ void __launch_bounds__(384, 1)
               g[16 + j] = pack_bf16x2(d2, d3);
             }
             stage(w, &tmC, col0, store_y, false);
-            stage(g, &tmC2, col0, store_y, false);
+            stage(g, &tmC2, col0, store_y, false, true);
           } else {  // EPI_MUL: acc * aux (bf16)
             uint32_t uw[32];
             if (row < a.M) {
