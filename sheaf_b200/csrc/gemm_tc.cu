@@ -111,6 +111,12 @@ constexpr size_t smem_bytes_for() {
 // `tfull` barriers of both CTAs; each CTA's epilogue drains the 128
 // accumulator rows in its own TMEM and arrives on rank 0's `tempty`. Halving
 // the B bytes per SM leaves room for deeper operand pipelines.
+//
+// BN = 384 (pairs only) covers N = 384 in one tile with two UMMAs per K step,
+// N = 256 into accumulator columns 0..255 and N = 128 into 256..383; each CTA
+// holds B rows 128r .. +127 and 256 + 64r .. +63 of the tile. One 384-column
+// accumulator fills the TMEM, so there is a single accumulator buffer. Per
+// byte of operands loaded it does twice the MMA work of 192-wide tiles.
 template <int BN, bool A_MN, bool B_MN, int STAGES, bool PAIR>
 __global__ void __launch_bounds__(384, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -119,7 +125,9 @@ __global__ void __launch_bounds__(384, 1)
   constexpr uint32_t kBBytes = BH * kBK * 2;
   constexpr uint32_t kTmemCols = tmem_cols_for(BN);
   constexpr int kRowsPerTile = PAIR ? 2 * kBM : kBM;
-  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "tile width must be 64, 128, 192 or 256");
+  constexpr bool kWide = PAIR && BN == 384;
+  constexpr int kAcc = kWide ? 1 : 2;  // accumulator buffers in TMEM
+  static_assert(BN % 64 == 0 && BN >= 64 && (BN <= 256 || kWide), "tile width must be 64, 128, 192, 256 (or 384 on pairs)");
   static_assert(!PAIR || (BH % 64 == 0), "pair tiles split B into 64-row halves");
 
   extern __shared__ uint8_t smem_raw[];
@@ -211,7 +219,18 @@ __global__ void __launch_bounds__(384, 1)
               tma_load_2d_pair(da, &tmA, fb, arow, kb * kBK);
               tma_load_2d_pair(da + 8192, &tmA, fb, arow + 64, kb * kBK);
             }
-            if (!B_MN) {
+            if constexpr (kWide) {
+              // three 64-row (K-major) or 64-column (MN-major) boxes: rows
+              // 128r, 128r + 64 (N = 256 UMMA) and 256 + 64r (N = 128 UMMA)
+#pragma unroll
+              for (int j = 0; j < 3; ++j) {
+                const int pos = nt * BN + (j < 2 ? static_cast<int>(rank) * 128 + j * 64 : 256 + static_cast<int>(rank) * 64);
+                if (!B_MN)
+                  tma_load_2d_pair(db + j * 8192, &tmB, fb, kb * kBK, pos);
+                else
+                  tma_load_2d_pair(db + j * 8192, &tmB, fb, pos, kb * kBK);
+              }
+            } else if (!B_MN) {
               tma_load_2d_pair(db, &tmB, fb, kb * kBK, brow);
             } else {
 #pragma unroll
@@ -241,15 +260,16 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(kRowsPerTile, BN, A_MN, B_MN);
+      constexpr uint32_t idesc = make_idesc_bf16(kRowsPerTile, kWide ? 256 : BN, A_MN, B_MN);
+      constexpr uint32_t idesc_hi = make_idesc_bf16(kRowsPerTile, 128, A_MN, B_MN);  // wide tiles' N = 128 part
       uint32_t it = 0;
       int local = 0;
       for (int u = cta0; u < units; u += ncta, ++local) {
         const int split = u % a.splits;
         const int kb0 = split * a.kb_per_split;
         const int kb1 = min(a.kb_total, kb0 + a.kb_per_split);
-        const int as = local & 1;
-        const uint32_t aph = (local >> 1) & 1;
+        const int as = local % kAcc;
+        const uint32_t aph = (local / kAcc) & 1;
         if (!mbar_wait(&tempty[as], aph ^ 1, a.err, abort_flag)) goto done;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + as * BN;
@@ -266,10 +286,16 @@ __global__ void __launch_bounds__(384, 1)
                                      : make_sw128_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? make_sw128_desc(b_addr + kk * 2048, 8192, 1024)
                                      : make_sw128_desc(b_addr + kk * 32, 16, 1024);
-            if constexpr (PAIR)
+            if constexpr (kWide) {
+              const uint64_t bd_hi = B_MN ? make_sw128_desc(b_addr + 16384 + kk * 2048, 8192, 1024)
+                                          : make_sw128_desc(b_addr + 16384 + kk * 32, 16, 1024);
               umma_f16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
-            else
+              umma_f16_pair(d_tmem + 256, ad, bd_hi, idesc_hi, (kb > kb0 || kk > 0) ? 1u : 0u);
+            } else if constexpr (PAIR) {
+              umma_f16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            } else {
               umma_f16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            }
           }
           if constexpr (PAIR)
             umma_commit_pair(&empty[s]);
@@ -283,9 +309,9 @@ __global__ void __launch_bounds__(384, 1)
       }
       if constexpr (PAIR) {
         // the peer's epilogue arrives remotely on tempty: wait for the
-        // releases of the last two accumulator buffers before leaving
-        for (int i = 0; i < 2; ++i, ++local)
-          if (!mbar_wait(&tempty[local & 1], ((local >> 1) & 1) ^ 1, a.err, abort_flag)) break;
+        // releases of the last accumulator buffers before leaving
+        for (int i = 0; i < kAcc; ++i, ++local)
+          if (!mbar_wait(&tempty[local % kAcc], ((local / kAcc) & 1) ^ 1, a.err, abort_flag)) break;
       }
     }
   } else if (warp >= 4) {
@@ -345,8 +371,8 @@ __global__ void __launch_bounds__(384, 1)
       const int split = u % a.splits;
       const int tile = u / a.splits;
       const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
-      const int as = local & 1;
-      const uint32_t aph = (local >> 1) & 1;
+      const int as = local % kAcc;
+      const uint32_t aph = (local / kAcc) & 1;
       const int row0 = mt * kRowsPerTile + static_cast<int>(rank) * kBM + q * 32;
       const int row = row0 + lane;
       if ((a.epi == EPI_ADD || a.epi == EPI_MUL) && row < a.M) {
@@ -591,7 +617,7 @@ int launch_tc(const GemmDesc& d, const GemmArgs& args, void* out, long ldo, long
     ok = make_map_bf16(&ta, d.A, d.K, d.M, d.lda, 64, kBK);
   if (!ok) return 2;
   if (!B_MN)
-    ok = make_map_bf16(&tb, d.B, d.N, d.K, d.ldb, kBK, PAIR ? BN / 2 : BN);
+    ok = make_map_bf16(&tb, d.B, d.N, d.K, d.ldb, kBK, PAIR ? (BN == 384 ? 64 : BN / 2) : BN);
   else
     ok = make_map_bf16(&tb, d.B, d.K, d.N, d.ldb, 64, kBK);
   if (!ok) return 2;
@@ -683,7 +709,15 @@ Plan plan_for(const GemmDesc& d) {
   // 256-row tiles on CTA pairs for tiles 256 or 128 wide (192-wide pair tiles
   // measured slower in the step) when padding M to 256 rows wastes little
   // (M = 384 would run 512 rows: a third more work per SM than 128-row tiles)
-  p.pair = (p.bn == 256 || p.bn == 128) && d.pair != 0 && (d.M % (2 * kBM) == 0 || d.M >= 4096);
+  // 257..384 columns: one 384-wide pair tile per 256 rows instead of two
+  // 192-wide tiles per 128 rows (half the operand bytes per MMA), over many
+  // rows or a long K (the dW GEMMs); a short-K GEMM over few rows runs one
+  // tile per pair, where the single accumulator buffer costs more than that
+  // saves (measured slower for M = 1024..8192 at K = 384)
+  const bool pair_rows = d.pair != 0 && (d.M % (2 * kBM) == 0 || d.M >= 4096);
+  if (d.bn == 0 && p.bn == 192 && d.N > 256 && d.N <= 384 && pair_rows && (d.M >= 4096 || d.K >= 4096))
+    p.bn = 384;
+  p.pair = p.bn == 384 || ((p.bn == 256 || p.bn == 128) && pair_rows);
   p.rows_per_tile = p.pair ? 2 * kBM : kBM;
   p.m_tiles = (d.M + p.rows_per_tile - 1) / p.rows_per_tile;
   p.n_tiles = (d.N + p.bn - 1) / p.bn;
@@ -795,6 +829,7 @@ int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaS
       rc = p.pair ? dispatch_major<256, 5, true>(d, a, out, ldo, rows, grid, s)
                   : dispatch_major<256, 4, false>(d, a, out, ldo, rows, grid, s);
       break;
+    case 384: rc = dispatch_major<384, 4, true>(d, a, out, ldo, rows, grid, s); break;
     case 192: rc = dispatch_major<192, 4, false>(d, a, out, ldo, rows, grid, s); break;
     case 128:
       rc = p.pair ? dispatch_major<128, 6, true>(d, a, out, ldo, rows, grid, s)

@@ -36,7 +36,7 @@ struct GemmDesc {
   void* out2 = nullptr;
   long ldo2 = 0;
   int splits = 0;  // 0 = choose; 1 = no split-K (split-K only with EPI_STORE)
-  int bn = 0;      // 0 = choose tile width
+  int bn = 0;      // 0 = choose tile width (64, 128, 192, 256; 384 runs on CTA pairs)
   int pair = -1;   // 256-row tiles on CTA pairs: -1 = when the tile allows, 0 = never
 };
 

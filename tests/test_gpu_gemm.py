@@ -26,6 +26,9 @@ CASES = [
     (512, 1536, 4096, 1, 0, 0, 0),  # CTA-pair tiles with split-K
     (4160, 256, 256, 0, 1, 0, 0),  # CTA pairs, the last pair tile half outside M
     (16384, 1152, 384, 0, 1, 0, 0),  # 256-wide pair tiles, the last column of tiles half outside N
+    (16384, 384, 384, 0, 1, 0, 0),  # 384-wide pair tiles (N = 256 + 128 UMMAs), K-major B
+    (8192, 384, 1536, 0, 0, 0, 0),  # 384-wide pair tiles, MN-major B
+    (4096, 300, 256, 1, 1, 0, 4),  # 384-wide pair tiles, columns past N (the N = 128 part partly empty)
 ]
 
 
