@@ -729,6 +729,7 @@ Plan plan_for(const GemmDesc& d) {
     const int slots = p.pair ? num_sms() / 2 : num_sms();  // tiles in flight at once
     if (d.epi == EPI_STORE && d.N % 4 == 0 && tiles * 2 <= slots && p.kb_total >= 8)
       splits = std::min(slots / tiles, p.kb_total / 4);
+    if (d.max_splits > 0) splits = std::min(splits, d.max_splits);
   }
   if (d.epi != EPI_STORE || d.N % 4 != 0) splits = 1;  // partial rows of N floats must be 16-byte multiples
   splits = std::max(1, std::min(splits, p.kb_total));
