@@ -714,7 +714,8 @@ Plan plan_for(const GemmDesc& d) {
   // rows or a long K (the dW GEMMs); a short-K GEMM over few rows runs one
   // tile per pair, where the single accumulator buffer costs more than that
   // saves (measured slower for M = 1024..8192 at K = 384)
-  const bool pair_rows = d.pair != 0 && (d.M % (2 * kBM) == 0 || d.M >= 4096);
+  const bool long_k = d.K >= 4096 && d.M >= 1024;  // dW GEMMs: a half-empty last pair tile costs little
+  const bool pair_rows = d.pair != 0 && (d.M % (2 * kBM) == 0 || d.M >= 4096 || long_k);
   if (d.bn == 0 && p.bn == 192 && d.N > 256 && d.N <= 384 && pair_rows && (d.M >= 4096 || d.K >= 4096))
     p.bn = 384;
   p.pair = p.bn == 384 || ((p.bn == 256 || p.bn == 128) && pair_rows);
