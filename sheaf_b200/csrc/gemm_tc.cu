@@ -334,13 +334,18 @@ __global__ void __launch_bounds__(384, 1)
     // only): evict first, so they do not push the next kernel's operands out
     uint64_t evict_first_policy;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(evict_first_policy));
-    auto stage = [&](const uint32_t(&w)[32], const CUtensorMap* map, int x, int y, bool accumulate,
-                     bool evict_first = false) {
+    // the next staging slot, once the bulk store that last used it has read it
+    auto acquire_slot = [&]() {
       const uint32_t slot = stg + (cc % kSlots) * kSlotBytes;
       if (cc >= static_cast<uint32_t>(kSlots)) {
         if (lane == 0) bulk_wait_read<kSlots - 1>();
         __syncwarp();
       }
+      return slot;
+    };
+    auto stage = [&](const uint32_t(&w)[32], const CUtensorMap* map, int x, int y, bool accumulate,
+                     bool evict_first = false, uint32_t held_slot = 0) {
+      const uint32_t slot = held_slot ? held_slot : acquire_slot();
       st_row128_sw(slot, lane, w);
       fence_proxy_async_smem();
       __syncwarp();
@@ -457,30 +462,45 @@ __global__ void __launch_bounds__(384, 1)
             stage(w, &tmC, col0, store_y, false);
             stage(g, &tmC2, col0, store_y, false, true);
           } else {  // EPI_MUL: acc * aux (bf16)
-            uint32_t uw[32];
-            if (row < a.M) {
-              const __nv_bfloat16* up =
-                  static_cast<const __nv_bfloat16*>(a.aux) + static_cast<long>(row) * a.ldaux + col0;
-              if (col0 + 64 <= a.N) {
+            // The warp's 32 x 64 aux block goes through the staging slot the
+            // result will leave from: coalesced loads (4 rows of 128 B per
+            // instruction) into the swizzled slot, then each lane reads its
+            // own row (a row per lane straight from global memory touches 32
+            // lines per instruction).
+            const __nv_bfloat16* ab = static_cast<const __nv_bfloat16*>(a.aux);
+            const int ch = lane & 7;
+            uint4 av[8];  // all eight loads in flight before any is stored
 #pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                  const uint4 r = *reinterpret_cast<const uint4*>(up + 2 * j);
-                  uw[j] = r.x;
-                  uw[j + 1] = r.y;
-                  uw[j + 2] = r.z;
-                  uw[j + 3] = r.w;
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                  const uint16_t lo = (col0 + 2 * j < a.N) ? reinterpret_cast<const uint16_t*>(up)[2 * j] : 0;
-                  const uint16_t hi = (col0 + 2 * j + 1 < a.N) ? reinterpret_cast<const uint16_t*>(up)[2 * j + 1] : 0;
-                  uw[j] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+            for (int k = 0; k < 8; ++k) {
+              const int grow = row0 + 4 * k + (lane >> 3), gcol = col0 + 8 * ch;
+              av[k] = make_uint4(0u, 0u, 0u, 0u);
+              if (grow < a.M) {
+                const __nv_bfloat16* src = ab + static_cast<long>(grow) * a.ldaux + gcol;
+                if (gcol + 8 <= a.N) {
+                  av[k] = *reinterpret_cast<const uint4*>(src);
+                } else if (gcol < a.N) {
+                  uint32_t e[4] = {0u, 0u, 0u, 0u};
+                  for (int t = 0; t < 8 && gcol + t < a.N; ++t)
+                    e[t >> 1] |= static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(src)[t]) << (16 * (t & 1));
+                  av[k] = make_uint4(e[0], e[1], e[2], e[3]);
                 }
               }
-            } else {
+            }
+            const uint32_t slot = acquire_slot();
 #pragma unroll
-              for (int j = 0; j < 32; ++j) uw[j] = 0;
+            for (int k = 0; k < 8; ++k) {
+              const int r = 4 * k + (lane >> 3);
+              st_shared_v4(slot + r * 128 + ((ch ^ (r & 7)) << 4), av[k].x, av[k].y, av[k].z, av[k].w);
+            }
+            __syncwarp();
+            uint32_t uw[32];
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+              const uint4 t = ld_shared_v4(slot + lane * 128 + ((ch ^ (lane & 7)) << 4));
+              uw[4 * ch] = t.x;
+              uw[4 * ch + 1] = t.y;
+              uw[4 * ch + 2] = t.z;
+              uw[4 * ch + 3] = t.w;
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -489,7 +509,7 @@ __global__ void __launch_bounds__(384, 1)
               w[16 + j] = pack_bf16x2(__uint_as_float(v1[2 * j]) * bf16_bits_to_f32(uw[16 + j] & 0xFFFFu),
                                       __uint_as_float(v1[2 * j + 1]) * bf16_bits_to_f32(uw[16 + j] >> 16));
             }
-            stage(w, &tmC, col0, store_y, false);
+            stage(w, &tmC, col0, store_y, false, false, slot);  // each lane overwrites only its own row
           }
         }
       }

@@ -144,6 +144,12 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 
 // Writes one 128-byte row (8 x 16 B) of a 128B-swizzled tile: chunk k of row
 // r lands at (k ^ (r % 8)) * 16, the layout TMA and UMMA use for SWIZZLE_128B.
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_row128_sw(uint32_t tile, int r, const uint32_t (&w)[32]) {
   const uint32_t row = tile + r * 128;
 #pragma unroll
