@@ -314,17 +314,26 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
         }
         tc_fence_before();
       }
-      if (ok && q < a.T) {
+      if (ok) {
+        // O leaves through the (now idle) P buffer: each lane writes its row
+        // swizzled, then every store instruction covers 4 rows x 128 B
+        // (a row per lane straight to global memory touches 32 lines)
         const float inv = 1.f / l;
-        __nv_bfloat16* orow = a.out + static_cast<long>(row0 + q) * a.D + h * kHd;
+        uint32_t w[32];
 #pragma unroll
-        for (int i = 0; i < 64; i += 8) {
-          uint4 pk = make_uint4(pack_bf16x2(o[i] * inv, o[i + 1] * inv), pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv),
-                                pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv), pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv));
-          *reinterpret_cast<uint4*>(orow + i) = pk;
+        for (int i = 0; i < 32; ++i) w[i] = pack_bf16x2(o[2 * i] * inv, o[2 * i + 1] * inv);
+        st_row128_sw(p_addr, r, w);
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int rr = quarter * 32 + 4 * k + (lane >> 3), ch = lane & 7;
+          const uint4 v = ld_shared_v4(p_addr + rr * 128 + ((ch ^ (rr & 7)) << 4));
+          if (qt * kT + rr < a.T)
+            *reinterpret_cast<uint4*>(a.out + static_cast<long>(row0 + qt * kT + rr) * a.D + h * kHd + ch * 8) = v;
         }
+        __syncwarp();  // the next item's P rows overwrite what the other lanes read
         // natural-log log-sum-exp of the scaled scores
-        a.lse[static_cast<long>(bh) * a.T + q] = (m + log2f(l)) / kLog2e;
+        if (q < a.T) a.lse[static_cast<long>(bh) * a.T + q] = (m + log2f(l)) / kLog2e;
       }
     }
   }
@@ -557,27 +566,40 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
     // Per query row of tile i of head bh into buffer s: lse (log2 units) and
     // delta * scale, delta = rowsum(dO * O). Issued one tile ahead so that
     // the global loads overlap the previous tile's UMMAs.
+    // delta of the warp's 32 rows with coalesced loads: instruction k reads
+    // rows 4k .. 4k+3 (eight lanes a row, 16 bytes each; all sixteen loads
+    // in flight first), the eight partial dot products of a row are summed
+    // by shuffles.
     auto load_row_stats = [&](const BwdItem& w, int i, int s) {
       const int q = i * kT + tid;
-      float dl = 0.f;
-      if (q < a.T) {
-        const long off = static_cast<long>(w.row0 + q) * a.D + w.h * kHd;
+      const int ch = lane & 7;
+      uint4 ov[8], dv[8];
 #pragma unroll
-        for (int u = 0; u < kHd; u += 8) {
-          const uint4 ov = *reinterpret_cast<const uint4*>(a.o + off + u);
-          const uint4 dv = *reinterpret_cast<const uint4*>(a.dout + off + u);
-          const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            dl += bf16_bits_to_f32(static_cast<uint16_t>(ow[k] & 0xFFFFu)) *
-                  bf16_bits_to_f32(static_cast<uint16_t>(dw[k] & 0xFFFFu));
-            dl += bf16_bits_to_f32(static_cast<uint16_t>(ow[k] >> 16)) *
-                  bf16_bits_to_f32(static_cast<uint16_t>(dw[k] >> 16));
-          }
+      for (int k = 0; k < 8; ++k) {
+        const int qk = i * kT + quarter * 32 + 4 * k + (lane >> 3);
+        ov[k] = dv[k] = make_uint4(0u, 0u, 0u, 0u);
+        if (qk < a.T) {
+          const long off = static_cast<long>(w.row0 + qk) * a.D + w.h * kHd + ch * 8;
+          ov[k] = *reinterpret_cast<const uint4*>(a.o + off);
+          dv[k] = *reinterpret_cast<const uint4*>(a.dout + off);
         }
       }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t ow[4] = {ov[k].x, ov[k].y, ov[k].z, ov[k].w}, dw[4] = {dv[k].x, dv[k].y, dv[k].z, dv[k].w};
+        float dl = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          dl += bf16_bits_to_f32(static_cast<uint16_t>(ow[e] & 0xFFFFu)) *
+                bf16_bits_to_f32(static_cast<uint16_t>(dw[e] & 0xFFFFu));
+          dl += bf16_bits_to_f32(static_cast<uint16_t>(ow[e] >> 16)) * bf16_bits_to_f32(static_cast<uint16_t>(dw[e] >> 16));
+        }
+        dl += __shfl_xor_sync(0xffffffffu, dl, 4);
+        dl += __shfl_xor_sync(0xffffffffu, dl, 2);
+        dl += __shfl_xor_sync(0xffffffffu, dl, 1);
+        if (ch == 0) sDel[s * kT + quarter * 32 + 4 * k + (lane >> 3)] = dl * a.scale;
+      }
       sLse[s * kT + tid] = (q < a.T) ? a.lse[static_cast<long>(w.bh) * a.T + q] * kLog2e : INFINITY;
-      sDel[s * kT + tid] = dl * a.scale;
       __syncwarp();
       if (lane == 0) mbar_arrive(&stats_full[s]);
     };
