@@ -79,6 +79,15 @@ __device__ __forceinline__ uint64_t mndesc(uint32_t tile, int kk, uint32_t lbo) 
   return make_sw128_desc(tile + kk * 2048, lbo, 1024);
 }
 
+// j-th work item of this CTA. Items come longest first; rounds of gridDim.x
+// items alternate direction, so the CTAs that took the last long items of one
+// round take the first short ones of the next and no CTA ends up with a long
+// item more than the others plus a short one.
+__device__ __forceinline__ int item_of(int j) {
+  const int g = static_cast<int>(gridDim.x), b = static_cast<int>(blockIdx.x);
+  return j * g + ((j & 1) ? g - 1 - b : b);
+}
+
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
@@ -152,7 +161,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
       uint32_t c = 0;
       int j = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++j) {
+      for (int u = item_of(j); u < nitems && ok; u = item_of(++j)) {
         int qt, bh, h, row0;
         fwd_item(a, u, qt, bh, h, row0);
         const int qb = j & 1;
@@ -191,7 +200,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
       uint32_t c = 0;
       int j = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++j) {
+      for (int u = item_of(j); u < nitems && ok; u = item_of(++j)) {
         int qt, bh, h, row0;
         fwd_item(a, u, qt, bh, h, row0);
         const int qb = j & 1;
@@ -229,7 +238,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
     const uint32_t p_addr = smem_u32(sP);
     uint32_t c = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x) {
+    int n = 0;  // items of this CTA
+    for (int u = item_of(n); u < nitems && ok; u = item_of(++n)) {
       int qt, bh, h, row0;
       fwd_item(a, u, qt, bh, h, row0);
       const int q = qt * kT + r;
@@ -457,7 +467,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
       uint32_t g = 0;  // query tiles loaded by this CTA
       int j = 0;       // items of this CTA
       bool ok = true;
-      for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++j) {
+      for (int u = item_of(j); u < nitems && ok; u = item_of(++j)) {
         const BwdItem w = bwd_item(a, u);
         const int kb = j & 1;
         if (!mbar_wait(&kv_empty[kb], ((j >> 1) & 1) ^ 1, a.err, abort_flag)) {
@@ -496,7 +506,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
       uint32_t g = 0;
       int j = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++j) {
+      for (int u = item_of(j); u < nitems && ok; u = item_of(++j)) {
         const BwdItem w = bwd_item(a, u);
         const int kb = j & 1;
         if (!mbar_wait(&kv_full[kb], (j >> 1) & 1, a.err, abort_flag)) {
@@ -561,6 +571,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
     const int tid = quarter * 32 + lane;  // 0..127: key row (S^T, dK, dV) / query row (dQ)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl = a.scale * kLog2e;
+    const float2 sl2 = make_float2(sl, sl), sc2 = make_float2(a.scale, a.scale);
     const uint32_t pt_addr = smem_u32(sPT), dst_addr = smem_u32(sdST);
     const uint32_t stg = smem_u32(sStg) + (warp - 2) * 4096;
     // Per query row of tile i of head bh into buffer s: lse (log2 units) and
@@ -613,7 +624,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
       const BwdItem w0 = bwd_item(a, blockIdx.x);
       load_row_stats(w0, w0.kt, 0);
     }
-    for (int u = blockIdx.x; u < nitems && ok; u += gridDim.x, ++j) {
+    for (int u = item_of(j); u < nitems && ok; u = item_of(++j)) {
       const BwdItem w = bwd_item(a, u);
       const int key = w.kt * kT + tid;
       for (int it = 0; it < w.nq; ++it, ++g) {
@@ -650,18 +661,28 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
             for (int t = 0; t < 32; t += 4) {
               const float4 l4 = *reinterpret_cast<const float4*>(lse2 + c * 32 + t);
               const float4 d4 = *reinterpret_cast<const float4*>(del + c * 32 + t);
-              const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dl[4] = {d4.x, d4.y, d4.z, d4.w};
-              float p[4], d[4];
+              // packed f32x2 arithmetic: the same single-precision fma / mul
+              // per element, one instruction per pair
+              const float2 e01 = __ffma2_rn(make_float2(__uint_as_float(sv[t]), __uint_as_float(sv[t + 1])), sl2,
+                                            make_float2(-l4.x, -l4.y));
+              const float2 e23 = __ffma2_rn(make_float2(__uint_as_float(sv[t + 2]), __uint_as_float(sv[t + 3])), sl2,
+                                            make_float2(-l4.z, -l4.w));
+              float p[4] = {ex2_approx(e01.x), ex2_approx(e01.y), ex2_approx(e23.x), ex2_approx(e23.y)};
+              if (part) {
 #pragma unroll
-              for (int uu = 0; uu < 4; ++uu) {
-                p[uu] = ex2_approx(fmaf(__uint_as_float(sv[t + uu]), sl, -lv[uu]));
-                if (part && t + uu < lane) p[uu] = 0.f;
-                d[uu] = p[uu] * fmaf(__uint_as_float(dv[t + uu]), a.scale, -dl[uu]);
+                for (int uu = 0; uu < 4; ++uu)
+                  if (t + uu < lane) p[uu] = 0.f;
               }
+              const float2 f01 = __ffma2_rn(make_float2(__uint_as_float(dv[t]), __uint_as_float(dv[t + 1])), sc2,
+                                            make_float2(-d4.x, -d4.y));
+              const float2 f23 = __ffma2_rn(make_float2(__uint_as_float(dv[t + 2]), __uint_as_float(dv[t + 3])), sc2,
+                                            make_float2(-d4.z, -d4.w));
+              const float2 d01 = __fmul2_rn(make_float2(p[0], p[1]), f01);
+              const float2 d23 = __fmul2_rn(make_float2(p[2], p[3]), f23);
               pp[t >> 1] = pack_bf16x2(p[0], p[1]);
               pp[(t >> 1) + 1] = pack_bf16x2(p[2], p[3]);
-              pd[t >> 1] = pack_bf16x2(d[0], d[1]);
-              pd[(t >> 1) + 1] = pack_bf16x2(d[2], d[3]);
+              pd[t >> 1] = pack_bf16x2(d01.x, d01.y);
+              pd[(t >> 1) + 1] = pack_bf16x2(d23.x, d23.y);
             }
           }
           store_row32(pt_addr, tid, c, pp);
@@ -674,8 +695,8 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
         // lse / delta of the next query tile (of this item or the next one)
         if (it + 1 < w.nq) {
           load_row_stats(w, i + 1, s ^ 1);
-        } else if (u + static_cast<int>(gridDim.x) < nitems) {
-          const BwdItem wn = bwd_item(a, u + gridDim.x);
+        } else if (item_of(j + 1) < nitems) {
+          const BwdItem wn = bwd_item(a, item_of(j + 1));
           load_row_stats(wn, wn.kt, s ^ 1);
         }
         // dQ tile partial: TMEM lane = query row of tile i
@@ -758,18 +779,23 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
   }
 }
 
-// dq (bf16, columns [0, D) of dqkv) = dq_acc (f32 [N, D])
-__global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv, long n, int D) {
+// dq (bf16, columns [0, D) of dqkv) = dq_acc (f32 [rows, D]). Block
+// (tx, ty): ty rows, each thread 8 consecutive values of a row per step (two
+// 16-byte loads, one 16-byte store); D is a multiple of 8 (64 per head).
+__global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dqkv, long rows, int D) {
   pdl_wait();
   pdl_trigger();
-  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n / 4;
-       i += static_cast<long>(gridDim.x) * blockDim.x) {
-    const long e = i * 4, r = e / D, c = e % D;
-    const float4 v = reinterpret_cast<const float4*>(acc)[i];
-    uint2 u;
-    u.x = pack_bf16x2(v.x, v.y);
-    u.y = pack_bf16x2(v.z, v.w);
-    *reinterpret_cast<uint2*>(dqkv + r * 3 * D + c) = u;
+  const long r = static_cast<long>(blockIdx.x) * blockDim.y + threadIdx.y;
+  if (r >= rows) return;
+  for (int c = threadIdx.x * 8; c < D; c += blockDim.x * 8) {
+    const float4* src = reinterpret_cast<const float4*>(acc + r * D + c);
+    const float4 v0 = src[0], v1 = src[1];
+    uint4 u;
+    u.x = pack_bf16x2(v0.x, v0.y);
+    u.y = pack_bf16x2(v0.z, v0.w);
+    u.z = pack_bf16x2(v1.x, v1.y);
+    u.w = pack_bf16x2(v1.z, v1.w);
+    *reinterpret_cast<uint4*>(dqkv + r * 3 * D + c) = u;
   }
 }
 
@@ -840,9 +866,9 @@ int attention_bwd_tc(const void* qkv, const void* o, const void* dout, const flo
   const int items = sh.B * sh.H * a.ntiles;
   launch_pdl(attn_bwd_tc, dim3(std::min(items, num_sms())), dim3(192), kBwdSmem, s, tq, td, tdq, tdkv, a);
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
-  const long n = static_cast<long>(N) * D;
-  const int blocks = static_cast<int>(std::min<long>((n / 4 + 255) / 256, 8L * num_sms()));
-  launch_pdl(dq_convert_kernel, dim3(blocks), dim3(256), 0, s, dq_acc, static_cast<__nv_bfloat16*>(dqkv), n, D);
+  const int tx = std::min(D / 8, 128), ty = std::max(1, 384 / tx);
+  launch_pdl(dq_convert_kernel, dim3((N + ty - 1) / ty), dim3(tx, ty), 0, s, dq_acc, static_cast<__nv_bfloat16*>(dqkv),
+             static_cast<long>(N), D);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 

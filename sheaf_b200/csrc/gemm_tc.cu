@@ -82,13 +82,24 @@ __device__ __forceinline__ float tanh_approx(float x) {
 
 // gelu(x) = 0.5 * (x * (1 + tanh(0.7978846 * (x + 0.044715 * (x * (x * x))))))
 // (lib/nn.shf:10-11) and its derivative by the chain rule of those primitive
-// ops, from one tanh: the forward epilogue saves gelu'(u) for the VJP.
-__device__ __forceinline__ void gelu_and_grad(float x, float& g, float& d) {
-  const float x2 = x * x;
-  const float t = tanh_approx(0.7978846f * (x + 0.044715f * (x * x2)));
-  const float hx = 0.5f * x;
-  g = fmaf(hx, t, hx);
-  d = fmaf(0.5f, t, 0.5f) + hx * fmaf(-t, t, 1.0f) * fmaf(0.7978846f * 0.134145f, x2, 0.7978846f);
+// ops, from one tanh: the forward epilogue saves gelu'(u) for the VJP. Two
+// elements at a time with packed f32x2 arithmetic (sm_100: one instruction
+// per pair for each multiply / fma, the same IEEE single-precision operations
+// and roundings as the scalar expressions), which halves the epilogue's
+// floating-point instruction count.
+__device__ __forceinline__ void gelu_and_grad2(float2 x, float2& g, float2& d) {
+  const float2 x2 = __fmul2_rn(x, x);
+  const float2 s = __ffma2_rn(make_float2(0.044715f, 0.044715f), __fmul2_rn(x, x2), x);
+  const float2 arg = __fmul2_rn(make_float2(0.7978846f, 0.7978846f), s);
+  const float2 t = make_float2(tanh_approx(arg.x), tanh_approx(arg.y));
+  const float2 hx = __fmul2_rn(make_float2(0.5f, 0.5f), x);
+  g = __ffma2_rn(hx, t, hx);  // 0.5 x (1 + t)
+  // gelu'(x) = 0.5 (1 + t) + 0.5 x (1 - t^2) 0.7978846 (1 + 3 * 0.044715 x^2)
+  const float2 a0 = __ffma2_rn(make_float2(0.5f, 0.5f), t, make_float2(0.5f, 0.5f));
+  const float2 omt = __ffma2_rn(make_float2(-t.x, -t.y), t, make_float2(1.0f, 1.0f));
+  const float2 poly =
+      __ffma2_rn(make_float2(0.7978846f * 0.134145f, 0.7978846f * 0.134145f), x2, make_float2(0.7978846f, 0.7978846f));
+  d = __ffma2_rn(__fmul2_rn(hx, omt), poly, a0);
 }
 
 __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
@@ -447,17 +458,15 @@ __global__ void __launch_bounds__(384, 1)
             uint32_t g[32];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              float y0, y1, y2, y3, d0, d1, d2, d3;
+              float2 ya, yb, da, db;
               const uint32_t r0 = pack_bf16x2(__uint_as_float(v0[2 * j]), __uint_as_float(v0[2 * j + 1]));
               const uint32_t r1 = pack_bf16x2(__uint_as_float(v1[2 * j]), __uint_as_float(v1[2 * j + 1]));
-              gelu_and_grad(__uint_as_float(r0 << 16), y0, d0);
-              gelu_and_grad(__uint_as_float(r0 & 0xFFFF0000u), y1, d1);
-              gelu_and_grad(__uint_as_float(r1 << 16), y2, d2);
-              gelu_and_grad(__uint_as_float(r1 & 0xFFFF0000u), y3, d3);
-              w[j] = pack_bf16x2(y0, y1);
-              w[16 + j] = pack_bf16x2(y2, y3);
-              g[j] = pack_bf16x2(d0, d1);
-              g[16 + j] = pack_bf16x2(d2, d3);
+              gelu_and_grad2(make_float2(__uint_as_float(r0 << 16), __uint_as_float(r0 & 0xFFFF0000u)), ya, da);
+              gelu_and_grad2(make_float2(__uint_as_float(r1 << 16), __uint_as_float(r1 & 0xFFFF0000u)), yb, db);
+              w[j] = pack_bf16x2(ya.x, ya.y);
+              w[16 + j] = pack_bf16x2(yb.x, yb.y);
+              g[j] = pack_bf16x2(da.x, da.y);
+              g[16 + j] = pack_bf16x2(db.x, db.y);
             }
             stage(w, &tmC, col0, store_y, false);
             stage(g, &tmC2, col0, store_y, false, true);
