@@ -336,6 +336,19 @@ def sweep_ops(only: str | None = None, reps: int = 10):
             tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
             emit({"op": name, "ms": ms, "achieved": tf, "unit": "TFLOP/s", "bound": "tensor" if kind == "bf16" else
                   "fp32 FFMA", "frac_of_bf16_peak": tf / tc_burst})
+        name = f"gemm_{kind}_step_fc_gelu"  # the same GEMM as the step runs it: gelu(u) and gelu'(u) stored
+        if kind == "bf16" and want(name):
+            M, N, K = CFG["batch"] * CFG["seq"], 4 * CFG["n_embd"], CFG["n_embd"]
+            a = torch.randn(M, K, device=dev).to(dt)
+            w = torch.randn(N, K, device=dev).to(dt)
+            g = torch.empty(M, N, device=dev, dtype=dt)
+            gd = torch.empty(M, N, device=dev, dtype=dt)
+            fn = lambda: L.sb_op_matmul_gelu(elem, a.data_ptr(), K, w.data_ptr(), K, M, N, K, g.data_ptr(),  # noqa
+                                             gd.data_ptr(), N, st())
+            ms = _time_op(fn, reps, flush)
+            tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+            emit({"op": name, "ms": ms, "achieved": tf, "unit": "TFLOP/s", "bound": "tensor + output bytes",
+                  "frac_of_bf16_peak": tf / tc_burst, "out_bytes": 2 * M * N * g.element_size()})
         for B, T, H, Hd in ((16, 1024, 12, 64), (CFG["batch"], CFG["seq"], CFG["n_head"], CFG["n_embd"] // CFG["n_head"])):
             name = f"attention_{kind}_{B}x{H}x{T}x{Hd}"
             if not want(name):
