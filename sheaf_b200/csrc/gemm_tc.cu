@@ -468,8 +468,37 @@ __global__ void __launch_bounds__(384, 1)
               g[j] = pack_bf16x2(da.x, da.y);
               g[16 + j] = pack_bf16x2(db.x, db.y);
             }
-            stage(w, &tmC, col0, store_y, false);
-            stage(g, &tmC2, col0, store_y, false, true);
+            if constexpr (kSlots >= 2) {
+              // both outputs of the block in one go: the two slots written,
+              // one proxy fence and one warp sync, both stores in one bulk
+              // group (every block of this launch does the same, so a group
+              // always covers both slots: wait for all earlier reads)
+              const uint32_t s0 = stg, s1 = stg + kSlotBytes;
+              if (cc > 0) {
+                if (lane == 0) bulk_wait_read<0>();
+                __syncwarp();
+              }
+              st_row128_sw(s0, lane, w);
+              st_row128_sw(s1, lane, g);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                                 reinterpret_cast<uint64_t>(&tmC)),
+                             "r"(s0), "r"(col0), "r"(store_y)
+                             : "memory");
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+                        reinterpret_cast<uint64_t>(&tmC2)),
+                    "r"(s1), "r"(col0), "r"(store_y), "l"(evict_first_policy)
+                    : "memory");
+                bulk_commit();
+              }
+              cc += 2;
+            } else {
+              stage(w, &tmC, col0, store_y, false);
+              stage(g, &tmC2, col0, store_y, false, true);
+            }
           } else {  // EPI_MUL: acc * aux (bf16)
             // The warp's 32 x 64 aux block goes through the staging slot the
             // result will leave from: coalesced loads (4 rows of 128 B per
