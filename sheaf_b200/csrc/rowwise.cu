@@ -237,26 +237,27 @@ __global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(con
 }
 
 // out[c] = sum_b part[b][c] in a fixed order, written as f32 or bf16. Block
-// of 256 threads per 32 columns: warp w sums partial rows w, w+8, ... (lane =
-// column, coalesced), then the 8 warp sums are combined in order.
-__global__ void __launch_bounds__(256) column_sum_kernel(const float* __restrict__ part, int nparts, long D, void* out,
-                                                         int out_f32) {
+// of 1024 threads per 32 columns: warp w sums partial rows w, w+32, ... (lane =
+// column, coalesced), then the 32 warp sums are combined in order. Many short
+// per-warp chains: the kernel is bound by load latency, not bytes.
+__global__ void __launch_bounds__(1024) column_sum_kernel(const float* __restrict__ part, int nparts, long D, void* out,
+                                                          int out_f32) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float sm[8][33];
+  __shared__ float sm[32][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long c = static_cast<long>(blockIdx.x) * 32 + lane;
   float acc = 0.f;
   if (c < D) {
-#pragma unroll 8
-    for (int b = warp; b < nparts; b += 8) acc += part[static_cast<long>(b) * D + c];
+#pragma unroll 4
+    for (int b = warp; b < nparts; b += 32) acc += part[static_cast<long>(b) * D + c];
   }
   sm[warp][lane] = acc;
   __syncthreads();
   if (warp == 0 && c < D) {
     float t = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) t += sm[w][lane];
+    for (int w = 0; w < 32; ++w) t += sm[w][lane];
     if (out_f32)
       static_cast<float*>(out)[c] = t;
     else
@@ -265,7 +266,7 @@ __global__ void __launch_bounds__(256) column_sum_kernel(const float* __restrict
 }
 
 int column_sum(const float* part, int nparts, long D, void* out, bool out_f32, cudaStream_t s) {
-  launch_pdl(column_sum_kernel, dim3(static_cast<unsigned>((D + 31) / 32)), dim3(256), 0, s, part, nparts, D, out,
+  launch_pdl(column_sum_kernel, dim3(static_cast<unsigned>((D + 31) / 32)), dim3(1024), 0, s, part, nparts, D, out,
              out_f32);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
