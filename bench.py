@@ -282,7 +282,8 @@ def measure_kernel_roofline(session, reps: int = 5, copies: int = 16):
 
 # --------------------------------------------------------------------------
 # Primitive op sweep (bf16 and fp32): dot_general M=N=K in {512, 2048, 8192},
-# attention [16, 12, 1024, 64] and the step's [64, 6, 256, 64] fwd + VJP,
+# the step's fc GEMM [16384, 384] x [384, 1536]^T (and, bf16, with its GELU
+# epilogue), attention [16, 12, 1024, 64] and the step's [64, 6, 256, 64] fwd + VJP,
 # layer-norm over [8192, 4096] and the step's [16384, 384], gelu over
 # [8192, 4096]; N(0,1) values, seed 0. One JSON line per op.
 # --------------------------------------------------------------------------
