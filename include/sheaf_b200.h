@@ -46,6 +46,7 @@ typedef struct sb_module_s sb_module;
 #define SB_STATUS_DEADLINE_EXCEEDED 4
 #define SB_STATUS_NOT_FOUND 5
 #define SB_STATUS_RESOURCE_EXHAUSTED 8
+#define SB_STATUS_FAILED_PRECONDITION 9
 #define SB_STATUS_UNIMPLEMENTED 12
 #define SB_STATUS_INTERNAL 13
 #define SB_STATUS_UNAVAILABLE 14
@@ -86,6 +87,13 @@ SB_API sb_status sb_session_get_stats(sb_session* session, sb_session_stats* out
 #define SB_NCCL_ID_BYTES 128
 SB_API sb_status sb_nccl_unique_id(void* out_id, size_t id_bytes);
 SB_API sb_status sb_session_join_group(sb_session* session, const void* nccl_id, size_t id_bytes, int rank, int world);
+/* Leaves the group; later calls run on this rank's data alone. Call it only
+ * between steps, with none of this session's collectives in flight: an
+ * enqueued all-reduce waits on the GPU for every peer without a limit. With
+ * `abort` non-zero the communicator is ended with ncclCommAbort (for the
+ * survivors of a rank that has left: nothing waits for the missing peer);
+ * otherwise with ncclCommDestroy. */
+SB_API sb_status sb_session_leave_group(sb_session* session, int abort);
 
 /* ---- buffers (replaces buffer_convert.rs:14-123, device_buffer.rs:47-134) ---- */
 /* Allocates a device buffer from the session pool and copies `bytes` of host

@@ -103,7 +103,10 @@ SB_API int sb_op_layernorm_bwd_noalloc(uint32_t elem, const void* dy, const void
  *   loss_f32[0] = -mean_r log_softmax(logits[r])[targets[r]];
  *   dlogits = (softmax(logits) - one_hot(targets)) / rows.
  * logits / dlogits of type `elem` with row strides ld / ldd; targets are f32
- * class ids (converted by truncation, as `stablehlo.convert` does). */
+ * class ids. As in the reference's one_hot (an f32 compare against an iota,
+ * sheaf/src/lowering/stablehlo/tensor_ops.rs:163-217), a target that is not
+ * exactly an integer in [0, v) selects no class: its row adds nothing to the
+ * loss (which still divides by every row) and its dlogits row is zero. */
 SB_API size_t sb_op_cross_entropy_workspace_size(int32_t rows);
 SB_API int sb_op_cross_entropy(uint32_t elem, const void* logits, int64_t ld, int32_t rows, int32_t v,
                                const void* targets, void* dlogits, int64_t ldd, void* workspace,
@@ -125,7 +128,10 @@ SB_API int sb_op_embedding_fwd(uint32_t elem, const void* ids, const void* wte, 
 /* Embedding VJP as a scatter-add (the reference's one-hot matmul,
  * sheaf/src/autodiff/reverse.rs:1077-1122) and the wpe slice VJP (pad,
  * sheaf/src/lowering/codegen/builtins.rs:208-271): dx f32 [b*t, d] ->
- * dwte [v, d], dwpe [p, d] (rows >= t zero), both of type `elem`. */
+ * dwte [v, d], dwpe [p, d] (rows >= t zero), both of type `elem`. The
+ * one-hot compares the f32 id with an f32 iota, so an id that is not exactly
+ * an integer in [0, v) adds nothing (the forward gather instead truncates
+ * and clamps it). */
 SB_API size_t sb_op_embedding_bwd_workspace_size(int32_t v, int32_t d);
 SB_API int sb_op_embedding_bwd(uint32_t elem, const void* ids, const void* dx, int32_t b, int32_t t, int32_t p,
                                int32_t v, int32_t d, void* dwte, void* dwpe, void* workspace, size_t workspace_bytes,

@@ -67,7 +67,9 @@ def save_bytes(entries: list[tuple[str, str, tuple, bytes]]) -> bytes:
         header[key] = {"data_offsets": [off, off + len(raw)], "dtype": dt, "shape": list(shape)}
         data += raw
         off += len(raw)
-    h = json.dumps(header, separators=(",", ":"), sort_keys=True).encode()
+    # serde_json writes strings as UTF-8, escaping only '"', '\\' and control
+    # characters (\b \f \n \r \t, else \u00xx): json's ensure_ascii=False form
+    h = json.dumps(header, separators=(",", ":"), sort_keys=True, ensure_ascii=False).encode("utf-8")
     h += b" " * ((8 - (8 + len(h)) % 8) % 8)
     return struct.pack("<Q", len(h)) + h + bytes(data)
 

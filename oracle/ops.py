@@ -132,8 +132,11 @@ def layer_norm(x, gamma, beta, axis=-1):
 # ---- losses ---------------------------------------------------------------
 
 def one_hot(idx, n, dtype):
-    idx = np.asarray(idx).astype(np.int64)
-    return (idx[..., None] == np.arange(n)).astype(dtype)
+    """tensor_ops.rs:163-217: compare(broadcast(idx), iota) == in f32, then
+    select 1 / 0. The ids stay f32, so a fractional id (2.5) or one outside
+    [0, n) matches no class and gives an all-zero row."""
+    idx = np.asarray(idx, dtype=np.float32)
+    return (idx[..., None] == np.arange(n, dtype=np.float32)).astype(dtype)
 
 
 def cross_entropy(logits, targets):
@@ -146,13 +149,15 @@ def cross_entropy(logits, targets):
 
 def cross_entropy_vjp(logits, targets, g=1.0):
     """Composition of the mean, sum, multiply and log-softmax VJP rules:
-    (softmax(logits) - one_hot) / N."""
+    (softmax(logits) * sum(one_hot) - one_hot) / N. A row whose one-hot is all
+    zero (a fractional or out-of-range target) gets a zero gradient; every
+    other row gets (softmax - one_hot) / N."""
     V = logits.shape[-1]
     flat = logits.reshape(-1, V)
     n = flat.shape[0]
     mask = one_hot(np.asarray(targets).reshape(-1), V, logits.dtype)
     t = logits.dtype.type
-    d = (softmax(flat) - mask) * t(g / n)
+    d = (softmax(flat) * mask.sum(axis=-1, keepdims=True) - mask) * t(g / n)
     return d.reshape(logits.shape)
 
 
@@ -183,11 +188,15 @@ def embedding(w, ids):
 
 def embedding_vjp(w_shape, ids, g, dtype):
     """reverse.rs:1077-1122: one_hot(idx, V)^T @ adj, i.e. a scatter-add of
-    rows; an index outside [0, V) has an all-zero one-hot row and adds nothing."""
+    rows. The one-hot compares the f32 id with an f32 iota, so only an id that
+    is exactly an integer in [0, V) adds its row; a fractional id (which the
+    forward gather truncates) or one outside [0, V) (which the gather clamps)
+    adds nothing."""
     out = np.zeros(w_shape, dtype=dtype)
-    idx = ids_to_index(ids).reshape(-1)
+    f = np.asarray(ids, dtype=np.float32).reshape(-1)
+    idx = ids_to_index(f)
     rows = g.reshape((len(idx),) + tuple(w_shape[1:]))
-    ok = (idx >= 0) & (idx < w_shape[0])
+    ok = (idx >= 0) & (idx < w_shape[0]) & (idx.astype(np.float32) == f)
     np.add.at(out, idx[ok], rows[ok])
     return out
 

@@ -92,6 +92,7 @@ SIGNATURES: dict[str, tuple] = {
     "sb_session_get_stats": (_P, [_P, C.POINTER(SessionStats)]),
     "sb_nccl_unique_id": (_P, [_P, C.c_size_t]),
     "sb_session_join_group": (_P, [_P, _P, C.c_size_t, C.c_int, C.c_int]),
+    "sb_session_leave_group": (_P, [_P, C.c_int]),
     "sb_buffer_alloc_copy": (_P, [_P, C.POINTER(C.c_int64), C.c_size_t, C.c_uint32, _P, C.c_size_t, C.POINTER(_P)]),
     "sb_buffer_alloc": (_P, [_P, C.POINTER(C.c_int64), C.c_size_t, C.c_uint32, C.POINTER(_P)]),
     "sb_buffer_h2d": (_P, [_P, _P, C.c_size_t]),

@@ -431,10 +431,29 @@ sb_status sb_safetensors_save(sb_session* s, const char* path, const char* const
   uint64_t off = 0;
   for (size_t i = 0; i < items.size(); ++i) {
     const Buffer* b = items[i].second;
+    // escaped as serde_json writes strings: \" and \\, the short forms \b \f
+    // \n \r \t, other control characters as \u00xx (lowercase hex)
     std::string k;
     for (char ch : items[i].first) {
-      if (ch == '"' || ch == '\\') k += '\\';
-      k += ch;
+      const unsigned char u = static_cast<unsigned char>(ch);
+      switch (ch) {
+        case '"': k += "\\\""; break;
+        case '\\': k += "\\\\"; break;
+        case '\b': k += "\\b"; break;
+        case '\f': k += "\\f"; break;
+        case '\n': k += "\\n"; break;
+        case '\r': k += "\\r"; break;
+        case '\t': k += "\\t"; break;
+        default:
+          if (u < 0x20) {
+            static const char hex[] = "0123456789abcdef";
+            k += "\\u00";
+            k += hex[u >> 4];
+            k += hex[u & 15];
+          } else {
+            k += ch;
+          }
+      }
     }
     h += (i ? ",\"" : "\"") + k + "\":{\"data_offsets\":[" + std::to_string(off) + "," +
          std::to_string(off + b->bytes()) + "],\"dtype\":\"" + dtype_for(b->elem) + "\",\"shape\":[";

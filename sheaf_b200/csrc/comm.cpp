@@ -6,9 +6,18 @@
 // equal shards is the mean of the shard means).
 //
 // libnccl.so.2 is opened at run time (the one torch already loaded, if any),
-// so the library itself carries no link-time NCCL dependency. Communicators
-// are created non-blocking and every wait is bounded: a rank that stops
-// answering turns into an error status, not a hang.
+// so the library itself carries no link-time NCCL dependency.
+//
+// What is bounded: communicators are created non-blocking, and the host-side
+// waits of set-up and of enqueueing a collective poll with a limit (a rank
+// that never joins turns into a DEADLINE_EXCEEDED status, not a hang). What
+// is not: an all-reduce that has been enqueued (or captured into a step's
+// CUDA graph) waits on the GPU for every peer with no limit, so a rank that
+// leaves in the middle of a step leaves the other ranks' NCCL kernels waiting.
+// A rank may therefore leave only between steps, with none of its
+// collectives in flight; the others learn of it on the host (the process
+// group's store or a heartbeat) before their next step and end their
+// communicators with ncclCommAbort (sb_session_leave_group with abort).
 #include <dlfcn.h>
 #include <nccl.h>
 
@@ -140,10 +149,13 @@ sb_status comm_allreduce_avg(Session& s, void* data, size_t count, uint32_t elem
   return nullptr;
 }
 
-void comm_destroy(Session& s) {
+void comm_destroy(Session& s, bool abort) {
   if (!s.comm) return;
   NcclApi& a = api();
-  if (a.destroy) a.destroy(s.comm->comm);
+  if (abort && a.abort)
+    a.abort(s.comm->comm);
+  else if (a.destroy)
+    a.destroy(s.comm->comm);
   delete s.comm;
   s.comm = nullptr;
   s.world = 1;
@@ -162,6 +174,15 @@ sb_status sb_nccl_unique_id(void* out_id, size_t id_bytes) {
 sb_status sb_session_join_group(sb_session* session, const void* nccl_id, size_t id_bytes, int rank, int world) {
   SB_RETURN_IF(!session || !nccl_id, SB_STATUS_INVALID_ARGUMENT, "null argument");
   return sb::comm_init(*static_cast<sb::Session*>(session), nccl_id, id_bytes, rank, world);
+}
+
+sb_status sb_session_leave_group(sb_session* session, int abort) {
+  SB_RETURN_IF(!session, SB_STATUS_INVALID_ARGUMENT, "null session");
+  auto* s = static_cast<sb::Session*>(session);
+  SB_RETURN_IF(!s->comm, SB_STATUS_FAILED_PRECONDITION, "session is not in a group");
+  std::lock_guard<std::mutex> lk(s->mu);
+  sb::comm_destroy(*s, abort != 0);
+  return nullptr;
 }
 
 }  // extern "C"

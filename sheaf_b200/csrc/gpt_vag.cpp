@@ -120,6 +120,7 @@ class GptVagModule : public Module {
   // of generate), its kernel nodes and the eager runs before the capture
   enum Mode { kVag, kTrain, kSample, kModes };
   cudaGraphExec_t exec[kModes] = {};
+  bool exec_dp[kModes] = {};  // whether the captured graph holds the all-reduce
   uint64_t kernels[kModes] = {};
   int eager[kModes] = {};
   bool use_graph = true;
@@ -156,6 +157,12 @@ class GptVagModule : public Module {
     for (void* p : owned) cudaFree(p);
     owned.clear();
   }
+
+  // false: calls skip the gradient all-reduce even in a data-parallel
+  // session (the front door's first-call check compares per-rank results)
+  bool collectives = true;
+  void set_collectives(bool on) override { collectives = on; }
+  bool group(const Session& s) const { return collectives && s.comm != nullptr && s.world > 1; }
 
   bool has_function(const std::string& fn) const override {
     return fn == "value_and_grad" || (train && fn == "train_step") || (sampler && fn == "generate");
@@ -417,7 +424,7 @@ class GptVagModule : public Module {
     const bool train_step = mode == kTrain;
     int* err = s.err_word;
     const bool f32 = !bf;
-    const bool dp = s.comm != nullptr && s.world > 1;
+    const bool dp = group(s);
     const AttnShape ash{B, T, H, D / H};
     int rc = 0;
 #define SB_K(expr)                                                                                  \
@@ -709,13 +716,19 @@ class GptVagModule : public Module {
   sb_status run(Session& s, cudaStream_t st, Mode mode) {
     cudaGraphExec_t& ex = exec[mode];
     uint64_t& nk = kernels[mode];
-    const bool dp = s.comm != nullptr && s.world > 1 && mode != kSample;
+    const bool dp = group(s) && mode != kSample;
     if (!use_graph || eager[mode] < 1) {
       SB_TRY(enqueue(s, st, mode));
       ++eager[mode];
       return nullptr;
     }
+    if (ex && exec_dp[mode] != dp) {  // joined or left a group since the capture
+      SB_CUDA_TRY(cudaStreamSynchronize(st));
+      cudaGraphExecDestroy(ex);
+      ex = nullptr;
+    }
     if (!ex) {
+      exec_dp[mode] = dp;
       cudaGraph_t graph = nullptr;
       SB_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
       sb_status e = enqueue(s, st, mode);
@@ -778,7 +791,7 @@ class GptVagModule : public Module {
     }
     const bool train_step = fn == "train_step";
     SB_TRY(train_step ? check_train_inputs(in) : check_inputs(in));
-    const bool dp = s.comm != nullptr && s.world > 1;
+    const bool dp = group(s);
     if (dp && bucket_events.empty()) {
       for (int i = 0; i < L + 2; ++i) {
         cudaEvent_t e;

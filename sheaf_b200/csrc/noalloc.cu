@@ -35,7 +35,12 @@ static __device__ __align__(256) float g_ln_bwd_scratch[kScratchFloats];
 
 // Device address of g_ln_bwd_scratch on the current device. In host code the
 // array's name is only a host-side stand-in, so the address is looked up once
-// per device (with that device current) and cached.
+// per device (with that device current, on the first call there) and cached
+// for the life of the process. A device reset (cudaDeviceReset, or anything
+// else that destroys the primary context) unloads the module and can place
+// the array elsewhere when it is loaded again: after one, reload the library
+// before calling this entry point again (every other object of the library,
+// sessions and modules included, is lost with the context too).
 float* scratch_on_current_device(int* rc) {
   static std::mutex mu;
   static std::map<int, float*> by_device;

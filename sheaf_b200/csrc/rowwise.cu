@@ -35,6 +35,15 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// The class an f32 token id selects in a one-hot built as
+// compare(id, iota) in f32 (tensor_ops.rs:163-217): the id itself when it is
+// exactly an integer in [0, V), else -1 (no class: an all-zero one-hot row).
+// The forward gather instead truncates and clamps (indexing_ops.rs:416-484).
+__device__ __forceinline__ int one_hot_class(float f, int V) {
+  const int i = static_cast<int>(f);
+  return (static_cast<float>(i) == f && i >= 0 && i < V) ? i : -1;
+}
+
 template <typename T>
 __device__ __forceinline__ float load1(const T* p);
 template <>
@@ -303,12 +312,16 @@ __global__ void __launch_bounds__(256) ce_fwd_bwd_kernel(const T* __restrict__ l
       m = nm;
     }
     const float logs = logf(s);
-    const int y = static_cast<int>(targets[row]);  // f32 -> i32 truncation
-    if (lane == 0 && y >= 0 && y < V) part += (load1(lr + y) - m) - logs;
+    // one_hot(y) compares the f32 target with an f32 iota: a fractional or
+    // out-of-range target matches no class, adds nothing to the loss and
+    // gets a zero gradient row ((softmax * sum(one_hot) - one_hot) / rows)
+    const int y = one_hot_class(targets[row], V);
+    if (lane == 0 && y >= 0) part += (load1(lr + y) - m) - logs;
     T* dr = dlogits + static_cast<long>(row) * ldd;
+    const float hit = y >= 0 ? 1.f : 0.f;
     for (int c = lane; c < V; c += 32) {
       const float p = expf((load1(lr + c) - m) - logs);
-      store1(dr + c, (p - (c == y ? 1.f : 0.f)) * inv_rows);
+      store1(dr + c, (p * hit - (c == y ? 1.f : 0.f)) * inv_rows);
     }
   }
   if (lane == 0) sm_part[warp] = part;
@@ -385,7 +398,7 @@ __global__ void embed_bwd_priv_kernel(const float* __restrict__ ids, const float
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int tt = t + u;
-      id[u] = (tt < t1) ? static_cast<int>(ids[tt]) : -1;
+      id[u] = (tt < t1) ? one_hot_class(ids[tt], V) : -1;
       g[u] = (tt < t1 && c < D) ? dx[static_cast<long>(tt) * D + c] : 0.f;
     }
 #pragma unroll
@@ -407,8 +420,8 @@ __global__ void embed_bwd_atomic_kernel(const float* __restrict__ ids, const flo
   const int warps = blockDim.x / 32;
   const int lane = threadIdx.x & 31;
   for (int n = blockIdx.x * warps + threadIdx.x / 32; n < ntok; n += gridDim.x * warps) {
-    const int id = static_cast<int>(ids[n]);
-    if (id < 0 || id >= V) continue;
+    const int id = one_hot_class(ids[n], V);
+    if (id < 0) continue;
     const float* g = dx + static_cast<long>(n) * D;
     float* o = acc + static_cast<long>(id) * D;
     for (int c = lane; c < D; c += 32) atomicAdd(o + c, g[c]);

@@ -74,6 +74,9 @@ struct Module {
                          std::vector<Buffer*>& out) = 0;
   // Releases CUDA graphs and device state before the session goes away.
   virtual void teardown() {}
+  // With `on` false, calls run on this rank's inputs alone even when the
+  // session belongs to a data-parallel group (no gradient all-reduce).
+  virtual void set_collectives(bool on) { (void)on; }
 };
 
 struct Comm;  // NCCL communicator wrapper (comm.cpp)
@@ -126,7 +129,7 @@ sb_status validate_stablehlo(const char* text, size_t len, std::string* summary)
 sb_status comm_init(Session& s, const void* unique_id, size_t id_bytes, int rank, int world);
 sb_status comm_get_unique_id(void* out, size_t bytes);
 sb_status comm_allreduce_avg(Session& s, void* data, size_t count, uint32_t elem, cudaStream_t stream);
-void comm_destroy(Session& s);
+void comm_destroy(Session& s, bool abort = false);
 
 }  // namespace sb
 

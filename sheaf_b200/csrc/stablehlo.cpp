@@ -1411,9 +1411,11 @@ bool match_gpt_vag(const HFunc& f, GptShape* g) {
 }
 
 // Host-side comparison of two output lists (per tensor, relative to the
-// largest magnitude of the reference).
+// largest magnitude of the reference). *worst receives the largest
+// max|a - b| / max|b| over the tensors.
 sb_status outputs_agree(const std::vector<Buffer*>& a, const std::vector<Buffer*>& b, double tol, bool* agree,
-                        std::string* why) {
+                        std::string* why, double* worst) {
+  *worst = 0;
   *agree = a.size() == b.size();
   for (size_t i = 0; i < a.size() && *agree; ++i) {
     const size_t n = a[i]->bytes();
@@ -1445,6 +1447,8 @@ sb_status outputs_agree(const std::vector<Buffer*>& a, const std::vector<Buffer*
       mx = std::max(mx, std::fabs(static_cast<double>(vb)));
       err = std::max(err, std::fabs(static_cast<double>(va) - vb));
     }
+    const double rel = err / std::max(mx, 1e-30);
+    *worst = std::max(*worst, rel);
     if (*agree && err > tol * mx) {
       *agree = false;
       *why = "output " + std::to_string(i) + ": max error " + std::to_string(err) + " vs max |ref| " +
@@ -1591,12 +1595,32 @@ void record_plan(const std::string& dir, const std::string& name, const PlanReco
   std::rename(tmp.c_str(), (dir + "/manifest.json").c_str());
 }
 
+// Tolerance of the first-call check of a fused plan against the generic
+// executor: the parity bar itself (1e-5 relative for f32, 2e-2 for bf16,
+// per tensor against its largest magnitude), since the generic executor runs
+// the module's ops one by one in their own element types, as the reference
+// does. SHEAF_B200_VERIFY_RTOL overrides it (tests use it to show that a
+// deviation above the bound is rejected).
+double verify_tolerance(int dt) {
+  const char* e = std::getenv("SHEAF_B200_VERIFY_RTOL");
+  if (e && *e) return std::atof(e);
+  return dt == DT_BF16 ? 2e-2 : 1e-5;
+}
+
+std::string fmt_dev(double v) {
+  char b[32];
+  std::snprintf(b, sizeof b, "%.2e", v);
+  return b;
+}
+
 class StableHloModule : public Module {
  public:
   struct Fn {
     std::unique_ptr<GenericFunc> generic;
-    std::unique_ptr<Module> fused;  // the fused plan, when recognised
+    std::unique_ptr<Module> fused;  // the fused plan, when recognised and built
+    bool vag = false;               // recognised as the nanoGPT value_and_grad (from the text alone)
     int fused_state = 0;            // 0 = unverified, 1 = verified, -1 = rejected
+    int group_state = 0;            // the same, decided jointly by a data-parallel group
     std::string note;
     std::string plan_hash;  // key of the plan cache entry
   };
@@ -1610,32 +1634,64 @@ class StableHloModule : public Module {
       if (kv.second.fused) kv.second.fused->teardown();
   }
 
+  // This rank's first-call check: the generic executor's outputs (`ref`) and
+  // whether the fused plan, run on this rank's inputs alone, agrees with
+  // them. Returns an error only when the generic run fails.
+  sb_status check_fused(Session& s, Fn& f, const std::vector<Buffer*>& in, std::vector<Buffer*>& ref,
+                        std::vector<Buffer*>* keep_fast, bool* agree, std::string* why) {
+    *agree = false;
+    SB_TRY(f.generic->run(s, in, ref));
+    if (!f.fused) {
+      *why = "fused plan not built";
+      return nullptr;
+    }
+    std::vector<Buffer*> fast;
+    f.fused->set_collectives(false);
+    sb_status st = f.fused->call(s, "value_and_grad", in, fast);
+    f.fused->set_collectives(true);
+    if (st) {
+      *why = sb_status_message(st);
+      sb_status_free(st);
+      return nullptr;
+    }
+    double worst = 0;
+    sb_status ce = cudaStreamSynchronize(s.stream) == cudaSuccess
+                       ? outputs_agree(fast, ref, verify_tolerance(f.generic->f.args[0].dt), agree, why, &worst)
+                       : make_status(SB_STATUS_INTERNAL, "stream synchronize failed");
+    if (ce) {
+      *agree = false;
+      *why = sb_status_message(ce);
+      sb_status_free(ce);
+    } else {
+      *why = (*agree ? "max deviation " : why->empty() ? "max deviation " : *why + "; max deviation ") +
+             fmt_dev(worst);
+    }
+    if (keep_fast && *agree) {
+      *keep_fast = fast;
+    } else {
+      for (Buffer* b : fast) buffer_release(b);
+    }
+    return nullptr;
+  }
+
   sb_status call(Session& s, const std::string& fn, const std::vector<Buffer*>& in,
                  std::vector<Buffer*>& out) override {
     Fn& f = fns.at(fn);
+    if (f.vag && s.comm && s.world > 1) return call_group(s, fn, f, in, out);
     if (f.fused && f.fused_state == 1) return f.fused->call(s, "value_and_grad", in, out);
     if (f.fused && f.fused_state == 0) {
       std::vector<Buffer*> ref, fast;
-      SB_TRY(f.generic->run(s, in, ref));
-      sb_status st = f.fused->call(s, "value_and_grad", in, fast);
       bool agree = false;
-      std::string why = st ? sb_status_message(st) : "";
-      if (!st) {
-        SB_CUDA_TRY(cudaStreamSynchronize(s.stream));
-        const double tol = f.generic->f.args[0].dt == DT_BF16 ? 5e-2 : 1e-3;
-        SB_TRY(outputs_agree(fast, ref, tol, &agree, &why));
-      } else {
-        sb_status_free(st);
-      }
+      std::string why;
+      SB_TRY(check_fused(s, f, in, ref, &fast, &agree, &why));
       if (agree) {
         f.fused_state = 1;
-        f.note = "fused nanoGPT plan (verified against the generic executor on the first call)";
+        f.note = "fused nanoGPT plan (verified against the generic executor on the first call, " + why + ")";
         for (Buffer* b : ref) buffer_release(b);
         out = fast;
       } else {
         f.fused_state = -1;
         f.note = "generic executor (fused plan disagreed: " + why + ")";
-        for (Buffer* b : fast) buffer_release(b);
         out = ref;
       }
       record_plan(cache_dir, name + "." + fn,
@@ -1643,6 +1699,81 @@ class StableHloModule : public Module {
       return nullptr;
     }
     return f.generic->run(s, in, out);
+  }
+
+  // A recognised value_and_grad in a data-parallel session. Its outputs are
+  // the loss and gradients averaged over the group, on either plan: the fused
+  // plan all-reduces inside its step, the generic executor's outputs are
+  // averaged after it. Which plan runs is decided by all ranks together, so
+  // every rank issues the same collectives: on the first call each rank
+  // checks the fused plan against the generic executor on its own inputs
+  // (plan cache entries are not consulted), then one all-reduce of
+  // {agrees, failed} settles it: the fused plan only if every rank agreed,
+  // an error on every rank if any rank's generic run failed.
+  sb_status call_group(Session& s, const std::string& fn, Fn& f, const std::vector<Buffer*>& in,
+                       std::vector<Buffer*>& out) {
+    if (f.group_state == 1) return f.fused->call(s, "value_and_grad", in, out);
+    if (f.group_state == -1) {
+      SB_TRY(f.generic->run(s, in, out));
+      return average_outputs(s, out);
+    }
+    std::vector<Buffer*> ref;
+    bool agree = false;
+    std::string why;
+    sb_status gen_err = check_fused(s, f, in, ref, nullptr, &agree, &why);
+    float flags[2] = {agree ? 1.f : 0.f, gen_err ? 1.f : 0.f};
+    Allocation* a = nullptr;
+    sb_status xs = session_alloc(s, 256, &a);
+    if (!xs) {
+      float* d = static_cast<float*>(a->ptr);
+      if (cudaMemcpyAsync(d, flags, sizeof flags, cudaMemcpyHostToDevice, s.stream) != cudaSuccess)
+        xs = make_status(SB_STATUS_INTERNAL, "flag upload failed");
+      if (!xs) xs = comm_allreduce_avg(s, d, 2, SB_ELEM_F32, s.stream);
+      if (!xs && (cudaMemcpyAsync(flags, d, sizeof flags, cudaMemcpyDeviceToHost, s.stream) != cudaSuccess ||
+                  cudaStreamSynchronize(s.stream) != cudaSuccess))
+        xs = make_status(SB_STATUS_INTERNAL, "flag exchange failed");
+      allocation_release(a);
+    }
+    if (xs || gen_err || flags[1] != 0.f) {
+      for (Buffer* b : ref) buffer_release(b);
+      if (gen_err) {
+        if (xs) sb_status_free(xs);
+        return gen_err;
+      }
+      if (xs) return xs;
+      return make_status(SB_STATUS_INTERNAL, "the first call failed on another rank of the group");
+    }
+    // the average of 1/0 flags over the ranks is exactly 1 only if all are 1
+    const bool fused = flags[0] == 1.f;
+    f.group_state = fused ? 1 : -1;
+    f.note = fused ? "fused nanoGPT plan, data-parallel (every rank's first-call check agreed; this rank: " + why + ")"
+                   : "generic executor, data-parallel outputs averaged (" +
+                         std::string(agree ? "another rank's" : "this rank's") + " first-call check disagreed; " +
+                         "this rank: " + why + ")";
+    if (s.rank == 0)
+      record_plan(cache_dir, name + "." + fn,
+                  PlanRecord{f.plan_hash, fused ? "fused-verified" : "fused-rejected", f.note});
+    if (fused) {
+      for (Buffer* b : ref) buffer_release(b);
+      return f.fused->call(s, "value_and_grad", in, out);
+    }
+    out = ref;
+    return average_outputs(s, out);
+  }
+
+  // Averages every output over the group (in place, on the session stream).
+  static sb_status average_outputs(Session& s, std::vector<Buffer*>& out) {
+    for (Buffer* b : out) {
+      const size_t es = elem_size(b->elem);
+      sb_status st = es ? comm_allreduce_avg(s, b->data(), b->bytes() / es, b->elem, s.stream)
+                        : make_status(SB_STATUS_INTERNAL, "output element type");
+      if (st) {
+        for (Buffer* x : out) buffer_release(x);
+        out.clear();
+        return st;
+      }
+    }
+    return nullptr;
   }
 };
 
@@ -1684,9 +1815,12 @@ sb_status load_stablehlo_module(Session& s, const char* text, size_t len, std::u
       return make_status(SB_STATUS_INVALID_ARGUMENT, std::string("stablehlo: ") + e.what());
     }
     GptShape g;
+    // recognition depends on the text alone, so every rank of a group
+    // recognises the same functions whatever its plan cache holds
+    fn.vag = match_gpt_vag(fn.generic->f, &g);
     if (cached && rec->second.plan == "fused-rejected") {
       fn.note = "generic executor (plan cache: " + rec->second.note + ")";
-    } else if (match_gpt_vag(fn.generic->f, &g)) {
+    } else if (fn.vag) {
       std::unique_ptr<Module> fused;
       sb_status st = make_gpt_vag_module(s, hm.name + "." + f.name, g, &fused);
       if (!st) {

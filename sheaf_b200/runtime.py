@@ -99,6 +99,12 @@ class Session:
     def join_group(self, nccl_id: bytes, rank: int, world: int) -> None:
         _check(lib().sb_session_join_group(self._h, nccl_id, len(nccl_id), rank, world))
 
+    def leave_group(self, abort: bool = False) -> None:
+        """Leaves the data-parallel group, between steps only (no collective of
+        this session in flight). abort=True ends the communicator without
+        waiting for peers: what the survivors of a departed rank do."""
+        _check(lib().sb_session_leave_group(self._h, int(abort)))
+
     # -- buffers -----------------------------------------------------------
     def upload(self, array, elem: int = ELEM_F32) -> "Buffer":
         """Host array -> new device buffer of element type `elem`."""
@@ -220,6 +226,29 @@ class Session:
         n = C.c_size_t()
         _check(lib().sb_call(self._h, qualified_name.encode(), arr, len(inputs), outs, max_outputs, C.byref(n)))
         return [Buffer(C.c_void_p(outs[i])) for i in range(n.value)]
+
+
+# ---- leaving a data-parallel group between steps -------------------------
+# An all-reduce enqueued on the GPU waits for every peer without a limit, so a
+# rank may leave only between steps. It announces its departure in the
+# process group's key-value store before the step-boundary barrier; after
+# that barrier every survivor reads the announcements, before it enqueues the
+# next step, and ends its communicator with Session.leave_group(abort=True).
+
+def _departure_key(rank: int) -> str:
+    return f"sheaf_b200/departed/{rank}"
+
+
+def announce_departure(store, rank: int) -> None:
+    """Marks `rank` as leaving after the current step (a torch.distributed
+    Store, e.g. the default process group's)."""
+    store.set(_departure_key(rank), "1")
+
+
+def departed_ranks(store, world: int) -> list[int]:
+    """Ranks that announced their departure (read after the step-boundary
+    barrier, so an announcement made before it is always seen)."""
+    return [r for r in range(world) if store.check([_departure_key(r)])]
 
 
 def validate_stablehlo(text: str) -> str:

@@ -33,6 +33,31 @@ def _worker(rank, world, port, mode, q):
     import bench
 
     try:
+        if mode == "leave_between_steps":
+            from torch.distributed.distributed_c10d import _get_default_store
+
+            import torch
+
+            from sheaf_b200.runtime import announce_departure, departed_ranks
+
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=20))
+            store = _get_default_store()
+            steps = 0
+            for step in range(3):
+                t = torch.ones(4)
+                dist.all_reduce(t)  # the step's collective
+                steps += 1
+                if rank == 1 and step == 0:
+                    announce_departure(store, rank)  # before the boundary barrier
+                dist.barrier()  # step boundary
+                gone = departed_ranks(store, world)
+                if gone:
+                    # survivors end the group here (Session.leave_group(abort=True)
+                    # on a GPU); nobody enqueues another collective
+                    q.put((rank, (steps, gone)))
+                    return
+            q.put((rank, (steps, [])))
+            return
         if mode == "dead_rank":
             dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=5))
             if rank == 1:
@@ -63,7 +88,7 @@ def _run(mode):
     for p in procs:
         p.start()
     results = {}
-    for _ in range(2 if mode != "dead_rank" else 1):
+    for _ in range(2 if mode != "dead_rank" else 1):  # the departing rank reports too
         r, v = q.get(timeout=120)
         results[r] = v
     for p in procs:
@@ -81,3 +106,12 @@ def test_group_id_broadcast_and_max_over_ranks():
 def test_dead_rank_becomes_an_error_not_a_hang():
     res = _run("dead_rank")
     assert res[0].startswith("error"), res
+
+
+def test_rank_leaves_between_steps_and_survivors_learn_before_the_next_step():
+    """A rank that leaves announces it in the store before the step-boundary
+    barrier; every rank sees the departure after that barrier, before it
+    would enqueue the next step's collective (so no collective waits on the
+    missing peer)."""
+    res = _run("leave_between_steps")
+    assert res[0] == (1, [1]) and res[1] == (1, [1]), res

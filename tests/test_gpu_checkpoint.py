@@ -52,13 +52,16 @@ def test_save_matches_the_reference_layout_byte_for_byte(session, tmp_path):
     h = rng.standard_normal((5, 4)).astype(np.float16)
     tree = {"params": {"lm_head": {"weight": session.upload(w, BF16)}, "ln": [session.upload(m, F32)]},
             "t": session.upload(np.float32(4.0).reshape(()), F32), "ids": session.upload(ids, I32),
-            "half": _dev_f16(session, h)}
+            "half": _dev_f16(session, h),
+            # escaped the way serde_json escapes: short forms, \u00xx, UTF-8 kept
+            'odd"key\\\n\t\x01\x1f\u00e9': session.upload(m, F32)}
     p = tmp_path / "ckpt.safetensors"
     session.save_safetensors(p, tree)
     want = ock.save_bytes([ock.entry_of("params.lm_head.weight", w, "BF16"), ock.entry_of("params.ln.0", m, "F32"),
                            ock.entry_of("t", np.float32(4.0), "F32"), ock.entry_of("ids", ids, "I32"),
-                           ock.entry_of("half", h, "F16")])
+                           ock.entry_of("half", h, "F16"), ock.entry_of('odd"key\\\n\t\x01\x1f\u00e9', m, "F32")])
     assert p.read_bytes() == want
+    assert b'"odd\\"key\\\\\\n\\t\\u0001\\u001f\xc3\xa9"' in want
 
 
 def test_load_decodes_every_dtype_like_the_reference(session, tmp_path):

@@ -38,6 +38,9 @@ def run_vag(cfg, kind, leaves, x, y, calls=1):
 CFGS = {
     "tiny": models.GPTConfig(n_layer=2, n_head=2, n_embd=128, block_size=64, vocab_size=65, batch=4, seq=64),
     "nanogpt_b2": models.GPTConfig(batch=2),
+    # 4096 tokens: the weight-gradient GEMMs contract over more than one
+    # 2048-token split, attention items outnumber the SMs
+    "nanogpt_b16": models.GPTConfig(batch=16),
 }
 
 
@@ -56,6 +59,45 @@ def test_vag_matches_oracle(name, kind, cuda):
     names = models.gpt_leaf_names(cfg)
     assert len(out) == 1 + len(names)
     for nm, g, r in zip(names, out[1:], ref_grads):
+        assert_close(g, r, tol, nm)
+
+
+def test_vag_full_nanogpt_matches_oracle(cuda):
+    """The benchmarked configuration itself (6L/6H/384, B=64, T=256, bf16):
+    loss and all 40 gradients against the oracle (evaluated in f32, far inside
+    the bf16 bar). This plan takes the paths smaller batches do not: 384-wide
+    CTA-pair tiles, six-way split-K over 16,384 tokens on the side stream,
+    persistent attention with several items per CTA."""
+    cfg = models.NANOGPT_CHAR
+    leaves, x, y = models.gpt_inputs(cfg)
+    leaves = [odt.round_bf16(l) for l in leaves]
+    (out,) = run_vag(cfg, "bf16", leaves, x, y)
+    ref_loss, ref_grads = models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float32)
+    assert abs(float(out[0]) - ref_loss) <= TOL_BF16 * abs(ref_loss), (float(out[0]), ref_loss)
+    names = models.gpt_leaf_names(cfg)
+    assert len(out) == 1 + len(names)
+    for nm, g, r in zip(names, out[1:], ref_grads):
+        assert_close(g, r, TOL_BF16, nm)
+
+
+@pytest.mark.parametrize("kind", ["f32", "bf16"])
+def test_vag_edge_token_ids(kind, cuda):
+    """Fractional, negative and out-of-range f32 ids in x and y: the gather
+    truncates and clamps, the embedding VJP and the cross-entropy one-hot drop
+    them (compare in f32, tensor_ops.rs:163-217)."""
+    cfg = CFGS["tiny"]
+    leaves, x, y = models.gpt_inputs(cfg)
+    if kind == "bf16":
+        leaves = [odt.round_bf16(l) for l in leaves]
+    edge = np.array([2.5, -1.0, -0.0, 0.75, 64.0, 65.0, 70.0, 64.75, -2.5, 1e6], np.float32)
+    x, y = x.copy(), y.copy()
+    x[0, :len(edge)] = edge
+    y[1, 3:3 + len(edge)] = edge
+    ref_loss, ref_grads = models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float64)
+    (out,) = run_vag(cfg, kind, leaves, x, y)
+    tol = TOL_F32 if kind == "f32" else TOL_BF16
+    assert abs(float(out[0]) - ref_loss) <= tol * abs(ref_loss), (float(out[0]), ref_loss)
+    for nm, g, r in zip(models.gpt_leaf_names(cfg), out[1:], ref_grads):
         assert_close(g, r, tol, nm)
 
 

@@ -129,6 +129,103 @@ def test_embedding(kind, V, cuda):
                  ops.slice_rows_vjp((P, D), 0, dx.reshape(B, T, D).astype(np.float64).sum(0)), tol, "dwpe")
 
 
+# Token ids at the edges of the reference's semantics: the forward gather
+# converts f32 -> i32 (truncation) and clamps into [0, V) (indexing_ops.rs:
+# 416-484), while the one-hot of the VJP and of the cross-entropy compares the
+# f32 id with an f32 iota (tensor_ops.rs:163-217), so a fractional or
+# out-of-range id matches no class there.
+def _edge_list(V):
+    return [2.5, 3.0, -1.0, -0.0, 0.75, -2.5, V - 1, V, V + 5, 1e6, V - 0.25, 5.0]
+
+
+EDGE_IDS = _edge_list(65)
+
+
+def _edge_ids(V, n, rng):
+    """n uniform ids in [0, V) whose first entries are the edge cases."""
+    ids = rng.integers(0, V, n).astype(np.float32)
+    ed = np.array(_edge_list(V), np.float32)
+    ids[:len(ed)] = ed
+    return ids
+
+
+@pytest.mark.parametrize("kind", ["f32", "bf16"])
+@pytest.mark.parametrize("V", [65, 5000])
+def test_embedding_edge_ids(kind, V, cuda):
+    """Fractional, negative and out-of-range f32 ids: the gather truncates and
+    clamps (rows compared bit-exactly); the scatter-add drops every id that is
+    not exactly an integer in [0, V), so a row reached only through such ids
+    stays exactly zero."""
+    import torch
+    import sheaf_b200 as sb
+
+    L = sb.lib()
+    dt = torch.float32 if kind == "f32" else torch.bfloat16
+    B, T, P, D = 2, 64, 64, 128
+    rng = np.random.default_rng(11 + V)
+    wte = _rt(rng.standard_normal((V, D)).astype(np.float32) * 0.02, kind)
+    wpe = _rt(rng.standard_normal((P, D)).astype(np.float32) * 0.02, kind)
+    ids = _edge_ids(V, B * T, rng)
+    # row 2 is reached only through 2.5 / -2.5 (truncated to 2 / -2): keep other ids off it
+    ids[len(EDGE_IDS):][ids[len(EDGE_IDS):] == 2.0] = 3.0
+    ids = ids.reshape(B, T)
+    idd = _dev(ids, torch.float32, cuda)
+    x = torch.empty(B * T, D, device=cuda)
+    assert L.sb_op_embedding_fwd(ELEMS[kind], idd.data_ptr(), _dev(wte, dt, cuda).data_ptr(),
+                                 _dev(wpe, dt, cuda).data_ptr(), x.data_ptr(), B * T, T, V, D, _stream()) == 0
+    ref = (ops.embedding(wte, ids) + wpe[:T][None]).reshape(B * T, D).astype(np.float32)
+    assert np.array_equal(x.cpu().numpy(), ref), "gathered rows must be bit-exact"
+    dx = rng.standard_normal((B * T, D)).astype(np.float32)
+    dwte = torch.full((V, D), float("nan"), dtype=dt, device=cuda)
+    dwpe = torch.empty(P, D, dtype=dt, device=cuda)
+    wsb = L.sb_op_embedding_bwd_workspace_size(V, D)
+    ws = torch.empty(wsb // 4 + 1, device=cuda)
+    assert L.sb_op_embedding_bwd(ELEMS[kind], idd.data_ptr(), _dev(dx, torch.float32, cuda).data_ptr(), B, T, P, V, D,
+                                 dwte.data_ptr(), dwpe.data_ptr(), ws.data_ptr(), wsb, _stream()) == 0
+    got = dwte.float().cpu().numpy()
+    exp = ops.embedding_vjp((V, D), ids, dx.astype(np.float64), np.float64)
+    # which rows receive anything is index work: the zero pattern is exact
+    assert np.array_equal(got == 0, exp == 0)
+    assert not got[2].any(), "row 2 is reached only through fractional ids"
+    assert_close(got, exp, TOL_F32 if kind == "f32" else TOL_BF16, "dwte")
+
+
+@pytest.mark.parametrize("kind", ["f32", "bf16"])
+@pytest.mark.parametrize("V", [65, 50304])
+def test_cross_entropy_edge_targets(kind, V, cuda):
+    """Targets that are fractional or outside [0, V) have an all-zero one-hot
+    row: they add nothing to the loss (still divided by every row) and their
+    dlogits rows are exactly zero."""
+    import torch
+    import sheaf_b200 as sb
+
+    L = sb.lib()
+    dt = torch.float32 if kind == "f32" else torch.bfloat16
+    rows = 96
+    ld = (V + 7) // 8 * 8
+    rng = np.random.default_rng(5 + V)
+    logits = _rt((rng.standard_normal((rows, V)) * 2).astype(np.float32), kind)
+    tgt = _edge_ids(V, rows, rng)
+    full = np.zeros((rows, ld), np.float32)
+    full[:, :V] = logits
+    dl = torch.full((rows, ld), float("nan"), dtype=dt, device=cuda)
+    dl[:, V:] = 0
+    td = _dev(tgt, torch.float32, cuda)
+    loss = torch.zeros(1, device=cuda)
+    wsb = L.sb_op_cross_entropy_workspace_size(rows)
+    ws = torch.empty(wsb // 4 + 1, device=cuda)
+    assert L.sb_op_cross_entropy(ELEMS[kind], _dev(full, dt, cuda).data_ptr(), ld, rows, V, td.data_ptr(),
+                                 dl.data_ptr(), ld, ws.data_ptr(), wsb, loss.data_ptr(), _stream()) == 0
+    ref_loss = ops.cross_entropy(logits.astype(np.float64), tgt)
+    ref_d = ops.cross_entropy_vjp(logits.astype(np.float64), tgt)
+    assert abs(loss.item() - ref_loss) <= 1e-5 * abs(ref_loss)
+    got = dl[:, :V].float().cpu().numpy()
+    invalid = ~((tgt == np.trunc(tgt)) & (tgt >= 0) & (tgt < V))
+    assert invalid.sum() >= 8
+    assert not got[invalid].any(), "rows without a class get no gradient"
+    assert_close(got, ref_d, TOL_F32 if kind == "f32" else TOL_BF16, "dlogits")
+
+
 def _attn_ref(qkv, B, T, H, Hd):
     q, k, v = (qkv[:, i * H * Hd:(i + 1) * H * Hd].reshape(B, T, H, Hd).transpose(0, 2, 1, 3) for i in range(3))
     s = q @ np.swapaxes(k, -1, -2) / np.sqrt(Hd)

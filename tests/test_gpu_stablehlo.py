@@ -16,8 +16,8 @@ import numpy as np
 import pytest
 
 from oracle import dtype as odt
-from oracle import hlo_emit, models
-from oracle.hlo_emit import Emitter, arg
+from oracle import hlo_emit, hlo_eval, models
+from tests.hlo_cases import GOLDEN_CASES, golden_module
 from tests.parity import TOL_BF16, TOL_F32, assert_close
 
 pytestmark = pytest.mark.gpu
@@ -51,51 +51,9 @@ def test_docs_forward_module(session):
     assert_close(out, x.astype(np.float64) @ W + b, TOL_F32, "forward")
 
 
-def _golden(name):
-    """Sheaf expression of vag_tests.yaml -> (module text, wrt argument)."""
-    e = Emitter()
-    if name == "vag-matmul":
-        w = arg(0, (2, 2), "f32")
-        x = e.const_array([[1.0, 2.0]])
-        y = e.matmul(x, w)
-        loss = e.sum_all(y)
-        g = e.matmul(e.transpose(x, [1, 0]), e.splat(1.0, (1, 2), "f32"))
-        return e.module("__vag_g", "value_and_grad", [w], [loss, g]), np.eye(2, dtype=np.float32)
-    if name == "vag-gelu":
-        x = arg(0, (2,), "f32")
-        loss = e.sum_all(hlo_emit.gelu(e, x))
-        g = hlo_emit.gelu_vjp(e, x, e.splat(1.0, (2,), "f32"))
-        return e.module("__vag_g", "value_and_grad", [x], [loss, g]), np.array([0.0, 1.0], np.float32)
-    if name == "vag-softmax":
-        x = arg(0, (3,), "f32")
-        sm = hlo_emit.softmax(e, x)
-        sel = e.const_array([1.0, 0.0, 0.0])
-        loss = e.sum_all(e.mul(sm, sel))
-        g = e.mul(sm, e.sub(sel, e.sum(e.mul(sel, sm), -1, keepdims=True)))
-        return e.module("__vag_g", "value_and_grad", [x], [loss, g]), np.array([1.0, 2.0, 3.0], np.float32)
-    if name == "vag-cross-entropy-loss":
-        w = arg(0, (3, 3), "f32")
-        x = e.const_array([[1.0, 2.0, 3.0]])
-        logits = e.matmul(x, w)
-        tgt = e.const_array([[2.0]])
-        loss, dlogits = hlo_emit.cross_entropy(e, e.reshape(logits, (1, 1, 3)), tgt)
-        g = e.matmul(e.transpose(x, [1, 0]), e.reshape(dlogits, (1, 3)))
-        return e.module("__vag_g", "value_and_grad", [w], [loss, g]), np.eye(3, dtype=np.float32)
-    if name == "vag-get-embedding-repeated":
-        emb = arg(0, (3, 2), "f32")
-        ids = e.const_array([0.0, 0.0, 1.0])
-        loss = e.sum_all(e.gather_rows(emb, ids))
-        oh = e.one_hot(ids, 3)
-        g = e.matmul(e.transpose(oh, [1, 0]), e.splat(1.0, (3, 2), "f32"))
-        return e.module("__vag_g", "value_and_grad", [emb], [loss, g]), \
-            np.array([[1, 2], [3, 4], [5, 6]], np.float32)
-    raise KeyError(name)
-
-
-@pytest.mark.parametrize("name", ["vag-matmul", "vag-gelu", "vag-softmax", "vag-cross-entropy-loss",
-                                  "vag-get-embedding-repeated"])
+@pytest.mark.parametrize("name", GOLDEN_CASES)
 def test_vag_goldens_through_the_front_door(session, name):
-    text, x = _golden(name)
+    text, x = golden_module(name)
     _, (loss, grad) = run(session, text, [x], [F32])
     got = np.concatenate([[float(loss)], grad.reshape(-1)])
     exp = np.array([float(v) for v in NUM.findall(GOLD["vag"][name]["expected"])])
@@ -113,11 +71,18 @@ def test_mlp_vag_front_door(session, dt):
         leaves = ins[:4]
     name, outs = run(session, text, ins, [elem] * 6)
     assert "generic executor" in session.describe(name)
-    ref_loss, ref_grads = models.mlp_value_and_grad(ins[:4], ins[4], ins[5], dtype=np.float64)
+    # the module's own arithmetic: every op rounded to its element type, as
+    # the reference compiles it (oracle/hlo_eval.py)
+    ref = hlo_eval.evaluate(text, ins)
     tol = TOL_F32 if dt == "f32" else TOL_BF16
-    assert abs(float(outs[0]) - ref_loss) <= tol * abs(ref_loss)
-    for nm, g, r in zip(["dW1", "db1", "dW2", "db2"], outs[1:], ref_grads):
-        assert_close(g, r, tol if dt == "f32" else 4e-2, nm)
+    assert abs(float(outs[0]) - float(ref[0])) <= tol * abs(float(ref[0]))
+    for nm, g, r in zip(["dW1", "db1", "dW2", "db2"], outs[1:], ref[1:]):
+        assert_close(g, r, tol, nm)
+    if dt == "f32":  # and in f32 the composed VJPs of the model oracle
+        ref_loss, ref_grads = models.mlp_value_and_grad(ins[:4], ins[4], ins[5], dtype=np.float64)
+        assert abs(float(outs[0]) - ref_loss) <= tol * abs(ref_loss)
+        for nm, g, r in zip(["dW1", "db1", "dW2", "db2"], outs[1:], ref_grads):
+            assert_close(g, r, tol, nm)
 
 
 @pytest.mark.parametrize("dt", ["bf16", "f32"])
@@ -136,10 +101,44 @@ def test_nanogpt_vag_front_door_uses_verified_fused_plan(session, dt):
     second = [o.to_host() for o in session.call(f"{name}.value_and_grad", bufs)]
     ref_loss, ref_grads = models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float64)
     tol = TOL_F32 if dt == "f32" else TOL_BF16
+    per_op = hlo_eval.evaluate(text, leaves + [x, y])  # the module's ops, each rounded to its type
     for outs in (first, second):
         assert abs(float(outs[0]) - ref_loss) <= tol * abs(ref_loss)
-        for nm, g, r in zip(models.gpt_leaf_names(cfg), outs[1:], ref_grads):
+        assert abs(float(outs[0]) - float(per_op[0])) <= tol * abs(float(per_op[0]))
+        for nm, g, r, p in zip(models.gpt_leaf_names(cfg), outs[1:], ref_grads, per_op[1:]):
             assert_close(g, r, tol, nm)
+            assert_close(g, p, tol, nm + " (per-op rounding)")
+
+
+def test_first_call_check_rejects_a_deviation_above_its_tolerance(cuda, monkeypatch):
+    """The first-call check holds the fused plan to the parity bar against
+    the generic executor and reports the deviation it measured; with the
+    tolerance set below that deviation the same text is rejected and the
+    generic executor's results (the module's per-op arithmetic) come back."""
+    from sheaf_b200.runtime import Session
+
+    cfg = models.GPTConfig(n_layer=1, n_head=2, n_embd=128, block_size=64, vocab_size=65, batch=2, seq=64)
+    leaves, x, y = models.gpt_inputs(cfg)
+    leaves = [odt.round_bf16(l) for l in leaves]
+    text = hlo_emit.gpt_vag_module(cfg, "bf16")
+
+    def load_and_call():
+        s = Session(0)
+        name = s.load_stablehlo(text)
+        bufs = [s.upload(l, BF16) for l in leaves] + [s.upload(x, F32), s.upload(y, F32)]
+        outs = [o.to_host() for o in s.call(f"{name}.value_and_grad", bufs)]
+        return s.describe(name), outs
+
+    note, _ = load_and_call()
+    assert "verified against the generic executor" in note, note
+    dev = float(re.search(r"max deviation ([0-9.e+-]+)", note).group(1))
+    assert 0 < dev <= TOL_BF16
+    monkeypatch.setenv("SHEAF_B200_VERIFY_RTOL", repr(dev / 2))
+    note, outs = load_and_call()
+    assert "generic executor (fused plan disagreed" in note, note
+    per_op = hlo_eval.evaluate(text, leaves + [x, y])
+    for g, p in zip(outs, per_op):
+        assert_close(np.asarray(g, np.float64).reshape(np.shape(p)), p, TOL_BF16)
 
 
 def test_full_nanogpt_text_module_verifies_at_full_size(session):

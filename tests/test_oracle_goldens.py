@@ -232,3 +232,41 @@ def test_mlp_grad_matches_finite_differences():
         lm[li][idx] -= h
         fd = (models.mlp_value_and_grad(lp, x, y)[0] - models.mlp_value_and_grad(lm, x, y)[0]) / (2 * h)
         assert abs(fd - grads[li][idx]) <= 1e-6 * (1 + abs(fd))
+
+
+EDGE = a([2.5, 3.0, -1.0, -0.0, 0.75, -2.5, 15.0, 16.0, 21.0, 1e6, 15.75, 5.0])
+
+
+def test_one_hot_compares_f32_ids():
+    """tensor_ops.rs:163-217: compare(id, iota) in f32, so only ids that are
+    exactly an integer in [0, n) select a class (-0.0 selects class 0)."""
+    oh = ops.one_hot(EDGE, 16, F)
+    assert oh.sum(1).tolist() == [0, 1, 0, 1, 0, 0, 1, 0, 0, 0, 0, 1]
+    assert oh[1, 3] == 1 and oh[3, 0] == 1 and oh[6, 15] == 1
+
+
+def test_embedding_edge_ids_follow_gather_and_one_hot():
+    """Forward: convert (truncation) + gather with clamping; VJP: exactly the
+    one_hot(ids)^T @ adj matmul the reference emits (reverse.rs:1108-1121)."""
+    w = np.arange(16 * 3, dtype=F).reshape(16, 3)
+    assert ops.embedding(w, EDGE)[:, 0].tolist() == [6, 9, 0, 0, 0, 0, 45, 45, 45, 45, 45, 15]
+    g = np.random.default_rng(0).standard_normal((len(EDGE), 3))
+    np.testing.assert_array_equal(ops.embedding_vjp((16, 3), EDGE, g, np.float64),
+                                  ops.one_hot(EDGE, 16, np.float64).T @ g)
+
+
+def test_cross_entropy_vjp_with_edge_targets_matches_finite_differences():
+    """A target without a class adds nothing to the loss and gets a zero
+    gradient row; the others get (softmax - one_hot) / rows."""
+    rng = np.random.default_rng(1)
+    logits = rng.standard_normal((len(EDGE), 16))
+    d = ops.cross_entropy_vjp(logits, EDGE)
+    h = 1e-6
+    for r in range(len(EDGE)):
+        for c in (0, 3, 15):
+            lp, lm = logits.copy(), logits.copy()
+            lp[r, c] += h
+            lm[r, c] -= h
+            fd = (ops.cross_entropy(lp, EDGE) - ops.cross_entropy(lm, EDGE)) / (2 * h)
+            assert abs(fd - d[r, c]) <= 1e-7 * (1 + abs(fd)), (r, c, fd, d[r, c])
+    assert not d[[0, 2, 4, 5, 7, 8, 9, 10]].any()

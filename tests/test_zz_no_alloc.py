@@ -5,9 +5,11 @@ latency-critical loop that cannot take cudaMalloc's device-wide sync).
 
 The variant keeps its scratch in a fixed array inside the library instead of
 a caller workspace. Checked through the C ABI against the workspace-taking
-sb_op_layernorm_bwd on two calls in a row with different shapes (so contents
-left in the shared array by the first call must not leak into the second),
-plus the size limit. This file is collected last on purpose.
+sb_op_layernorm_bwd and against the oracle's layer-norm VJP, on calls in a
+row with different shapes (so contents left in the shared array by one call
+must not leak into the next), up to the widest accepted row (4096, where
+the array holds the partials of only 8 blocks and every block strides over
+many rows), plus the size limit. This file is collected last on purpose.
 """
 import numpy as np
 import pytest
@@ -65,8 +67,9 @@ def test_no_alloc_matches_workspace_entry_point(kind, cuda):
     L = sb.lib()
     stream = torch.cuda.current_stream().cuda_stream
     tol = 1e-5 if kind == "f32" else 2e-2
-    # two calls in a row, the second with a different shape
-    for rows, D, seed in [(1000, 384, 1), (77, 768, 2)]:
+    # calls in a row, each with a different shape; the last at the widest
+    # accepted rows
+    for rows, D, seed in [(1000, 384, 1), (77, 768, 2), (300, 4096, 3), (1000, 384, 4)]:
         c = _case(kind, rows, D, seed, cuda)
         ref_dres, ref_dg = _with_workspace(L, kind, c, rows, D, stream)
         got_dres, got_dg = _no_alloc(L, kind, c, rows, D, stream)
@@ -76,7 +79,22 @@ def test_no_alloc_matches_workspace_entry_point(kind, cuda):
         a, e = got_dg.double().cpu().numpy(), ref_dg.double().cpu().numpy()
         assert np.isfinite(a).all()
         assert np.abs(a - e).max() <= tol * np.abs(e).max()
+        _check_oracle(c, got_dres, got_dg, tol)
     assert L.sb_op_device_error() == 0
+
+
+def _check_oracle(c, got_dres, got_dg, tol):
+    """dres - dres0 and dgamma against the oracle's layer-norm VJP (fp64)."""
+    from oracle import ops
+    from tests.parity import assert_close
+
+    x = c["x"].double().cpu().numpy()
+    g = c["gamma"].double().cpu().numpy()
+    dy = c["dy"].double().cpu().numpy()
+    _, cache = ops.layer_norm_nb(x, g)
+    dx_ref, dg_ref = ops.layer_norm_nb_vjp(cache, g, dy)
+    assert_close(got_dres.double().cpu().numpy() - c["dres"].double().cpu().numpy(), dx_ref, 1e-5, "dx")
+    assert_close(got_dg.double().cpu().numpy(), dg_ref, tol, "dgamma")
 
 
 def test_no_alloc_rejects_rows_wider_than_its_scratch(cuda):
