@@ -13,6 +13,12 @@ token ids uniform in [0, 65), mirroring init-gpt-params and random-randint.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sheaf_b200|reference]
 
+`--config gpt2` runs GPT-2-small instead (12L/12H/768, T=1024, V=50304,
+batch 8 per GPU); `--dtype f32` the fp32 step; `--strong` splits the
+reference's global batch of 64 over the GPUs instead of giving every GPU its
+own (strong scaling). The line's `roofline` is the step's fc GEMM with its
+GELU epilogue timed alone; `kernels` lists the step's main kernels likewise.
+
 Prints one JSON line on rank 0. `--sample` instead times autoregressive
 sampling (generate-token + slide-window, 256 new tokens from a one-token
 prompt, batch 1 and 32, bf16, temperature 1.0 over the whole vocabulary) on
@@ -37,12 +43,37 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "nanoGPT fwd+VJP tokens/sec"
 UNIT = "tokens/s"
-CFG = dict(n_layer=6, n_head=6, n_embd=384, block_size=256, vocab_size=65, batch=64, seq=256)
+# nanoGPT-char (the headline workload) and GPT-2-small (the data-parallel
+# workload: 12L/12H/768, T=1024, V=50304, global batch 64 = 8 per GPU at 8 GPUs)
+CONFIGS = {
+    "nanogpt": dict(n_layer=6, n_head=6, n_embd=384, block_size=256, vocab_size=65, batch=64, seq=256),
+    "gpt2": dict(n_layer=12, n_head=12, n_embd=768, block_size=1024, vocab_size=50304, batch=8, seq=1024),
+}
+CFG = CONFIGS["nanogpt"]
+WORKLOAD = {
+    "nanogpt": "nanoGPT-char value_and_grad 6L/6H/384 T=256 V=65",
+    "gpt2": "GPT-2-small value_and_grad 12L/12H/768 T=1024 V=50304",
+}
+# global batch of the strong-scaling line (the reference's own batch)
+STRONG_GLOBAL = {"nanogpt": 64, "gpt2": 64}
 BF16 = 0x22000010
 F32 = 0x21000020
-# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the fc GEMM
-# (13.8 MB + 1.1 MB: A and B read once, the output still in L2 at the end)
-FC_GEMM_DRAM_BYTES = 14.9e6
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the nanoGPT
+# fc GEMM with its GELU epilogue (13.8 MB read: A and B once; 41.5 MB of the
+# 100.7 MB of gelu(u) and gelu'(u) written reach DRAM during the launch)
+FC_GELU_DRAM_BYTES = {"nanogpt": 55.3e6}
+# FP32 CUDA-core peak, nominal: 148 SMs x 128 lanes x 2 flops x 1.965 GHz
+FP32_NOMINAL_TFLOPS = 74.4
+
+
+def cpu_model() -> str:
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def model_flops_per_token(c=CFG) -> float:
@@ -169,40 +200,65 @@ def barrier(world: int):
 # CPU baseline: the oracle (numpy restatement of the reference math)
 # --------------------------------------------------------------------------
 
-def cpu_sample(target_s: float = 12.0, batch: int = 4):
-    """Times the oracle's fp32 fwd+VJP on a bounded sample of the workload
-    (batch `batch` of the 64, same model). Returns (tokens/s, cores, sample)."""
+def _oracle_cfg(c):
     from oracle import models
 
-    cfg = models.GPTConfig(batch=batch)
-    leaves, x, y = synthetic_inputs(0, dict(CFG, batch=batch))
-    models.gpt_value_and_grad(leaves, x[:1, :64], y[:1, :64], models.GPTConfig(batch=1, seq=64), dtype=np.float32)
+    return models.GPTConfig(n_layer=c["n_layer"], n_head=c["n_head"], n_embd=c["n_embd"],
+                            block_size=c["block_size"], vocab_size=c["vocab_size"], batch=c["batch"], seq=c["seq"])
+
+
+def _cpu_batch(name: str, c) -> int:
+    """Sequences per CPU step: the whole batch for nanoGPT-char (a few seconds
+    on the host cores), one sequence of GPT-2-small's eight."""
+    return c["batch"] if name == "nanogpt" else 1
+
+
+def _cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_sample(name: str, c, dtype: str, target_s: float = 15.0):
+    """Times the oracle's fwd+VJP (numpy, BLAS on every host core) on a
+    bounded sample of the workload. Returns (tokens/s, cores, sample)."""
+    from oracle import models
+
+    batch = _cpu_batch(name, c)
+    cc = dict(c, batch=batch)
+    cfg = _oracle_cfg(cc)
+    leaves, x, y = synthetic_inputs(0, cc)
+    npdt = np.float32
+    models.gpt_value_and_grad(leaves, x[:1, :64], y[:1, :64], _oracle_cfg(dict(c, batch=1, seq=64)), dtype=npdt)
     t0 = time.perf_counter()
     n = 0
     while True:
-        models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float32)
+        models.gpt_value_and_grad(leaves, x, y, cfg, dtype=npdt)
         n += 1
         el = time.perf_counter() - t0
         if el >= target_s or n >= 20:
             break
-    tok = n * batch * CFG["seq"] / el
-    cores = os.cpu_count() or 1
-    return tok, cores, f"{n} x fp32 numpy fwd+VJP steps of batch {batch} (of 64) x 256 tokens, same 6L/6H/384 model"
+    tok = n * batch * c["seq"] / el
+    cores = _cpu_threads()
+    return tok, cores, (f"{n} x fp32 numpy oracle fwd+VJP steps of batch {batch} (of {c['batch']}) x {c['seq']} "
+                        f"tokens, same model; BLAS on {cores} threads of {cpu_model()}")
 
 
 def run_reference(args, world, rank):
     """Reference arm: the reference's own math on the host cores (the oracle
-    port; the reference's IREE llvm-cpu path cannot be built here)."""
+    port; the reference's IREE llvm-cpu path cannot be built here). Rank 0
+    alone runs it."""
     if rank != 0:
         return
-    import numpy as _np  # noqa: F401
-
     from oracle import models
 
-    batch = 4
-    cfg = models.GPTConfig(batch=batch)
-    leaves, x, y = synthetic_inputs(0, dict(CFG, batch=batch))
-    for _ in range(args.warmup):
+    name, c = args.config, CONFIGS[args.config]
+    batch = _cpu_batch(name, c)
+    cc = dict(c, batch=batch)
+    cfg = _oracle_cfg(cc)
+    leaves, x, y = synthetic_inputs(0, cc)
+    for _ in range(min(args.warmup, 1)):
         models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float32)
     times = []
     for _ in range(args.steps):
@@ -210,14 +266,15 @@ def run_reference(args, world, rank):
         models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float32)
         times.append(time.perf_counter() - t0)
     tot = sum(times)
-    v = args.steps * batch * CFG["seq"] / tot
-    cores = os.cpu_count() or 1
-    sample = f"each step: fp32 numpy oracle fwd+VJP of batch {batch} (of 64) x 256 tokens, 6L/6H/384/V65"
+    v = args.steps * batch * c["seq"] / tot
+    cores = _cpu_threads()
+    sample = (f"each step: fp32 numpy oracle fwd+VJP of batch {batch} (of {c['batch']}) x {c['seq']} tokens, "
+              f"{WORKLOAD[name]}; BLAS on {cores} threads of {cpu_model()}")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "nanoGPT-char value_and_grad 6L/6H/384 T=256 V=65", "global_batch": batch,
-                       "seq_len": CFG["seq"], "parallelism": "host cores"},
+            "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD[name], "global_batch": batch, "seq_len": c["seq"],
+                       "parallelism": "host cores", "cpu": cpu_model(), "threads": cores},
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -227,57 +284,150 @@ def run_reference(args, world, rank):
 # B200 arm
 # --------------------------------------------------------------------------
 
-def measure_kernel_roofline(session, reps: int = 5, copies: int = 16):
-    """Times the dominant kernel with CUDA events on the session stream: the
-    fc GEMM of the step (tokens x 384 @ 384 x 1536, bf16 in, tcgen05).
+def _rotated_ms(launch, copies: int, reps: int, st) -> float:
+    """Average ms per launch of launch(i) for i over `copies` operand sets,
+    launched back to back between two CUDA events on stream `st` (so no launch
+    finds its operands left in L2 by the previous one); mean of `reps` rounds
+    after 3 warm-up launches."""
+    import torch
 
-    Back to back, as the step runs it: `copies` launches in a row, each on its
-    own A, B and output (16 x 64 MB, far above the 126 MB L2, so no launch
-    finds its operands left in L2 by the one before), between two events;
-    the average over `reps` such batches. Also returns one launch timed alone
-    after an L2 flush, which adds the launch latency the step hides.
-    Returns (avg_ms, single_launch_ms, flops_per_launch)."""
+    for i in range(3):
+        launch(i)
+    out = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for i in range(copies):
+            launch(i)
+        e1.record(st)
+        st.synchronize()
+        out.append(e0.elapsed_time(e1) / copies)
+    return sum(out) / len(out)
+
+
+def measure_step_kernels(session, c, elem, reps: int = 5):
+    """Times the step's own kernels alone, at the step's shapes and with the
+    epilogues the plan uses, with CUDA events on the session stream: the fc
+    GEMM with its GELU epilogue (both outputs), the fc weight-gradient GEMM
+    (dU^T h2 over every token, split-K with its reduction), the attention
+    forward and VJP, the layer-norm forward and VJP, the cross-entropy. Each
+    is launched back to back over enough operand sets to exceed L2.
+    Returns one dict per kernel (ms, algorithmic work, achieved, bound)."""
     import torch
 
     import sheaf_b200 as sb
 
     L = sb.lib()
-    N, D = CFG["batch"] * CFG["seq"], CFG["n_embd"]
+    bf = elem == BF16
+    dt = torch.bfloat16 if bf else torch.float32
+    es = 2 if bf else 4
+    N, D, H, T, B, V = c["batch"] * c["seq"], c["n_embd"], c["n_head"], c["seq"], c["batch"], c["vocab_size"]
+    Hd = D // H
+    ldl = (V + 7) // 8 * 8
     dev = torch.device(f"cuda:{session.device}")
-    sets = [(torch.randn(N, D, device=dev).to(torch.bfloat16), torch.randn(4 * D, D, device=dev).to(torch.bfloat16),
-             torch.empty(N, 4 * D, device=dev, dtype=torch.bfloat16)) for _ in range(copies)]
     st = torch.cuda.ExternalStream(session.stream, device=dev)
-    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    sp = session.stream
+    res = []
 
-    def launch(i):
-        a, w, c = sets[i % copies]
-        rc = L.sb_op_matmul(BF16, a.data_ptr(), D, 0, w.data_ptr(), D, 1, N, 4 * D, D, c.data_ptr(), 4 * D, BF16,
-                            None, 0, session.stream)
-        assert rc == 0
+    def nsets(bytes_per_set):
+        return max(2, min(16, int(1.2e9 // max(bytes_per_set, 1))))
 
-    batch_ms, single_ms = [], []
+    def add(name, kernel, ms, work, unit, bound):
+        res.append({"kernel": name, "template": kernel, "ms": ms, "work": work, "bound": bound,
+                    "achieved": work / (ms / 1e3) / (1e12 if unit == "TFLOP/s" else 1e9), "unit": unit})
+
     with torch.cuda.stream(st):
-        for i in range(3):
-            launch(i)
-        for r in range(reps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            for i in range(copies):
-                launch(i)
-            e1.record(st)
-            st.synchronize()
-            batch_ms.append(e0.elapsed_time(e1) / copies)
-        for r in range(reps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            launch(r)
-            e1.record(st)
-            st.synchronize()
-            single_ms.append(e0.elapsed_time(e1))
-    del sets
-    return sum(batch_ms) / len(batch_ms), sum(single_ms) / len(single_ms), 2.0 * N * D * 4 * D
+        r = lambda *shape: torch.randn(*shape, device=dev).to(dt)  # noqa: E731
+        # fc GEMM + GELU epilogue: u = h2 W_fc^T; gelu(u), gelu'(u) stored
+        k = nsets(N * D * es + 4 * D * D * es + 2 * N * 4 * D * es)
+        sets = [(r(N, D), r(4 * D, D), torch.empty(N, 4 * D, device=dev, dtype=dt),
+                 torch.empty(N, 4 * D, device=dev, dtype=dt)) for _ in range(k)]
+
+        def fc(i):
+            a, w, g, gd = sets[i % k]
+            assert L.sb_op_matmul_gelu(elem, a.data_ptr(), D, w.data_ptr(), D, N, 4 * D, D, g.data_ptr(),
+                                       gd.data_ptr(), 4 * D, sp) == 0
+        add("fc GEMM + GELU epilogue", "gemm_tc_kernel<256,0,0,5,1>" if bf else "gemm_f32",
+            _rotated_ms(fc, k, reps, st), 2.0 * N * D * 4 * D, "TFLOP/s", "tensor" if bf else "fp32 FFMA")
+        del sets
+        # fc weight gradient: dW_fc [4D, D] = dU^T [4D, N] h2 [N, D]
+        wsb = L.sb_op_matmul_workspace_size(elem, 1, 0, 4 * D, D, N)
+        ws = torch.empty(max(wsb // 4, 1), device=dev)
+        k = nsets(N * 4 * D * es + N * D * es)
+        sets = [(r(N, 4 * D), r(N, D), torch.empty(4 * D, D, device=dev, dtype=dt)) for _ in range(k)]
+
+        def dw(i):
+            du, h2, o = sets[i % k]
+            assert L.sb_op_matmul(elem, du.data_ptr(), 4 * D, 1, h2.data_ptr(), D, 0, 4 * D, D, N, o.data_ptr(), D,
+                                  elem, ws.data_ptr(), wsb, sp) == 0
+        add("fc weight-gradient GEMM (+ split-K reduction)", "gemm_tc_kernel<384,1,1,4,1> + splitk_reduce_kernel"
+            if bf else "gemm_f32", _rotated_ms(dw, k, reps, st), 2.0 * N * D * 4 * D, "TFLOP/s",
+            "tensor" if bf else "fp32 FFMA")
+        del sets, ws
+        # attention forward and VJP (causal: half the dense T x T work)
+        wsb = L.sb_op_attention_bwd_workspace_size(elem, B, T, H, Hd)
+        ws = torch.empty(wsb // 4 + 1, device=dev)
+        k = nsets(N * 3 * D * es * 2 + N * D * es * 3)
+        sets = [(r(N, 3 * D), torch.empty(N, D, device=dev, dtype=dt), r(N, D),
+                 torch.empty(N, 3 * D, device=dev, dtype=dt), torch.empty(B * H * T, device=dev)) for _ in range(k)]
+
+        def afwd(i):
+            q, o, do, dq, lse = sets[i % k]
+            assert L.sb_op_attention_fwd(elem, q.data_ptr(), o.data_ptr(), lse.data_ptr(), B, T, H, Hd, sp) == 0
+
+        def abwd(i):
+            q, o, do, dq, lse = sets[i % k]
+            assert L.sb_op_attention_bwd(elem, q.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(),
+                                         dq.data_ptr(), ws.data_ptr(), wsb, B, T, H, Hd, sp) == 0
+        causal = 2.0 * B * H * T * T * Hd  # QK^T + PV over the lower triangle
+        for i in range(k):
+            afwd(i)  # real O and lse for the VJP
+        add("attention forward", "attn_fwd_tc" if bf else "attn_fwd_simt", _rotated_ms(afwd, k, reps, st), causal,
+            "TFLOP/s", "tensor" if bf else "fp32 FFMA")
+        add("attention VJP", "attn_bwd_tc + dq_convert_kernel" if bf else "attn_bwd_simt",
+            _rotated_ms(abwd, k, reps, st), 2.5 * causal, "TFLOP/s", "tensor" if bf else "fp32 FFMA")
+        del sets, ws
+        # layer norm forward / VJP over [N, D] (residual stream f32)
+        wsb = L.sb_op_layernorm_bwd_workspace_size(N, D)
+        ws = torch.empty(wsb // 4 + 1, device=dev)
+        k = nsets(N * D * (4 + es + 4 + 4 + 4))
+        g = r(D)
+        sets = [(torch.randn(N, D, device=dev), torch.empty(N, D, device=dev, dtype=dt), torch.empty(N, device=dev),
+                 torch.empty(N, device=dev), torch.randn(N, D, device=dev), torch.zeros(N, D, device=dev),
+                 torch.empty(D, device=dev, dtype=dt)) for _ in range(k)]
+
+        def lnf(i):
+            x, y, mu, rs, dy, dres, dg = sets[i % k]
+            assert L.sb_op_layernorm_fwd(elem, x.data_ptr(), g.data_ptr(), y.data_ptr(), mu.data_ptr(),
+                                         rs.data_ptr(), N, D, sp) == 0
+
+        def lnb(i):
+            x, y, mu, rs, dy, dres, dg = sets[i % k]
+            assert L.sb_op_layernorm_bwd(elem, dy.data_ptr(), x.data_ptr(), mu.data_ptr(), rs.data_ptr(),
+                                         g.data_ptr(), dres.data_ptr(), dg.data_ptr(), ws.data_ptr(), wsb, N, D,
+                                         sp) == 0
+        add("layer-norm forward", "ln_fwd_kernel", _rotated_ms(lnf, k, reps, st), N * D * (4 + es) + 8 * N, "GB/s",
+            "hbm")
+        add("layer-norm VJP (+ dgamma column sums)", "ln_bwd_kernel + column_sum_kernel",
+            _rotated_ms(lnb, k, reps, st), N * D * 16 + 8 * N, "GB/s", "hbm")
+        del sets, ws
+        # cross-entropy forward + VJP over [N, V] logits (rows padded to ldl)
+        wsb = L.sb_op_cross_entropy_workspace_size(N)
+        ws = torch.empty(wsb // 4 + 1, device=dev)
+        k = nsets(2 * N * ldl * es)
+        tg = torch.randint(0, V, (N,), device=dev).float()
+        loss = torch.zeros(1, device=dev)
+        sets = [(r(N, ldl), torch.empty(N, ldl, device=dev, dtype=dt)) for _ in range(k)]
+
+        def ce(i):
+            lg, dl = sets[i % k]
+            assert L.sb_op_cross_entropy(elem, lg.data_ptr(), ldl, N, V, tg.data_ptr(), dl.data_ptr(), ldl,
+                                         ws.data_ptr(), wsb, loss.data_ptr(), sp) == 0
+        add("cross-entropy fwd+VJP", "ce_fwd_bwd_kernel", _rotated_ms(ce, k, reps, st), 2 * N * V * es + 4 * N,
+            "GB/s", "hbm")
+        del sets, ws
+    torch.cuda.synchronize(dev)
+    return res
 
 
 # --------------------------------------------------------------------------
@@ -444,6 +594,11 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="primitive op sweep (one JSON line per op)")
     ap.add_argument("--op", default=None, help="run only this op of the sweep (e.g. gemm_bf16_8192)")
     ap.add_argument("--sample", action="store_true", help="autoregressive sampling tokens/s (1 GPU)")
+    ap.add_argument("--config", default="nanogpt", choices=sorted(CONFIGS),
+                    help="nanogpt: nanoGPT-char, batch 64 per GPU; gpt2: GPT-2-small, batch 8 per GPU")
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--strong", action="store_true",
+                    help="strong scaling: the reference's global batch (64) split over the GPUs")
     args = ap.parse_args()
     if args.sweep or args.op:
         sweep_ops(args.op, reps=args.steps if args.op else 10)
@@ -536,6 +691,17 @@ def bench_b200(args, world, rank, local):
 
     from sheaf_b200.runtime import Session
 
+    name = args.config
+    strong = args.strong
+    base = CONFIGS[name]
+    if strong:
+        gb = STRONG_GLOBAL[name]
+        if gb % world:
+            raise SystemExit(f"global batch {gb} does not split over {world} GPUs")
+        c = dict(base, batch=gb // world)
+    else:
+        c = dict(base)
+    elem = BF16 if args.dtype == "bf16" else F32
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
     s = Session(local)
@@ -545,9 +711,9 @@ def bench_b200(args, world, rank, local):
         obj = [Session.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         s.join_group(obj[0], rank, world)
-    s.create_gpt_vag("gpt", **CFG, elem=BF16)
-    leaves, x, y = synthetic_inputs(1234 + rank)
-    inputs = [s.upload(l, BF16) for l in leaves]
+    s.create_gpt_vag("gpt", **c, elem=elem)
+    leaves, x, y = synthetic_inputs(1234 + rank, c)
+    inputs = [s.upload(l, elem) for l in leaves]
     xb, yb = s.upload(x, F32), s.upload(y, F32)
     inputs += [xb, yb]
     st = torch.cuda.ExternalStream(s.stream, device=dev)
@@ -581,7 +747,7 @@ def bench_b200(args, world, rank, local):
     local_ms = sum(a.elapsed_time(b) for a, b in events)
     total_ms = allmax(local_ms, world)
     barrier(world)
-    tokens = world * CFG["batch"] * CFG["seq"] * args.steps
+    tokens = world * c["batch"] * c["seq"] * args.steps
     value = tokens / (total_ms / 1e3)
     ms_per_step = total_ms / args.steps
 
@@ -601,36 +767,52 @@ def bench_b200(args, world, rank, local):
     e2e_s = allmax(time.perf_counter() - t0, world)
     e2e_value = tokens / e2e_s
 
-    # ---- roofline of the dominant kernel (tcgen05 GEMM), back-to-back launches
-    k_ms, k_single_ms, k_flops = measure_kernel_roofline(s)
+    # ---- the step's own kernels, each timed alone (rank 0's GPU)
     hbm, tc_burst, tc_sust, src = peaks()
-    achieved_tf = k_flops / (k_ms / 1e3) / 1e12
-    step_tf = model_flops_per_token() * CFG["batch"] * CFG["seq"] / (ms_per_step / 1e3) / 1e12
-
+    bf = elem == BF16
+    kernels = measure_step_kernels(s, c, elem) if rank == 0 else []
+    for kr in kernels:
+        if kr["unit"] == "GB/s":
+            kr["peak"], kr["frac"] = hbm, kr["achieved"] / hbm
+        else:
+            kr["peak"] = tc_burst if bf else FP32_NOMINAL_TFLOPS
+            kr["frac"] = kr["achieved"] / kr["peak"]
+    head = kernels[0] if kernels else None
+    step_tf = model_flops_per_token(c) * c["batch"] * c["seq"] / (ms_per_step / 1e3) / 1e12
+    step_peak = tc_sust if bf else FP32_NOMINAL_TFLOPS
+    parallel = f"dp{world}" + (" strong" if strong else "")
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "nanoGPT-char value_and_grad 6L/6H/384 T=256 V=65, batch 64 per GPU",
-                   "global_batch": CFG["batch"] * world, "seq_len": CFG["seq"], "parallelism": f"dp{world}",
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong" if strong else "weak",
+        "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
+        "config": {"workload": f"{WORKLOAD[name]}, batch {c['batch']} per GPU", "global_batch": c["batch"] * world,
+                   "seq_len": c["seq"], "parallelism": parallel,
                    "l2": "256 MB buffer written before every timed step (outside the events)",
-                   "step_tflops": step_tf, "step_frac_of_bf16_peak": step_tf * 1e12 / (tc_sust * 1e12),
-                   "model_flop_per_token": model_flops_per_token(), "loss_at_warmup": loss0},
-        "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (fc: 16384x384 @ 384x1536, bf16)",
-                     "achieved": achieved_tf, "peak": tc_burst, "unit": "TFLOP/s", "frac": achieved_tf / tc_burst,
-                     # DRAM read + write per launch, from one ncu capture of this kernel and shape
-                     "traffic": FC_GEMM_DRAM_BYTES, "traffic_unit": "bytes per launch (ncu dram read + write)",
-                     "peak_source": f"{src} bf16_tflops (burst, kernel timed alone)",
-                     "timing": "16 back-to-back launches between CUDA events, each on its own operands and output "
-                               "(1 GB in all, above L2); mean of 5 batches",
-                     "launch_ms": k_ms, "single_launch_ms": k_single_ms},
+                   "step_tflops": step_tf, "step_frac_of_peak": step_tf / step_peak,
+                   "step_peak": ("measured bf16_tflops_sustained" if bf else "nominal FP32 CUDA-core peak") +
+                                f" {step_peak}",
+                   "model_flop_per_token": model_flops_per_token(c), "loss_at_warmup": loss0},
         "clocks": clk.summary(),
         "gpu_launches": int(launches),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(x.nbytes + y.nbytes),
-                "d2h_bytes_per_step": 2},
+                "d2h_bytes_per_step": 2 if bf else 4},
     }
+    if head is not None:
+        line["roofline"] = {
+            "bound": head["bound"], "kernel": f"{head['template']}: {head['kernel']} "
+                                              f"[{c['batch'] * c['seq']} x {c['n_embd']}] x [{c['n_embd']} x "
+                                              f"{4 * c['n_embd']}], as the step runs it",
+            "achieved": head["achieved"], "peak": head["peak"], "unit": head["unit"], "frac": head["frac"],
+            "traffic": FC_GELU_DRAM_BYTES.get(name) if bf else None,
+            "traffic_unit": "bytes per launch (ncu dram read + write)",
+            "peak_source": (f"{src} bf16_tflops (burst, kernel timed alone)" if bf else
+                            "nominal FP32 CUDA-core peak (no measured figure)"),
+            "timing": "back-to-back launches between CUDA events on the session stream, each on its own operands "
+                      "(over 1 GB in all, above L2); mean of 5 rounds",
+            "launch_ms": head["ms"]}
+        line["kernels"] = [{k: v for k, v in kr.items() if k != "work"} for kr in kernels]
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, sample = cpu_sample()
+        v, cores, sample = cpu_sample(name, c, args.dtype)
         line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
     if rank == 0:
         print(json.dumps(line), flush=True)

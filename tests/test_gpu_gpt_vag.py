@@ -150,6 +150,21 @@ def test_gpt2_small_shape_matches_oracle(cuda):
         assert_close(g, r, TOL_BF16, nm)
 
 
+def test_gpt2_small_shape_at_full_context_matches_oracle(cuda):
+    """GPT-2-small widths (12 heads, d 768, V=50304) at the full 1024-token
+    context, two layers, one sequence, bf16: attention over 1024 positions
+    (8 key tiles per query tile), the 50304-wide cross-entropy and head GEMMs,
+    the atomic embedding VJP of a large vocabulary. Oracle evaluated in f32."""
+    cfg = models.GPTConfig(n_layer=2, n_head=12, n_embd=768, block_size=1024, vocab_size=50304, batch=1, seq=1024)
+    leaves, x, y = models.gpt_inputs(cfg)
+    leaves = [odt.round_bf16(l) for l in leaves]
+    (out,) = run_vag(cfg, "bf16", leaves, x, y)
+    ref_loss, ref_grads = models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float32)
+    assert abs(float(out[0]) - ref_loss) <= TOL_BF16 * abs(ref_loss), (float(out[0]), ref_loss)
+    for nm, g, r in zip(models.gpt_leaf_names(cfg), out[1:], ref_grads):
+        assert_close(g, r, TOL_BF16, nm)
+
+
 def test_vag_rejects_bad_inputs(cuda):
     from sheaf_b200.runtime import SheafB200Error, Session
 
