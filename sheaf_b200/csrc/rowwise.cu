@@ -333,6 +333,134 @@ __global__ void __launch_bounds__(256) ce_fwd_bwd_kernel(const T* __restrict__ l
   }
 }
 
+// Cross-entropy for wide rows (GPT-2's 50304-entry vocabulary): one block
+// per row, 16-byte loads and stores. Pass 1 keeps an online (max, sum of
+// exp) per thread over 16-byte chunks, merged across the block; pass 2
+// re-reads the row (from L2: a row is at most a few hundred KB and the rows
+// in flight fit in L2) and writes dlogits. The row's loss term is read by
+// thread 0; each block sums its rows' terms in order into row_part.
+constexpr int kCeWideThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ void load_vec16(const T* p, float (&v)[16 / sizeof(T)]);
+template <>
+__device__ __forceinline__ void load_vec16<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load_vec16<float>(const float* p, float (&v)[4]) {
+  const float4 u = *reinterpret_cast<const float4*>(p);
+  v[0] = u.x;
+  v[1] = u.y;
+  v[2] = u.z;
+  v[3] = u.w;
+}
+template <typename T>
+__device__ __forceinline__ void store_vec16(T* p, const float (&v)[16 / sizeof(T)]);
+template <>
+__device__ __forceinline__ void store_vec16<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+template <>
+__device__ __forceinline__ void store_vec16<float>(float* p, const float (&v)[4]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kCeWideThreads) ce_wide_kernel(const T* __restrict__ logits, long ld, int rows,
+                                                                 int V, const float* __restrict__ targets,
+                                                                 T* __restrict__ dlogits, long ldd,
+                                                                 float* __restrict__ row_part, float inv_rows) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int E = 16 / sizeof(T);
+  constexpr int W = kCeWideThreads / 32;
+  __shared__ float sm_m[W], sm_s[W];
+  __shared__ float sm_row[2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+  const int nvec = V / E;  // whole 16-byte chunks; the tail (V % E) is done by scalar accesses
+  float part = 0.f;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const T* lr = logits + static_cast<long>(row) * ld;
+    float m = -INFINITY, sum = 0.f;
+    for (int i = threadIdx.x; i < nvec; i += kCeWideThreads) {
+      float v[E];
+      load_vec16(lr + static_cast<long>(i) * E, v);
+      float cm = v[0];
+#pragma unroll
+      for (int e = 1; e < E; ++e) cm = fmaxf(cm, v[e]);
+      const float nm = fmaxf(m, cm);
+      float acc = sum * expf(m - nm);
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc += expf(v[e] - nm);
+      sum = acc;
+      m = nm;
+    }
+    for (int c = nvec * E + threadIdx.x; c < V; c += kCeWideThreads) {
+      const float v = load1(lr + c);
+      const float nm = fmaxf(m, v);
+      sum = sum * expf(m - nm) + expf(v - nm);
+      m = nm;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, sum, o);
+      const float nm = fmaxf(m, m2);
+      // a lane that saw nothing has m = -inf, sum = 0: its term is 0
+      sum = (m == -INFINITY ? 0.f : sum * expf(m - nm)) + (m2 == -INFINITY ? 0.f : s2 * expf(m2 - nm));
+      m = nm;
+    }
+    if (lane == 0) {
+      sm_m[warp] = m;
+      sm_s[warp] = sum;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float bm = sm_m[0], bs = sm_s[0];
+      for (int w = 1; w < W; ++w) {  // fixed order
+        const float nm = fmaxf(bm, sm_m[w]);
+        bs = (bm == -INFINITY ? 0.f : bs * expf(bm - nm)) + (sm_m[w] == -INFINITY ? 0.f : sm_s[w] * expf(sm_m[w] - nm));
+        bm = nm;
+      }
+      const float lse = bm + logf(bs);
+      sm_row[0] = lse;
+      const int y = one_hot_class(targets[row], V);
+      sm_row[1] = static_cast<float>(y);
+      if (y >= 0) part += load1(lr + y) - lse;
+    }
+    __syncthreads();
+    const float lse = sm_row[0];
+    const int y = static_cast<int>(sm_row[1]);
+    const float hit = y >= 0 ? inv_rows : 0.f;
+    T* dr = dlogits + static_cast<long>(row) * ldd;
+    for (int i = threadIdx.x; i < nvec; i += kCeWideThreads) {
+      float v[E];
+      load_vec16(lr + static_cast<long>(i) * E, v);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const int c = i * E + e;
+        v[e] = expf(v[e] - lse) * hit - (c == y ? inv_rows : 0.f);
+      }
+      store_vec16(dr + static_cast<long>(i) * E, v);
+    }
+    for (int c = nvec * E + threadIdx.x; c < V; c += kCeWideThreads)
+      store1(dr + c, expf(load1(lr + c) - lse) * hit - (c == y ? inv_rows : 0.f));
+    __syncthreads();  // sm_m / sm_row are rewritten by the next row
+  }
+  if (threadIdx.x == 0) row_part[blockIdx.x] = part;
+}
+
 // loss = -(sum of block partials) / rows, written as f32 and/or bf16.
 __global__ void ce_finish_kernel(const float* __restrict__ part, int nparts, float inv_rows, float* loss_f32,
                                  __nv_bfloat16* loss_bf16) {
@@ -608,7 +736,18 @@ int cross_entropy_fwd_bwd(const void* logits, bool f32, long ld, int rows, int V
   const int warps = 8;
   const int grid = std::min((rows + warps - 1) / warps, 4 * num_sms_cached());
   const float inv = 1.0f / static_cast<float>(rows);
-  if (f32)
+  const size_t es = f32 ? 4 : 2;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(logits) | reinterpret_cast<uintptr_t>(dlogits) |
+                         (static_cast<uintptr_t>(ld) * es) | (static_cast<uintptr_t>(ldd) * es)) & 15) == 0;
+  if (V >= 2048 && aligned) {  // a block per row (grid <= the workspace's partial count)
+    if (f32)
+      launch_pdl((ce_wide_kernel<float>), dim3(grid), dim3(kCeWideThreads), 0, s, static_cast<const float*>(logits),
+                 ld, rows, V, targets, static_cast<float*>(dlogits), ldd, ws, inv);
+    else
+      launch_pdl((ce_wide_kernel<__nv_bfloat16>), dim3(grid), dim3(kCeWideThreads), 0, s,
+                 static_cast<const __nv_bfloat16*>(logits), ld, rows, V, targets,
+                 static_cast<__nv_bfloat16*>(dlogits), ldd, ws, inv);
+  } else if (f32)
     launch_pdl((ce_fwd_bwd_kernel<float>), dim3(grid), dim3(warps * 32), 0, s, static_cast<const float*>(logits), ld,
                rows, V, targets, static_cast<float*>(dlogits), ldd, ws, inv);
   else

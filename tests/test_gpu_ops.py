@@ -68,7 +68,10 @@ def test_layernorm(kind, rows, D, cuda):
 
 
 @pytest.mark.parametrize("kind", ["f32", "bf16"])
-@pytest.mark.parametrize("rows,V,ld", [(4096, 65, 72), (300, 1000, 1000), (64, 50304, 50304)])
+@pytest.mark.parametrize("rows,V,ld", [(4096, 65, 72), (300, 1000, 1000), (64, 50304, 50304),
+                                       # wide rows: 16-byte chunks plus a scalar tail (V % 8 != 0), an
+                                       # unaligned row stride (scalar warp path), more rows than blocks
+                                       (2000, 50257, 50264), (37, 4099, 4099), (1500, 2048, 2048)])
 def test_cross_entropy(kind, rows, V, ld, cuda):
     import torch
     import sheaf_b200 as sb
