@@ -245,6 +245,156 @@ __global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(con
   }
 }
 
+// ---------------------------------------------------------------------------
+// Layer norm for wide rows (D >= 1024): one block per row, each thread owning
+// CPT float4 column chunks (c = (j * threads + tid) * 4) of every row the
+// block visits, so no thread holds more than CPT x 16 bytes of a row in
+// registers and many rows are in flight per SM. Row sums go through warp
+// shuffles and one shared-memory word per warp, read back in warp order by
+// every thread (the same order for all rows: deterministic).
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float block_sum_ordered(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  const int warps = blockDim.x >> 5;
+  for (int w = 0; w < warps; ++w) t += red[w];
+  return t;
+}
+
+template <int CPT, typename TO>
+__global__ void __launch_bounds__(256) ln_fwd_wide_kernel(const float* __restrict__ x, const void* __restrict__ gamma,
+                                                          int gamma_f32, TO* __restrict__ y,
+                                                          float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                                          int rows, int D, float* __restrict__ x_copy) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red1[32], red2[32];
+  const int nt = blockDim.x, tid = threadIdx.x;
+  float4 g[CPT];
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int c = (j * nt + tid) * 4;
+    g[j] = c < D ? (gamma_f32 ? load4(static_cast<const float*>(gamma) + c)
+                              : load4(static_cast<const __nv_bfloat16*>(gamma) + c))
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const long off = static_cast<long>(row) * D;
+    float4 v[CPT];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int c = (j * nt + tid) * 4;
+      v[j] = c < D ? load4(x + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    }
+    if (x_copy) {
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        const int c = (j * nt + tid) * 4;
+        if (c < D) store4(x_copy + off + c, v[j]);
+      }
+    }
+    const float mean = block_sum_ordered(s, red1) / static_cast<float>(D);
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int c = (j * nt + tid) * 4;
+      if (c < D) {
+        const float a = v[j].x - mean, b = v[j].y - mean, cc = v[j].z - mean, d = v[j].w - mean;
+        q += (a * a + b * b) + (cc * cc + d * d);
+      }
+    }
+    const float var = block_sum_ordered(q, red2) / static_cast<float>(D);
+    const float rstd = 1.0f / sqrtf(var + 1e-5f);
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int c = (j * nt + tid) * 4;
+      if (c < D)
+        store4(y + off + c, make_float4(((v[j].x - mean) * rstd) * g[j].x, ((v[j].y - mean) * rstd) * g[j].y,
+                                        ((v[j].z - mean) * rstd) * g[j].z, ((v[j].w - mean) * rstd) * g[j].w));
+    }
+    if (tid == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+}
+
+template <int CPT, typename TI>
+__global__ void __launch_bounds__(256) ln_bwd_wide_kernel(const TI* __restrict__ dy, const float* __restrict__ x,
+                                                          const float* __restrict__ mean_in,
+                                                          const float* __restrict__ rstd_in,
+                                                          const void* __restrict__ gamma, int gamma_f32,
+                                                          float* __restrict__ dres, __nv_bfloat16* __restrict__ dres_bf,
+                                                          float* __restrict__ dgamma_part, int rows, int D) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red1[32], red2[32];
+  const int nt = blockDim.x, tid = threadIdx.x;
+  float4 g[CPT], dg[CPT];
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int c = (j * nt + tid) * 4;
+    g[j] = c < D ? (gamma_f32 ? load4(static_cast<const float*>(gamma) + c)
+                              : load4(static_cast<const __nv_bfloat16*>(gamma) + c))
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    dg[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const long off = static_cast<long>(row) * D;
+    const float mean = mean_in[row], rstd = rstd_in[row];
+    float4 xh[CPT], dxh[CPT], r[CPT];
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int c = (j * nt + tid) * 4;
+      const bool in = c < D;
+      xh[j] = in ? load4(x + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      dxh[j] = in ? load4(dy + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      r[j] = in ? load4(dres + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int c = (j * nt + tid) * 4;
+      if (c < D) {
+        xh[j] = make_float4((xh[j].x - mean) * rstd, (xh[j].y - mean) * rstd, (xh[j].z - mean) * rstd,
+                            (xh[j].w - mean) * rstd);
+        dg[j].x += dxh[j].x * xh[j].x;
+        dg[j].y += dxh[j].y * xh[j].y;
+        dg[j].z += dxh[j].z * xh[j].z;
+        dg[j].w += dxh[j].w * xh[j].w;
+        dxh[j] = make_float4(dxh[j].x * g[j].x, dxh[j].y * g[j].y, dxh[j].z * g[j].z, dxh[j].w * g[j].w);
+        s1 += (dxh[j].x + dxh[j].y) + (dxh[j].z + dxh[j].w);
+        s2 += (dxh[j].x * xh[j].x + dxh[j].y * xh[j].y) + (dxh[j].z * xh[j].z + dxh[j].w * xh[j].w);
+      }
+    }
+    const float c1 = block_sum_ordered(s1, red1) / static_cast<float>(D);
+    const float c2 = block_sum_ordered(s2, red2) / static_cast<float>(D);
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int c = (j * nt + tid) * 4;
+      if (c < D) {
+        r[j].x += rstd * (dxh[j].x - c1 - xh[j].x * c2);
+        r[j].y += rstd * (dxh[j].y - c1 - xh[j].y * c2);
+        r[j].z += rstd * (dxh[j].z - c1 - xh[j].z * c2);
+        r[j].w += rstd * (dxh[j].w - c1 - xh[j].w * c2);
+        store4(dres + off + c, r[j]);
+        if (dres_bf) store4(dres_bf + off + c, r[j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int c = (j * nt + tid) * 4;
+    if (c < D) *reinterpret_cast<float4*>(&dgamma_part[static_cast<long>(blockIdx.x) * D + c]) = dg[j];
+  }
+}
+
 // out[c] = sum_b part[b][c] in a fixed order, written as f32 or bf16. Block
 // of 1024 threads per 32 columns: warp w sums partial rows w, w+32, ... (lane =
 // column, coalesced), then the 32 warp sums are combined in order. Many short
@@ -614,6 +764,50 @@ __global__ void gelu_kernel(const T* __restrict__ x, const T* __restrict__ g, T*
   }
 }
 
+// bf16 GELU / GELU-VJP: 16-byte loads and stores (8 values), tanh from the
+// hardware approximation (PTX tanh.approx.f32, one MUFU op; its relative
+// error, about 2^-11, is below the bf16 rounding of the result). The f32
+// path keeps tanhf.
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool BWD>
+__global__ void __launch_bounds__(256) gelu_bf16_kernel(const __nv_bfloat16* __restrict__ x,
+                                                        const __nv_bfloat16* __restrict__ g,
+                                                        __nv_bfloat16* __restrict__ y, long n) {
+  pdl_wait();
+  pdl_trigger();
+  const long n8 = n / 8;
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    float a[8], gv[8], r[8];
+    load_vec16(x + 8 * i, a);
+    if (BWD) load_vec16(g + 8 * i, gv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float v = a[e], v2 = v * v;
+      const float t = tanh_fast(0.7978846f * (v + 0.044715f * (v * v2)));
+      if (BWD)
+        r[e] = gv[e] * (0.5f * (1.0f + t) + 0.5f * v * (1.0f - t * t) * 0.7978846f * (1.0f + 0.134145f * v2));
+      else
+        r[e] = 0.5f * (v * (1.0f + t));
+    }
+    store_vec16(y + 8 * i, r);
+  }
+  for (long i = n8 * 8 + blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const float v = __bfloat162float(x[i]), v2 = v * v;
+    const float t = tanh_fast(0.7978846f * (v + 0.044715f * (v * v2)));
+    const float r = BWD ? __bfloat162float(g[i]) *
+                              (0.5f * (1.0f + t) + 0.5f * v * (1.0f - t * t) * 0.7978846f * (1.0f + 0.134145f * v2))
+                        : 0.5f * (v * (1.0f + t));
+    y[i] = __float2bfloat16_rn(r);
+  }
+}
+
 __global__ void convert_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, long n) {
   pdl_wait();
   pdl_trigger();
@@ -654,9 +848,42 @@ int num_sms_cached() {
     else return 1;                                \
   } while (0)
 
+// Rows at least this wide take the block-per-row kernels.
+constexpr int kLnWideMin = 1024;
+
+namespace {
+// Threads per row (a multiple of 32, at most 256) and float4 chunks per
+// thread of the wide layer-norm kernels.
+int ln_wide_threads(int D) { return std::min(256, (D / 4 + 31) / 32 * 32); }
+int ln_wide_cpt(int D) { return (D / 4 + ln_wide_threads(D) - 1) / ln_wide_threads(D); }
+int ln_wide_grid(int rows) { return std::max(1, std::min(rows, 4 * num_sms_cached())); }
+}  // namespace
+
+#define SB_LN_WIDE_DISPATCH(CPT_EXPR, LAUNCH)              \
+  do {                                                     \
+    const int cpt_ = (CPT_EXPR);                           \
+    if (cpt_ <= 1) { constexpr int C = 1; LAUNCH; }        \
+    else if (cpt_ <= 2) { constexpr int C = 2; LAUNCH; }   \
+    else if (cpt_ <= 4) { constexpr int C = 4; LAUNCH; }   \
+    else if (cpt_ <= 8) { constexpr int C = 8; LAUNCH; }   \
+    else return 1;                                         \
+  } while (0)
+
 int layernorm_fwd(const float* x, const void* gamma, bool gamma_f32, void* y, bool y_f32, float* mean, float* rstd,
                   int rows, int D, cudaStream_t s, float* x_copy) {
   if (rows <= 0 || D <= 0 || (D & 3)) return 1;
+  if (D >= kLnWideMin) {
+    const int nt = ln_wide_threads(D), grid = ln_wide_grid(rows);
+    if (y_f32)
+      SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_fwd_wide_kernel<C, float>), dim3(grid), dim3(nt), 0, s, x,
+                                                      gamma, gamma_f32, static_cast<float*>(y), mean, rstd, rows, D,
+                                                      x_copy)));
+    else
+      SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_fwd_wide_kernel<C, __nv_bfloat16>), dim3(grid), dim3(nt), 0,
+                                                      s, x, gamma, gamma_f32, static_cast<__nv_bfloat16*>(y), mean,
+                                                      rstd, rows, D, x_copy)));
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+  }
   const int warps = 8;
   const int grid = std::min((rows + 2 * warps - 1) / (2 * warps), 4 * num_sms_cached());
   if (y_f32)
@@ -677,6 +904,7 @@ int ln_bwd_warps_for(int D) { return (D + 127) / 128 <= 3 ? 24 : 8; }
 }  // namespace
 
 size_t layernorm_bwd_workspace_bytes(int rows, int D) {
+  if (D >= kLnWideMin) return static_cast<size_t>(ln_wide_grid(rows)) * D * sizeof(float);
   return static_cast<size_t>(ln_bwd_grid(rows, ln_bwd_warps_for(D))) * D * sizeof(float);
 }
 
@@ -684,6 +912,19 @@ int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean
                   bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma, bool dgamma_f32, float* ws,
                   int rows, int D, cudaStream_t s) {
   if (rows <= 0 || D <= 0 || (D & 3)) return 1;
+  if (D >= kLnWideMin) {
+    const int nt = ln_wide_threads(D), grid = ln_wide_grid(rows);
+    if (dy_f32)
+      SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, float>), dim3(grid), dim3(nt), 0, s,
+                                                      static_cast<const float*>(dy), x, mean, rstd, gamma, gamma_f32,
+                                                      dres, dres_bf, ws, rows, D)));
+    else
+      SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, __nv_bfloat16>), dim3(grid), dim3(nt), 0,
+                                                      s, static_cast<const __nv_bfloat16*>(dy), x, mean, rstd, gamma,
+                                                      gamma_f32, dres, dres_bf, ws, rows, D)));
+    if (cudaPeekAtLastError() != cudaSuccess) return 4;
+    return column_sum(ws, grid, D, dgamma, dgamma_f32, s);
+  }
   const int warps = ln_bwd_warps_for(D);
   const int grid = ln_bwd_grid(rows, warps);
   const size_t smem = static_cast<size_t>(warps) * D * sizeof(float);
@@ -821,7 +1062,15 @@ int gelu(const void* x, const void* g, void* y, bool f32, bool bwd, long n, cuda
                  static_cast<float*>(y), n);
   } else {
     using B = __nv_bfloat16;
-    if (bwd)
+    const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                      (bwd ? reinterpret_cast<uintptr_t>(g) : 0)) & 15) == 0;
+    if (al && bwd)
+      launch_pdl((gelu_bf16_kernel<true>), dim3(blocks), dim3(256), 0, s, static_cast<const B*>(x),
+                 static_cast<const B*>(g), static_cast<B*>(y), n);
+    else if (al)
+      launch_pdl((gelu_bf16_kernel<false>), dim3(blocks), dim3(256), 0, s, static_cast<const B*>(x), nullptr,
+                 static_cast<B*>(y), n);
+    else if (bwd)
       launch_pdl((gelu_kernel<B, true>), dim3(blocks), dim3(256), 0, s, static_cast<const B*>(x),
                  static_cast<const B*>(g), static_cast<B*>(y), n);
     else

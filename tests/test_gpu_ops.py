@@ -33,7 +33,9 @@ def _stream():
 
 
 @pytest.mark.parametrize("kind", ["f32", "bf16"])
-@pytest.mark.parametrize("rows,D", [(1000, 384), (77, 768), (64, 4096)])
+@pytest.mark.parametrize("rows,D", [(1000, 384), (77, 768), (64, 4096),
+                                    # block-per-row kernels: more rows than blocks, a ragged last chunk
+                                    (1500, 4096), (700, 1024), (33, 8192), (2000, 2052)])
 def test_layernorm(kind, rows, D, cuda):
     import torch
     import sheaf_b200 as sb
