@@ -953,6 +953,13 @@ int layernorm_bwd_capped(const float* dy, const float* x, const float* mean, con
                          bool gamma_f32, float* dres, void* dgamma, bool dgamma_f32, float* scratch, int max_blocks,
                          int rows, int D, cudaStream_t s) {
   if (rows <= 0 || D <= 0 || (D & 3) || max_blocks <= 0) return 1;
+  if (D >= kLnWideMin) {  // the kernel layernorm_bwd uses at this width, on fewer blocks
+    const int nt = ln_wide_threads(D), grid = std::min(ln_wide_grid(rows), max_blocks);
+    SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, float>), dim3(grid), dim3(nt), 0, s, dy, x,
+                                                    mean, rstd, gamma, gamma_f32, dres, nullptr, scratch, rows, D)));
+    if (cudaPeekAtLastError() != cudaSuccess) return 4;
+    return column_sum(scratch, grid, D, dgamma, dgamma_f32, s);
+  }
   const int warps = 8;
   const int grid = std::min(std::min((rows + warps - 1) / warps, 2 * num_sms_cached()), max_blocks);
   const size_t smem = static_cast<size_t>(warps) * D * sizeof(float);
