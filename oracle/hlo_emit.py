@@ -332,7 +332,9 @@ def softmax(e: Emitter, x: V) -> V:
 
 
 def cross_entropy(e: Emitter, logits: V, y: V):
-    """lib/nn.shf:44-50 and its VJP (softmax - one_hot) / N."""
+    """lib/nn.shf:44-50 and its VJP (softmax * sum(one_hot) - one_hot) / N
+    (the mean, sum, multiply and log-softmax rules composed: a row whose
+    one-hot is all zero gets no gradient)."""
     Vn = logits.shape[-1]
     flat = e.reshape(logits, (int(np.prod(logits.shape[:-1])), Vn))
     s = e.sub(flat, e.reduce("maximum", flat, -1, True))
@@ -346,7 +348,7 @@ def cross_entropy(e: Emitter, logits: V, y: V):
     loss = e.mul(e.mean(tl, 0), e.scal(-1.0, tl))
     n = float(flat.shape[0])
     p = e.unary("exponential", logp)
-    dflat = e.div(e.sub(p, mask), e.scal(n, p))
+    dflat = e.div(e.sub(e.mul(p, e.sum(mask, -1, keepdims=True)), mask), e.scal(n, p))
     return loss, e.reshape(dflat, logits.shape)
 
 
@@ -381,12 +383,19 @@ def gpt_vag_module(cfg: models.GPTConfig, dt: str = "bf16") -> str:
     of model.shf:85-113 + cross-entropy and a backward following the VJP
     rules. Args: the params leaves in sorted-key order, then x, y ids (f32)."""
     e = Emitter()
-    L, H, D, Vv, P, B, T = cfg.n_layer, cfg.n_head, cfg.n_embd, cfg.vocab_size, cfg.block_size, cfg.batch, cfg.seq
-    Hd = D // H
+    B, T = cfg.batch, cfg.seq
     shapes = models.gpt_leaf_shapes(cfg)
     params = [arg(i, s, dt) for i, s in enumerate(shapes)]
     xid = arg(len(shapes), (B, T), "f32")
     yid = arg(len(shapes) + 1, (B, T), "f32")
+    loss, grads = gpt_vag_graph(e, cfg, dt, params, xid, yid)
+    return e.module("__vag_nanogpt", "value_and_grad", params + [xid, yid], [loss] + grads)
+
+
+def gpt_vag_graph(e: Emitter, cfg: models.GPTConfig, dt: str, params, xid: V, yid: V):
+    """Emits the nanoGPT loss and its gradients (one per params leaf)."""
+    L, H, D, Vv, P, B, T = cfg.n_layer, cfg.n_head, cfg.n_embd, cfg.vocab_size, cfg.block_size, cfg.batch, cfg.seq
+    Hd = D // H
     head = params[0]
     blocks = [params[1 + 6 * l: 7 + 6 * l] for l in range(L)]
     lnf, wpe, wte = params[1 + 6 * L], params[2 + 6 * L], params[3 + 6 * L]
@@ -462,7 +471,63 @@ def gpt_vag_module(cfg: models.GPTConfig, dt: str = "bf16") -> str:
         oh = e.convert(oh, dt)
     grads[3 + 6 * L] = e.matmul(e.transpose(oh, [1, 0]), flat(dx, D))
     grads[2 + 6 * L] = e.pad(e.sum(dx, 0), [0, 0], [P - T, 0])
-    return e.module("__vag_nanogpt", "value_and_grad", params + [xid, yid], [loss] + grads)
+    return loss, grads
+
+
+def gpt_train_module(cfg: models.GPTConfig, dt: str = "bf16", b1=0.9, b2=0.95, eps=1e-8, wd=0.1, max_norm=1.0,
+                     with_key=False) -> str:
+    """nanoGPT train-step (examples/nanogpt/train.shf:26-33) as one module:
+    value_and_grad, clip-by-global-norm and adamw-step (sheaf/lib/optim.shf,
+    inlined with the literals train-step passes). Args: the state pytree's
+    leaves in sorted-key order -- [key [4] when the state carries one], loss,
+    m leaves, params leaves, t (f32), v leaves -- then x, y ids and lr (f32);
+    returns the new state in the same order (`assoc` keeps the key)."""
+    e = Emitter()
+    B, T = cfg.batch, cfg.seq
+    shapes = models.gpt_leaf_shapes(cfg)
+    n = len(shapes)
+    i = 0
+    key = None
+    if with_key:
+        key = arg(0, (4,), "f32")
+        i = 1
+    loss0 = arg(i, (), dt)
+    m = [arg(i + 1 + j, s, dt) for j, s in enumerate(shapes)]
+    params = [arg(i + 1 + n + j, s, dt) for j, s in enumerate(shapes)]
+    t = arg(i + 1 + 2 * n, (), "f32")
+    v = [arg(i + 2 + 2 * n + j, s, dt) for j, s in enumerate(shapes)]
+    xid = arg(i + 2 + 3 * n, (B, T), "f32")
+    yid = arg(i + 3 + 3 * n, (B, T), "f32")
+    lr = arg(i + 4 + 3 * n, (), "f32")
+    loss, grads = gpt_vag_graph(e, cfg, dt, params, xid, yid)
+    # clip-by-global-norm (optim.shf): sqrt of the f32 sum of every leaf's sum of squares
+    total = e.const(0.0, "f32")
+    for g in grads:
+        sq = e.binop("power", g, e.scal(2.0, g))
+        total = e.add(total, e.convert(e.sum_all(sq), "f32") if dt != "f32" else e.sum_all(sq))
+    gnorm = e.unary("sqrt", total)
+    factor = e.binop("minimum", e.const(1.0, "f32"), e.div(e.const(max_norm, "f32"),
+                                                          e.add(gnorm, e.const(1e-8, "f32"))))
+    fac = e.convert(factor, dt) if dt != "f32" else factor
+    grads = [e.mul(g, fac) for g in grads]
+    # adamw-step
+    t1 = e.add(t, e.const(1.0, "f32"))
+    bcm = e.div(e.const(1.0, "f32"), e.sub(e.const(1.0, "f32"), e.binop("power", e.const(b1, "f32"), t1)))
+    bcv = e.div(e.const(1.0, "f32"), e.sub(e.const(1.0, "f32"), e.binop("power", e.const(b2, "f32"), t1)))
+    cast = (lambda x: e.convert(x, dt)) if dt != "f32" else (lambda x: x)  # noqa: E731
+    bcm_t, bcv_t, lr_t = cast(bcm), cast(bcv), cast(lr)
+    new_m, new_v, new_p = [], [], []
+    for mj, vj, pj, gj in zip(m, v, params, grads):
+        nm = e.add(e.mul(e.const(b1, dt), mj), e.mul(e.const(1.0 - b1, dt), gj))
+        nv = e.add(e.mul(e.const(b2, dt), vj), e.mul(e.const(1.0 - b2, dt), e.mul(gj, gj)))
+        upd = e.div(e.mul(nm, bcm_t), e.add(e.unary("sqrt", e.mul(nv, bcv_t)), e.const(eps, dt)))
+        np_ = e.sub(pj, e.mul(lr_t, e.add(e.mul(e.const(wd, dt), pj), upd)))
+        new_m.append(nm)
+        new_v.append(nv)
+        new_p.append(np_)
+    ins = ([key] if key else []) + [loss0] + m + params + [t] + v + [xid, yid, lr]
+    outs = ([key] if key else []) + [loss] + new_m + new_p + [t1] + new_v
+    return e.module("__jit_train_step", "train_step", ins, outs)
 
 
 def _tril(e: Emitter, T: int, dt: str) -> V:

@@ -446,10 +446,133 @@ int dynamic_update(void* out, const void* upd, int dt, const DynSlice& d, cudaSt
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
+// ---------------------------------------------------------------------------
+// Rows longer than one CTA's shared memory holds: a stable sort on 64-bit
+// composite keys, (order-preserving image of the key) << 32 | position, so
+// that ascending unsigned order is (key in the requested direction, then
+// position) and every composite is distinct. -0.0 is folded into +0.0 (the
+// two compare equal, so they keep their positions' order). Chunks of
+// kSortChunk composites are sorted in shared memory, then runs are merged
+// pairwise in global memory (merge path: each thread finds its split of the
+// two runs by binary search, then merges kSortIpt outputs); a last pass
+// copies the keys and payload of each position into place.
+// ---------------------------------------------------------------------------
+
+constexpr int kSortChunk = 8192;
+constexpr int kSortIpt = 8;
+
+__device__ __forceinline__ uint64_t sort_composite(float v, int pos, int descending) {
+  if (v == 0.f) v = 0.f;  // -0.0 -> +0.0
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // ascending float order as unsigned order
+  if (descending) u = ~u;
+  return (static_cast<uint64_t>(u) << 32) | static_cast<uint32_t>(pos);
+}
+
+__global__ void __launch_bounds__(1024) sort_chunk_kernel(const void* keys, int key_dt, int n, int npad,
+                                                          int descending, uint64_t* out) {
+  extern __shared__ uint64_t sk[];  // kSortChunk composites (64 KB, dynamic)
+  const long row = blockIdx.y;
+  const int base = blockIdx.x * kSortChunk;
+  for (int i = threadIdx.x; i < kSortChunk; i += blockDim.x) {
+    const int pos = base + i;
+    sk[i] = pos < n ? sort_composite(ld(keys, row * n + pos, key_dt), pos, descending) : ~0ull;
+  }
+  __syncthreads();
+  for (int size = 2; size <= kSortChunk; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < kSortChunk; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const uint64_t a = sk[i], b = sk[j];
+          const bool up = (i & size) == 0;
+          if (up ? (b < a) : (a < b)) {
+            sk[i] = b;
+            sk[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  uint64_t* o = out + row * npad + base;
+  for (int i = threadIdx.x; i < kSortChunk; i += blockDim.x) o[i] = sk[i];
+}
+
+// Merges the run pairs of length `run` of every row (npad composites a row).
+__global__ void __launch_bounds__(256) sort_merge_kernel(const uint64_t* in, uint64_t* out, int npad, int run) {
+  const long row = blockIdx.y;
+  const long k0 = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) * kSortIpt;
+  if (k0 >= npad) return;
+  const long base = k0 / (2L * run) * (2L * run);
+  const uint64_t* A = in + row * npad + base;
+  const long lenA = min(static_cast<long>(run), npad - base);
+  const uint64_t* Bp = A + lenA;
+  const long lenB = max(0L, min(static_cast<long>(run), npad - base - lenA));
+  const long k = k0 - base;
+  long lo = max(0L, k - lenB), hi = min(k, lenA);
+  while (lo < hi) {  // i = number of A elements among the first k outputs
+    const long mid = (lo + hi) >> 1;
+    if (A[mid] <= Bp[k - 1 - mid])
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  long i = lo, j = k - lo;
+  uint64_t* o = out + row * npad + base + k;
+  const long cnt = min(static_cast<long>(kSortIpt), lenA + lenB - k);
+  for (long t = 0; t < cnt; ++t) {
+    const bool takeA = j >= lenB || (i < lenA && A[i] <= Bp[j]);
+    o[t] = takeA ? A[i++] : Bp[j++];
+  }
+}
+
+__global__ void sort_gather_kernel(const uint64_t* sorted, int npad, const void* keys, int key_dt,
+                                   const int32_t* payload, void* out_keys, int32_t* out_payload, long rows, int n) {
+  const long total = rows * n;
+  const int es = key_dt == DT_F32 ? 4 : 2;
+  for (long e = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<long>(gridDim.x) * blockDim.x) {
+    const long row = e / n, i = e % n;
+    const long src = row * n + static_cast<uint32_t>(sorted[row * npad + i]);
+    out_payload[e] = payload[src];
+    const char* kp = static_cast<const char*>(keys) + src * es;
+    char* op = static_cast<char*>(out_keys) + e * es;
+    for (int b = 0; b < es; ++b) op[b] = kp[b];
+  }
+}
+
+size_t sort_rows_workspace_bytes(long rows, int n) {
+  if (n <= kSortSmemRow) return 0;
+  const long npad = (static_cast<long>(n) + kSortChunk - 1) / kSortChunk * kSortChunk;
+  return static_cast<size_t>(2 * rows * npad) * sizeof(uint64_t);
+}
+
 int sort_rows(const void* keys, int key_dt, const int32_t* payload, void* out_keys, int32_t* out_payload, long rows,
-              int n, bool descending, cudaStream_t s) {
+              int n, bool descending, void* ws, size_t ws_bytes, cudaStream_t s) {
   if (rows == 0 || n == 0) return 0;
   if (n > kSortMaxRow || (key_dt != DT_F32 && key_dt != DT_BF16)) return 1;
+  if (n > kSortSmemRow) {
+    if (!ws || ws_bytes < sort_rows_workspace_bytes(rows, n) || rows > 65535) return 1;
+    const int npad = (n + kSortChunk - 1) / kSortChunk * kSortChunk;
+    uint64_t* a = static_cast<uint64_t*>(ws);
+    uint64_t* b = a + rows * npad;
+    const size_t csm = kSortChunk * sizeof(uint64_t);
+    if (cudaFuncSetAttribute(sort_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(csm)) !=
+        cudaSuccess)
+      return 3;
+    sort_chunk_kernel<<<dim3(npad / kSortChunk, static_cast<unsigned>(rows)), 1024, csm, s>>>(
+        keys, key_dt, n, npad, descending ? 1 : 0, a);
+    for (int run = kSortChunk; run < npad; run *= 2) {
+      const long threads = (npad + kSortIpt - 1) / kSortIpt;
+      sort_merge_kernel<<<dim3(static_cast<unsigned>((threads + 255) / 256), static_cast<unsigned>(rows)), 256, 0,
+                          s>>>(a, b, npad, run);
+      std::swap(a, b);
+    }
+    sort_gather_kernel<<<blocks_for(rows * n), 256, 0, s>>>(a, npad, keys, key_dt, payload, out_keys, out_payload,
+                                                           rows, n);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+  }
   int np2 = 1;
   while (np2 < n) np2 <<= 1;
   const size_t smem = static_cast<size_t>(np2) * 8;

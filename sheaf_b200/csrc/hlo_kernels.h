@@ -45,7 +45,10 @@ struct DynSlice {
 };
 
 // Longest row the sort kernel handles (one CTA sorts a row in shared memory).
-constexpr int kSortMaxRow = 16384;
+// Rows up to kSortSmemRow sort in one CTA's shared memory; longer rows (up to
+// kSortMaxRow) take a chunked merge sort with sort_rows_workspace_bytes of scratch.
+constexpr int kSortSmemRow = 16384;
+constexpr int kSortMaxRow = 1 << 24;
 
 int dt_size(int dt);
 int unary(const void* a, void* out, long n, int op, int dta, int dto, cudaStream_t s);
@@ -67,8 +70,9 @@ int dynamic_update(void* out, const void* upd, int dt, const DynSlice& d, cudaSt
 // Stable sort of `rows` rows of n keys (f32 or bf16) along the last axis,
 // carrying an i32 payload: descending for a GT comparator, ascending for LT;
 // equal keys keep their input order.
+size_t sort_rows_workspace_bytes(long rows, int n);
 int sort_rows(const void* keys, int key_dt, const int32_t* payload, void* out_keys, int32_t* out_payload, long rows,
-              int n, bool descending, cudaStream_t s);
+              int n, bool descending, void* ws, size_t ws_bytes, cudaStream_t s);
 
 }  // namespace hlo
 }  // namespace sb

@@ -527,8 +527,19 @@ __device__ __forceinline__ void store_vec16<float>(float* p, const float (&v)[4]
   *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
 }
 
+// 2^x from the hardware approximation (PTX ex2.approx.ftz.f32: relative
+// error about 2^-22, far below the bf16 rounding of dlogits and the f32
+// parity bar).
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Scores are handled in log2 units (x * log2 e), so every exponential is one
+// ex2. Four 16-byte chunks per thread are loaded before any is used.
 template <typename T>
-__global__ void __launch_bounds__(kCeWideThreads) ce_wide_kernel(const T* __restrict__ logits, long ld, int rows,
+__global__ void __launch_bounds__(kCeWideThreads, 3) ce_wide_kernel(const T* __restrict__ logits, long ld, int rows,
                                                                  int V, const float* __restrict__ targets,
                                                                  T* __restrict__ dlogits, long ldd,
                                                                  float* __restrict__ row_part, float inv_rows) {
@@ -536,6 +547,8 @@ __global__ void __launch_bounds__(kCeWideThreads) ce_wide_kernel(const T* __rest
   pdl_trigger();
   constexpr int E = 16 / sizeof(T);
   constexpr int W = kCeWideThreads / 32;
+  constexpr int U = 4;
+  constexpr float kL2e = 1.4426950408889634f;
   __shared__ float sm_m[W], sm_s[W];
   __shared__ float sm_row[2];
   const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
@@ -543,24 +556,40 @@ __global__ void __launch_bounds__(kCeWideThreads) ce_wide_kernel(const T* __rest
   float part = 0.f;
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
     const T* lr = logits + static_cast<long>(row) * ld;
-    float m = -INFINITY, sum = 0.f;
-    for (int i = threadIdx.x; i < nvec; i += kCeWideThreads) {
-      float v[E];
-      load_vec16(lr + static_cast<long>(i) * E, v);
-      float cm = v[0];
+    float m = -INFINITY, sum = 0.f;  // running max (log2 units) and sum of 2^(x - m)
+    for (int i0 = threadIdx.x; i0 < nvec; i0 += U * kCeWideThreads) {
+      float v[U][E];
 #pragma unroll
-      for (int e = 1; e < E; ++e) cm = fmaxf(cm, v[e]);
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * kCeWideThreads;
+        if (i < nvec) {
+          load_vec16(lr + static_cast<long>(i) * E, v[u]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < E; ++e) v[u][e] = -INFINITY;
+        }
+      }
+      float cm = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          v[u][e] *= kL2e;
+          cm = fmaxf(cm, v[u][e]);
+        }
       const float nm = fmaxf(m, cm);
-      float acc = sum * expf(m - nm);
+      float acc = m == -INFINITY ? 0.f : sum * ex2_fast(m - nm);
 #pragma unroll
-      for (int e = 0; e < E; ++e) acc += expf(v[e] - nm);
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc += ex2_fast(v[u][e] - nm);
       sum = acc;
       m = nm;
     }
     for (int c = nvec * E + threadIdx.x; c < V; c += kCeWideThreads) {
-      const float v = load1(lr + c);
+      const float v = load1(lr + c) * kL2e;
       const float nm = fmaxf(m, v);
-      sum = sum * expf(m - nm) + expf(v - nm);
+      sum = (m == -INFINITY ? 0.f : sum * ex2_fast(m - nm)) + ex2_fast(v - nm);
       m = nm;
     }
 #pragma unroll
@@ -568,7 +597,7 @@ __global__ void __launch_bounds__(kCeWideThreads) ce_wide_kernel(const T* __rest
       const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, sum, o);
       const float nm = fmaxf(m, m2);
       // a lane that saw nothing has m = -inf, sum = 0: its term is 0
-      sum = (m == -INFINITY ? 0.f : sum * expf(m - nm)) + (m2 == -INFINITY ? 0.f : s2 * expf(m2 - nm));
+      sum = (m == -INFINITY ? 0.f : sum * ex2_fast(m - nm)) + (m2 == -INFINITY ? 0.f : s2 * ex2_fast(m2 - nm));
       m = nm;
     }
     if (lane == 0) {
@@ -580,32 +609,43 @@ __global__ void __launch_bounds__(kCeWideThreads) ce_wide_kernel(const T* __rest
       float bm = sm_m[0], bs = sm_s[0];
       for (int w = 1; w < W; ++w) {  // fixed order
         const float nm = fmaxf(bm, sm_m[w]);
-        bs = (bm == -INFINITY ? 0.f : bs * expf(bm - nm)) + (sm_m[w] == -INFINITY ? 0.f : sm_s[w] * expf(sm_m[w] - nm));
+        bs = (bm == -INFINITY ? 0.f : bs * ex2_fast(bm - nm)) +
+             (sm_m[w] == -INFINITY ? 0.f : sm_s[w] * ex2_fast(sm_m[w] - nm));
         bm = nm;
       }
-      const float lse = bm + logf(bs);
-      sm_row[0] = lse;
+      const float lse2 = bm + log2f(bs);  // log-sum-exp in log2 units
+      sm_row[0] = lse2;
       const int y = one_hot_class(targets[row], V);
       sm_row[1] = static_cast<float>(y);
-      if (y >= 0) part += load1(lr + y) - lse;
+      if (y >= 0) part += (load1(lr + y) * kL2e - lse2) * (1.0f / kL2e);
     }
     __syncthreads();
-    const float lse = sm_row[0];
+    const float lse2 = sm_row[0];
     const int y = static_cast<int>(sm_row[1]);
     const float hit = y >= 0 ? inv_rows : 0.f;
     T* dr = dlogits + static_cast<long>(row) * ldd;
-    for (int i = threadIdx.x; i < nvec; i += kCeWideThreads) {
-      float v[E];
-      load_vec16(lr + static_cast<long>(i) * E, v);
+    for (int i0 = threadIdx.x; i0 < nvec; i0 += U * kCeWideThreads) {
+      float v[U][E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const int c = i * E + e;
-        v[e] = expf(v[e] - lse) * hit - (c == y ? inv_rows : 0.f);
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * kCeWideThreads;
+        if (i < nvec) load_vec16(lr + static_cast<long>(i) * E, v[u]);
       }
-      store_vec16(dr + static_cast<long>(i) * E, v);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * kCeWideThreads;
+        if (i < nvec) {
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            const int c = i * E + e;
+            v[u][e] = ex2_fast(fmaf(v[u][e], kL2e, -lse2)) * hit - (c == y ? inv_rows : 0.f);
+          }
+          store_vec16(dr + static_cast<long>(i) * E, v[u]);
+        }
+      }
     }
     for (int c = nvec * E + threadIdx.x; c < V; c += kCeWideThreads)
-      store1(dr + c, expf(load1(lr + c) - lse) * hit - (c == y ? inv_rows : 0.f));
+      store1(dr + c, ex2_fast(fmaf(load1(lr + c), kL2e, -lse2)) * hit - (c == y ? inv_rows : 0.f));
     __syncthreads();  // sm_m / sm_row are rewritten by the next row
   }
   if (threadIdx.x == 0) row_part[blockIdx.x] = part;

@@ -45,6 +45,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <fstream>
+#include <functional>
 #include <map>
 #include <mutex>
 #include <memory>
@@ -115,6 +116,7 @@ struct HOp {
 
 struct HFunc {
   std::string name;
+  std::vector<std::string> arg_names;
   std::vector<TType> args;
   std::vector<TType> rets;
   std::vector<HOp> ops;
@@ -702,7 +704,7 @@ HModule parse_module(const char* text, size_t len) {
     c.expect("(");
     if (!c.accept(")")) {
       do {
-        c.value();
+        f.arg_names.push_back(c.value());
         c.expect(":");
         f.args.push_back(c.type());
         if (c.peek("{")) {  // argument attributes
@@ -1041,6 +1043,10 @@ class GenericFunc {
   }
 
   size_t op_scratch(const HOp& op) const {
+    if (op.kind == "sort") {
+      const int64_t len = op.type.shape.back();
+      return len ? sort_rows_workspace_bytes(op.type.numel() / len, static_cast<int>(len)) : 0;
+    }
     if (op.kind != "dot_general") return 0;
     Dot d = dot_of(op);
     size_t s = 0;
@@ -1279,8 +1285,9 @@ class GenericFunc {
     }
     if (k == "sort") {
       const int len = static_cast<int>(op.type.shape.back());
+      const long rows = len ? n / len : 0;
       return sort_rows(P(0), op.type.dt, static_cast<const int32_t*>(P(1)), o, static_cast<int32_t*>(ptr(op.result2, in)),
-                       len ? n / len : 0, len, op.descending, st);
+                       rows, len, op.descending, arena + scratch_off, sort_rows_workspace_bytes(rows, len), st);
     }
     if (k == "concatenate") {
       long off = 0;
@@ -1408,6 +1415,139 @@ bool match_gpt_vag(const HFunc& f, GptShape* g) {
   *g = GptShape{L, H, static_cast<int>(D), static_cast<int>(P), static_cast<int>(V), static_cast<int>(B),
                 static_cast<int>(T), elem_of(dt)};
   return true;
+}
+
+// The nanoGPT params leaves (sorted keys: lm_head, the blocks' six leaves each,
+// ln_f, wpe, wte) as args[first .. first + n) of element type dt; sets the
+// layer count, vocabulary, width and wpe rows.
+bool gpt_leaf_layout(const std::vector<TType>& a, size_t first, size_t n, int dt, int* L_out, int64_t* V_out,
+                     int64_t* D_out, int64_t* P_out) {
+  if (n < 10 || (n - 4) % 6 != 0 || first + n > a.size()) return false;
+  const int L = static_cast<int>((n - 4) / 6);
+  const auto& head = a[first].shape;
+  if (a[first].dt != dt || head.size() != 2) return false;
+  const int64_t V = head[0], D = head[1];
+  auto is = [&](size_t i, std::vector<int64_t> sh) { return a[first + i].dt == dt && a[first + i].shape == sh; };
+  for (int l = 0; l < L; ++l) {
+    const size_t b = 1 + 6 * l;
+    if (!is(b, {3 * D, D}) || !is(b + 1, {D, D}) || !is(b + 2, {D}) || !is(b + 3, {D}) || !is(b + 4, {4 * D, D}) ||
+        !is(b + 5, {D, 4 * D}))
+      return false;
+  }
+  const size_t t = 1 + 6 * L;
+  const TType& wpe = a[first + t + 1];
+  if (!is(t, {D}) || wpe.dt != dt || wpe.shape.size() != 2 || wpe.shape[1] != D || !is(t + 2, {V, D})) return false;
+  *L_out = L;
+  *V_out = V;
+  *D_out = D;
+  *P_out = wpe.shape[0];
+  return true;
+}
+
+// Heads of the attention: the q/k/v split reshapes [.., T, D] into [B, T, H, D/H].
+int gpt_heads(const HFunc& f, int64_t B, int64_t T, int64_t V, int64_t D, int L) {
+  int H = 0, gathers = 0, dots = 0;
+  for (auto& op : f.ops) {
+    if (op.kind == "gather" && op.operand_types[0].shape == std::vector<int64_t>({V, D})) ++gathers;
+    if (op.kind == "dot_general") ++dots;
+    const auto& s = op.type.shape;
+    if (op.kind == "reshape" && s.size() == 4 && s[0] == B && s[1] == T && s[2] * s[3] == D && H == 0)
+      H = static_cast<int>(s[2]);
+  }
+  return (gathers >= 1 && dots >= 4 * L) ? H : 0;
+}
+
+// Recognizer: nanoGPT train-step (examples/nanogpt/train.shf:26-33), one
+// module holding value_and_grad, clip-by-global-norm and adamw-step
+// (lib/optim.shf). Arguments: the state pytree's leaves in sorted-key order
+// -- an optional key [4] (f32), loss, m leaves, params leaves, t (f32), v
+// leaves -- then x, y (f32 ids [B, T]) and lr (f32); results: the new state
+// in the same order. The hyperparameters are literals in the module; they are
+// read off the ops that use them: b1 and b2 multiply the incoming m and v,
+// wd the incoming params, eps is added to sqrt(v-hat), and max_norm divides
+// the global norm plus 1e-8.
+bool match_gpt_train(const HFunc& f, GptShape* g, AdamwConfig* hp, bool* has_key) {
+  if (f.name.find("train_step") == std::string::npos) return false;
+  const size_t na = f.args.size();
+  for (size_t k = 0; k <= 1; ++k) {
+    if (k == 1 && !(f.args[0].dt == DT_F32 && f.args[0].shape == std::vector<int64_t>({4}))) continue;
+    if (na < k + 5 || (na - k - 5) % 3 != 0) continue;
+    const size_t n = (na - k - 5) / 3;
+    const int dt = f.args[k].dt;
+    if ((dt != DT_BF16 && dt != DT_F32) || !f.args[k].shape.empty()) continue;
+    int L = 0;
+    int64_t V = 0, D = 0, P = 0;
+    const size_t im = k + 1, ip = k + 1 + n, it = k + 1 + 2 * n, iv = k + 2 + 2 * n, ix = k + 2 + 3 * n;
+    if (!gpt_leaf_layout(f.args, ip, n, dt, &L, &V, &D, &P)) continue;
+    bool same = true;
+    for (size_t i = 0; i < n; ++i) same = same && f.args[im + i] == f.args[ip + i] && f.args[iv + i] == f.args[ip + i];
+    const TType& t = f.args[it];
+    const TType& x = f.args[ix];
+    const TType& lr = f.args[ix + 2];
+    if (!same || t.dt != DT_F32 || !t.shape.empty() || lr.dt != DT_F32 || !lr.shape.empty()) continue;
+    if (x.dt != DT_F32 || !(x == f.args[ix + 1]) || x.shape.size() != 2 || x.shape[1] > P) continue;
+    if (f.rets.size() != ix) continue;
+    bool rets_ok = true;
+    for (size_t i = 0; i < ix; ++i) rets_ok = rets_ok && f.rets[i] == f.args[i];
+    if (!rets_ok) continue;
+    const int64_t B = x.shape[0], T = x.shape[1];
+    const int H = gpt_heads(f, B, T, V, D, L);
+    if (H == 0) continue;
+    // hyperparameters
+    std::map<std::string, const HOp*> def;
+    for (auto& op : f.ops) def[op.result] = &op;
+    std::function<bool(const std::string&, double*)> scalar = [&](const std::string& r, double* v) {
+      auto it2 = def.find(r);
+      if (it2 == def.end()) return false;
+      const HOp* op = it2->second;
+      if (op->kind == "constant") {
+        if (op->values.size() != 1) return false;
+        *v = op->values[0];
+        return true;
+      }
+      if (op->kind == "broadcast_in_dim" || op->kind == "convert" || op->kind == "reshape")
+        return scalar(op->operands[0], v);
+      return false;
+    };
+    auto bin = [](const HOp& op, int b) { return op.kind == "binary" && op.binary_op == b && op.operands.size() == 2; };
+    auto is_sqrt = [&](const std::string& r) {
+      auto it2 = def.find(r);
+      return it2 != def.end() && it2->second->kind == "unary" && it2->second->unary_op == U_SQRT;
+    };
+    // the constant operand of a multiply whose other operand is `r`
+    auto const_times = [&](const std::string& r, double* v) {
+      for (auto& op : f.ops)
+        if (bin(op, B_MUL))
+          for (int s2 = 0; s2 < 2; ++s2)
+            if (op.operands[s2] == r && scalar(op.operands[1 - s2], v)) return true;
+      return false;
+    };
+    double b1 = 0, b2 = 0, wd = 0, eps = 0, mx = 0;
+    bool found_eps = false, found_mx = false;
+    for (auto& op : f.ops) {
+      if (bin(op, B_ADD) && op.type.shape == f.args[ip].shape)
+        for (int s2 = 0; s2 < 2 && !found_eps; ++s2)
+          if (is_sqrt(op.operands[s2]) && scalar(op.operands[1 - s2], &eps)) found_eps = true;
+      if (bin(op, B_DIV) && op.type.shape.empty() && !found_mx) {
+        double c = 0;
+        auto d = def.find(op.operands[1]);
+        if (scalar(op.operands[0], &mx) && d != def.end() && bin(*d->second, B_ADD) &&
+            (scalar(d->second->operands[1], &c) || scalar(d->second->operands[0], &c)) &&
+            std::fabs(c - 1e-8) < 1e-12)
+          found_mx = true;
+      }
+    }
+    if (f.arg_names.size() != na || !const_times(f.arg_names[im], &b1) || !const_times(f.arg_names[iv], &b2) ||
+        !const_times(f.arg_names[ip], &wd) || !found_eps || !found_mx)
+      continue;
+    *g = GptShape{L, H, static_cast<int>(D), static_cast<int>(P), static_cast<int>(V), static_cast<int>(B),
+                  static_cast<int>(T), elem_of(dt)};
+    *hp = AdamwConfig{static_cast<float>(b1), static_cast<float>(b2), static_cast<float>(eps),
+                      static_cast<float>(wd), static_cast<float>(mx)};
+    *has_key = k == 1;
+    return true;
+  }
+  return false;
 }
 
 // Host-side comparison of two output lists (per tensor, relative to the
@@ -1619,6 +1759,8 @@ class StableHloModule : public Module {
     std::unique_ptr<GenericFunc> generic;
     std::unique_ptr<Module> fused;  // the fused plan, when recognised and built
     bool vag = false;               // recognised as the nanoGPT value_and_grad (from the text alone)
+    bool train = false;             // recognised as the nanoGPT train-step
+    bool has_key = false;           // train-step state carries a PRNG key leaf first
     int fused_state = 0;            // 0 = unverified, 1 = verified, -1 = rejected
     int group_state = 0;            // the same, decided jointly by a data-parallel group
     std::string note;
@@ -1634,6 +1776,31 @@ class StableHloModule : public Module {
       if (kv.second.fused) kv.second.fused->teardown();
   }
 
+  // Runs the fused plan: value_and_grad as is; train_step without the key
+  // leaf (the plan does not use it), which is copied back in front of the
+  // new state.
+  sb_status fused_call(Session& s, Fn& f, const std::vector<Buffer*>& in, std::vector<Buffer*>& out) {
+    if (!f.train) return f.fused->call(s, "value_and_grad", in, out);
+    if (!f.has_key) return f.fused->call(s, "train_step", in, out);
+    std::vector<Buffer*> rest(in.begin() + 1, in.end());
+    std::vector<Buffer*> o;
+    SB_TRY(f.fused->call(s, "train_step", rest, o));
+    Buffer* key = nullptr;
+    sb_status st = buffer_create(s, in[0]->shape, in[0]->elem, &key);
+    if (!st && cudaMemcpyAsync(key->data(), in[0]->data(), in[0]->bytes(), cudaMemcpyDeviceToDevice, s.stream) !=
+                   cudaSuccess)
+      st = make_status(SB_STATUS_INTERNAL, "key copy failed");
+    if (st) {
+      if (key) buffer_release(key);
+      for (Buffer* b : o) buffer_release(b);
+      return st;
+    }
+    out.clear();
+    out.push_back(key);
+    out.insert(out.end(), o.begin(), o.end());
+    return nullptr;
+  }
+
   // This rank's first-call check: the generic executor's outputs (`ref`) and
   // whether the fused plan, run on this rank's inputs alone, agrees with
   // them. Returns an error only when the generic run fails.
@@ -1647,7 +1814,7 @@ class StableHloModule : public Module {
     }
     std::vector<Buffer*> fast;
     f.fused->set_collectives(false);
-    sb_status st = f.fused->call(s, "value_and_grad", in, fast);
+    sb_status st = fused_call(s, f, in, fast);
     f.fused->set_collectives(true);
     if (st) {
       *why = sb_status_message(st);
@@ -1677,8 +1844,8 @@ class StableHloModule : public Module {
   sb_status call(Session& s, const std::string& fn, const std::vector<Buffer*>& in,
                  std::vector<Buffer*>& out) override {
     Fn& f = fns.at(fn);
-    if (f.vag && s.comm && s.world > 1) return call_group(s, fn, f, in, out);
-    if (f.fused && f.fused_state == 1) return f.fused->call(s, "value_and_grad", in, out);
+    if ((f.vag || f.train) && s.comm && s.world > 1) return call_group(s, fn, f, in, out);
+    if (f.fused && f.fused_state == 1) return fused_call(s, f, in, out);
     if (f.fused && f.fused_state == 0) {
       std::vector<Buffer*> ref, fast;
       bool agree = false;
@@ -1686,7 +1853,8 @@ class StableHloModule : public Module {
       SB_TRY(check_fused(s, f, in, ref, &fast, &agree, &why));
       if (agree) {
         f.fused_state = 1;
-        f.note = "fused nanoGPT plan (verified against the generic executor on the first call, " + why + ")";
+        f.note = std::string(f.train ? "fused nanoGPT train-step plan" : "fused nanoGPT plan") +
+                 " (verified against the generic executor on the first call, " + why + ")";
         for (Buffer* b : ref) buffer_release(b);
         out = fast;
       } else {
@@ -1712,8 +1880,13 @@ class StableHloModule : public Module {
   // an error on every rank if any rank's generic run failed.
   sb_status call_group(Session& s, const std::string& fn, Fn& f, const std::vector<Buffer*>& in,
                        std::vector<Buffer*>& out) {
-    if (f.group_state == 1) return f.fused->call(s, "value_and_grad", in, out);
+    // a train step's outputs are the updated state: they cannot be averaged
+    // after the fact, so a group that rejects the fused train plan stops
+    const char* no_train = "train_step text in a data-parallel group needs the fused plan, which a rank's first-call "
+                           "check rejected";
+    if (f.group_state == 1) return fused_call(s, f, in, out);
     if (f.group_state == -1) {
+      if (f.train) return make_status(SB_STATUS_UNIMPLEMENTED, no_train);
       SB_TRY(f.generic->run(s, in, out));
       return average_outputs(s, out);
     }
@@ -1755,7 +1928,11 @@ class StableHloModule : public Module {
                   PlanRecord{f.plan_hash, fused ? "fused-verified" : "fused-rejected", f.note});
     if (fused) {
       for (Buffer* b : ref) buffer_release(b);
-      return f.fused->call(s, "value_and_grad", in, out);
+      return fused_call(s, f, in, out);
+    }
+    if (f.train) {
+      for (Buffer* b : ref) buffer_release(b);
+      return make_status(SB_STATUS_UNIMPLEMENTED, no_train);
     }
     out = ref;
     return average_outputs(s, out);
@@ -1818,18 +1995,21 @@ sb_status load_stablehlo_module(Session& s, const char* text, size_t len, std::u
     // recognition depends on the text alone, so every rank of a group
     // recognises the same functions whatever its plan cache holds
     fn.vag = match_gpt_vag(fn.generic->f, &g);
+    AdamwConfig hp{};
+    fn.train = !fn.vag && match_gpt_train(fn.generic->f, &g, &hp, &fn.has_key);
     if (cached && rec->second.plan == "fused-rejected") {
       fn.note = "generic executor (plan cache: " + rec->second.note + ")";
-    } else if (fn.vag) {
+    } else if (fn.vag || fn.train) {
       std::unique_ptr<Module> fused;
-      sb_status st = make_gpt_vag_module(s, hm.name + "." + f.name, g, &fused);
+      sb_status st = make_gpt_vag_module(s, hm.name + "." + f.name, g, &fused, fn.train ? &hp : nullptr);
       if (!st) {
         fn.fused = std::move(fused);
+        const std::string what = fn.train ? "fused nanoGPT train-step plan" : "fused nanoGPT plan";
         if (cached && rec->second.plan == "fused-verified") {
           fn.fused_state = 1;
-          fn.note = "fused nanoGPT plan (verified on an earlier load of this text by this build; plan cache)";
+          fn.note = what + " (verified on an earlier load of this text by this build; plan cache)";
         } else {
-          fn.note = "fused nanoGPT plan pending first-call verification";
+          fn.note = what + " pending first-call verification";
         }
       } else {
         fn.note = std::string("generic executor (fused plan unavailable: ") + sb_status_message(st) + ")";
@@ -1856,9 +2036,15 @@ sb_status validate_stablehlo(const char* text, size_t len, std::string* summary)
       GptShape gs;
       os << "\n" << f.name << ": " << f.ops.size() << " ops, " << f.args.size() << " args, " << f.rets.size()
          << " results, arena " << g.arena_bytes << " B";
+      AdamwConfig hp{};
+      bool key = false;
       if (match_gpt_vag(g.f, &gs))
         os << ", nanoGPT value_and_grad L=" << gs.n_layer << " H=" << gs.n_head << " D=" << gs.n_embd
            << " V=" << gs.vocab << " B=" << gs.batch << " T=" << gs.seq;
+      else if (match_gpt_train(g.f, &gs, &hp, &key))
+        os << ", nanoGPT train_step L=" << gs.n_layer << " H=" << gs.n_head << " D=" << gs.n_embd
+           << " V=" << gs.vocab << " B=" << gs.batch << " T=" << gs.seq << " b1=" << hp.b1 << " b2=" << hp.b2
+           << " eps=" << hp.eps << " wd=" << hp.wd << " max_norm=" << hp.max_norm << (key ? " (key leaf)" : "");
     }
     if (summary) *summary = os.str();
   } catch (const ParseError& e) {

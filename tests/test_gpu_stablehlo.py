@@ -141,6 +141,55 @@ def test_first_call_check_rejects_a_deviation_above_its_tolerance(cuda, monkeypa
         assert_close(np.asarray(g, np.float64).reshape(np.shape(p)), p, TOL_BF16)
 
 
+@pytest.mark.parametrize("dt,key", [("bf16", False), ("bf16", True), ("f32", False)])
+def test_nanogpt_train_step_text_uses_the_fused_train_plan(session, dt, key):
+    """The train-step module (value_and_grad + clip-by-global-norm + AdamW in
+    one text, examples/nanogpt/train.shf:26-33) is recognised, checked against
+    the generic executor on the first call and then run on the fused train
+    plan; two steps in a row (the second on the first's state) against the
+    model and optimizer oracles; a key leaf passes through unchanged."""
+    from oracle import optim
+
+    cfg = models.GPTConfig(n_layer=2, n_head=2, n_embd=128, block_size=64, vocab_size=65, batch=4, seq=64)
+    leaves, x, y = models.gpt_inputs(cfg)
+    rng = np.random.default_rng(9)
+    m = [rng.standard_normal(l.shape).astype(np.float32) * 1e-3 for l in leaves]
+    v = [np.abs(rng.standard_normal(l.shape)).astype(np.float32) * 1e-6 for l in leaves]
+    bf = dt == "bf16"
+    rnd = odt.round_bf16 if bf else (lambda a: np.asarray(a, np.float32))
+    leaves, m, v = [rnd(a) for a in leaves], [rnd(a) for a in m], [rnd(a) for a in v]
+    elem = BF16 if bf else F32
+    n = len(leaves)
+    text = hlo_emit.gpt_train_module(cfg, dt, with_key=key)
+    name = session.load_stablehlo(text)
+    assert "fused nanoGPT train-step plan pending first-call verification" in session.describe(name)
+    keyv = np.array([7.0, 1.0, 0.0, 3.0], np.float32)
+    t, lr = 2.0, 6e-4
+    state = [np.float32(0.0)] + m + leaves + [np.float32(t)] + v
+    elems = [elem] + [elem] * n + [elem] * n + [F32] + [elem] * n
+    tol = TOL_F32 if not bf else TOL_BF16
+    for step in range(2):
+        ins = ([keyv] if key else []) + state + [x, y, np.float32(lr)]
+        ies = ([F32] if key else []) + elems + [F32, F32, F32]
+        bufs = [session.upload(a, e) for a, e in zip(ins, ies)]
+        outs = [o.to_host() for o in session.call(f"{name}.train_step", bufs)]
+        if step == 0:
+            assert "fused nanoGPT train-step plan (verified" in session.describe(name), session.describe(name)
+        if key:
+            assert np.array_equal(outs[0], keyv)
+            outs = outs[1:]
+        mm, pp, tt, vv = state[1:1 + n], state[1 + n:1 + 2 * n], float(state[1 + 2 * n]), state[2 + 2 * n:]
+        loss, grads = models.gpt_value_and_grad(pp, x, y, cfg, dtype=np.float64)
+        p2, m2, v2, t2 = optim.adamw_step(pp, grads, mm, vv, tt, lr, bf16=bf)
+        assert abs(float(outs[0]) - loss) <= tol * abs(loss)
+        assert float(outs[1 + 2 * n]) == t2
+        for i in range(n):
+            assert_close(outs[1 + i], m2[i], tol, f"m {i}")
+            assert_close(outs[1 + n + i], p2[i], tol, f"p {i}")
+            assert_close(outs[2 + 2 * n + i], v2[i], tol, f"v {i}")
+        state = [np.asarray(o, np.float32) for o in outs]
+
+
 def test_full_nanogpt_text_module_verifies_at_full_size(session):
     """The 1948-op nanoGPT-char value_and_grad text (B=64, T=256): the first
     call runs the generic executor and the fused plan on the same inputs and
@@ -200,17 +249,23 @@ def test_reverse_and_dynamic_slices(session):
         assert np.array_equal(dus2, e)
 
 
-@pytest.mark.parametrize("direction,key", [("GT", "f32"), ("LT", "f32"), ("GT", "bf16")])
-def test_top_k_sort(session, direction, key):
-    """top_k through the emitter's sort: stable (ties keep index order), the
-    first k of every row, indices converted to f32; compared bit-exactly with
-    numpy's stable argsort."""
+@pytest.mark.parametrize("direction,key,n", [("GT", "f32", 1000), ("LT", "f32", 1000), ("GT", "bf16", 1000),
+                                             # rows beyond one CTA's shared memory (chunked merge sort):
+                                             # GPT-2's 50304-entry top_k, just past the limit, a partial chunk
+                                             ("GT", "f32", 50304), ("LT", "bf16", 50304), ("GT", "bf16", 16385),
+                                             ("GT", "f32", 70001)])
+def test_top_k_sort(session, direction, key, n):
+    """top_k through the emitter's sort: stable (ties keep index order, -0.0
+    ties with 0.0), the first k of every row, indices converted to f32;
+    compared bit-exactly with numpy's stable argsort."""
     from tests.test_stablehlo_parse import top_k_module
 
-    rows, n, k = 5, 1000, 37
+    rows, k = 5, 37 if n < 10000 else 200
     rng = np.random.default_rng(3)
     x = rng.integers(-20, 20, (rows, n)).astype(np.float32) * 0.25  # many ties
     x[0, :7] = 3.5
+    x[1, 5:9] = [0.0, -0.0, 0.0, -0.0]
+    x[1, 10:12] = 100.0
     if key == "bf16":
         x = odt.round_bf16(x)
     _, (vals, idx) = run(session, top_k_module(rows, n, k, direction, key), [x], [BF16 if key == "bf16" else F32])

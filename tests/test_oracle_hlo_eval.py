@@ -99,3 +99,32 @@ def test_indexing_forms():
     exp = np.zeros((5, 3))
     exp[1:3, 0:2] = tv[1:3]
     np.testing.assert_array_equal(pv, exp)
+
+
+@pytest.mark.parametrize("with_key", [False, True])
+def test_train_step_module_f32_matches_the_model_and_optimizer_oracles(with_key):
+    """The train-step text (value_and_grad + clip-by-global-norm + AdamW,
+    examples/nanogpt/train.shf:26-33 with lib/optim.shf inlined), evaluated
+    in f32, against oracle.models + oracle.optim."""
+    from oracle import optim
+
+    cfg = models.GPTConfig(n_layer=1, n_head=2, n_embd=128, block_size=64, vocab_size=65, batch=2, seq=64)
+    leaves, x, y = models.gpt_inputs(cfg)
+    rng = np.random.default_rng(3)
+    m = [rng.standard_normal(l.shape).astype(np.float32) * 1e-3 for l in leaves]
+    v = [np.abs(rng.standard_normal(l.shape)).astype(np.float32) * 1e-6 for l in leaves]
+    t, lr = 3.0, 6e-4
+    key = [np.arange(4, dtype=np.float32)] if with_key else []
+    ins = key + [np.float32(0.0)] + m + leaves + [np.float32(t)] + v + [x, y, np.float32(lr)]
+    out = hlo_eval.evaluate(hlo_emit.gpt_train_module(cfg, "f32", with_key=with_key), ins)
+    n = len(leaves)
+    if with_key:
+        np.testing.assert_array_equal(out[0], key[0])
+        out = out[1:]
+    loss, grads = models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float64)
+    p2, m2, v2, t2 = optim.adamw_step(leaves, grads, m, v, t, lr)
+    assert abs(float(out[0]) - loss) <= 1e-6 * abs(loss)
+    assert float(out[1 + 2 * n]) == t2
+    assert _max_rel(out[1:1 + n], m2) <= 2e-5
+    assert _max_rel(out[1 + n:1 + 2 * n], p2) <= 1e-5
+    assert _max_rel(out[2 + 2 * n:], v2) <= 2e-5

@@ -3,6 +3,7 @@ sb_stablehlo_validate on the module printed in the reference's docs, on
 modules in the emitter's text forms (oracle/hlo_emit.py), and rejection of
 ops outside the library's surface."""
 import json
+import re
 from pathlib import Path
 
 import pytest
@@ -30,6 +31,36 @@ def test_nanogpt_vag_module_is_recognised(dt):
     cfg = models.GPTConfig(n_layer=2, n_head=2, n_embd=128, block_size=64, vocab_size=65, batch=4, seq=64)
     s = validate_stablehlo(hlo_emit.gpt_vag_module(cfg, dt))
     assert "nanoGPT value_and_grad L=2 H=2 D=128 V=65 B=4 T=64" in s
+
+
+@pytest.mark.parametrize("dt,key,hp", [("bf16", False, {}), ("bf16", True, {}),
+                                       ("f32", False, dict(b1=0.8, b2=0.99, eps=1e-6, wd=0.01, max_norm=0.5))])
+def test_nanogpt_train_step_module_is_recognised(dt, key, hp):
+    """train-step (examples/nanogpt/train.shf:26-33): the state leaves, x, y, lr;
+    the AdamW / clip literals are read off the ops that use them."""
+    cfg = models.GPTConfig(n_layer=2, n_head=2, n_embd=128, block_size=64, vocab_size=65, batch=4, seq=64)
+    s = validate_stablehlo(hlo_emit.gpt_train_module(cfg, dt, with_key=key, **hp))
+    want = dict(b1=0.9, b2=0.95, eps=1e-8, wd=0.1, max_norm=1.0, **hp) if not hp else hp
+    assert "nanoGPT train_step L=2 H=2 D=128 V=65 B=4 T=64" in s, s
+    got = dict(re.findall(r"(b1|b2|eps|wd|max_norm)=([0-9.e+-]+)", s))
+    for k, v in want.items():
+        assert abs(float(got[k]) - v) <= 1e-6 * v, (k, got[k], v)
+    assert ("(key leaf)" in s) == key
+
+
+def test_train_step_with_a_missing_literal_is_not_recognised():
+    """Without the weight-decay multiply the hyperparameters cannot all be read:
+    the function stays on the generic executor."""
+    cfg = models.GPTConfig(n_layer=1, n_head=2, n_embd=128, block_size=64, vocab_size=65, batch=2, seq=64)
+    text = hlo_emit.gpt_train_module(cfg, "f32")
+    # the weight-decay term wd * p: replace it by p itself
+    lines = text.splitlines()
+    for i, ln in enumerate(lines):
+        m = re.match(r"\s+(%\d+) = stablehlo\.multiply (%\d+), (%arg\d+) : (tensor<[^>]*>)", ln)
+        if m:
+            lines[i] = f"    {m.group(1)} = stablehlo.add {m.group(3)}, {m.group(3)} : {m.group(4)}"
+    s = validate_stablehlo("\n".join(lines) + "\n")
+    assert "train_step" in s and "nanoGPT train_step" not in s
 
 
 def test_full_nanogpt_vag_module_plans():
@@ -120,7 +151,7 @@ def test_top_k_sort_parses():
 
 def test_sort_and_dynamic_slice_rejections():
     bad_cmp = top_k_module(3, 65, 5).replace('"stablehlo.compare"(%3, %4)', '"stablehlo.compare"(%5, %6)')
-    too_long = top_k_module(1, 20000, 5)
+    too_long = top_k_module(1, (1 << 24) + 8, 5)
     eq = top_k_module(3, 65, 5, "EQ")
     bad_start = INDEXING.replace("%arg1: tensor<i32>", "%arg1: tensor<f32>").replace(
         "tensor<i32>, tensor<i32>) -> tensor<2x3xf32>", "tensor<f32>, tensor<i32>) -> tensor<2x3xf32>")
