@@ -1598,6 +1598,105 @@ sb_status outputs_agree(const std::vector<Buffer*>& a, const std::vector<Buffer*
   return nullptr;
 }
 
+// Host copy of a float buffer (f32 or bf16) as doubles.
+sb_status host_values(const Buffer* b, std::vector<double>* out) {
+  const size_t n = b->bytes();
+  std::vector<char> h(n);
+  if (n) SB_CUDA_TRY(cudaMemcpy(h.data(), b->data(), n, cudaMemcpyDeviceToHost));
+  const bool bf = b->elem == SB_ELEM_BF16;
+  const size_t cnt = n / (bf ? 2 : 4);
+  out->resize(cnt);
+  for (size_t k = 0; k < cnt; ++k) {
+    float v;
+    if (bf) {
+      const uint32_t u = static_cast<uint32_t>(reinterpret_cast<uint16_t*>(h.data())[k]) << 16;
+      std::memcpy(&v, &u, 4);
+    } else {
+      v = reinterpret_cast<float*>(h.data())[k];
+    }
+    (*out)[k] = v;
+  }
+  return nullptr;
+}
+
+// The first-call comparison of a train step's new state (fast) with the
+// generic executor's (ref). loss and m within tol of their largest
+// magnitude, v within 2 tol, t exact; parameters by the bound an AdamW step
+// allows: p' - p = -lr (wd p + m_hat / (sqrt(v_hat) + eps)), whose Adam part is
+// close to lr * sign(g) where v_hat is dominated by g^2, so wherever a gradient
+// lies within its own rounding of zero the two results may differ by up to
+// 2 lr. Every parameter within 3 lr (plus two ulps of the element type), and
+// at most 2% of them beyond 1% of lr.
+sb_status train_outputs_agree(const std::vector<Buffer*>& fast, const std::vector<Buffer*>& ref, size_t first,
+                              size_t n, double lr, double tol, bool* agree, std::string* why, double* worst) {
+  *agree = fast.size() == ref.size() && ref.size() == first + 3 * n + 2;
+  *worst = 0;
+  if (!*agree) {
+    *why = "output count";
+    return nullptr;
+  }
+  size_t flips = 0, total = 0;
+  for (size_t i = 0; i < ref.size() && *agree; ++i) {
+    std::vector<double> a, b;
+    SB_TRY(host_values(fast[i], &a));
+    SB_TRY(host_values(ref[i], &b));
+    if (a.size() != b.size()) {
+      *agree = false;
+      *why = "output " + std::to_string(i) + ": size";
+      break;
+    }
+    const size_t j = i - first;  // position in [loss | m | p | t | v]
+    if (i < first) {  // the key leaf: passed through
+      for (size_t k = 0; k < a.size() && *agree; ++k) *agree = a[k] == b[k];
+      if (!*agree) *why = "key leaf";
+      continue;
+    }
+    const bool is_p = j >= 1 + n && j < 1 + 2 * n;
+    const bool is_t = j == 1 + 2 * n;
+    const bool is_v = j > 1 + 2 * n;
+    const bool bf = ref[i]->elem == SB_ELEM_BF16;
+    double mx = 0, err = 0;
+    for (size_t k = 0; k < a.size(); ++k) {
+      if (!std::isfinite(a[k])) {
+        *agree = false;
+        *why = "output " + std::to_string(i) + ": non-finite";
+        break;
+      }
+      const double d = std::fabs(a[k] - b[k]);
+      mx = std::max(mx, std::fabs(b[k]));
+      err = std::max(err, d);
+      if (is_p) {
+        const double slack = std::fabs(b[k]) * (bf ? 1.0 / 128 : 1e-6);
+        if (d > 3.0 * lr + slack) {
+          *agree = false;
+          *why = "parameter output " + std::to_string(i) + ": moved " + std::to_string(d) + " from the reference";
+          break;
+        }
+        if (d > 1e-2 * lr + slack) ++flips;
+        ++total;
+      }
+    }
+    if (!*agree) break;
+    if (is_t) {
+      *agree = err == 0;
+      if (!*agree) *why = "t differs";
+    } else if (!is_p) {
+      const double lim = (is_v ? 2 : 1) * tol;
+      *worst = std::max(*worst, err / std::max(mx, 1e-30));
+      if (err > lim * mx) {
+        *agree = false;
+        *why = "output " + std::to_string(i) + ": max error " + std::to_string(err) + " vs max |ref| " +
+               std::to_string(mx);
+      }
+    }
+  }
+  if (*agree && flips > total / 50) {
+    *agree = false;
+    *why = std::to_string(flips) + " of " + std::to_string(total) + " parameters differ by more than 1% of lr";
+  }
+  return nullptr;
+}
+
 // ---------------------------------------------------------------------------
 // Plan cache (manifest of first-call verification outcomes)
 // ---------------------------------------------------------------------------
@@ -1822,9 +1921,20 @@ class StableHloModule : public Module {
       return nullptr;
     }
     double worst = 0;
-    sb_status ce = cudaStreamSynchronize(s.stream) == cudaSuccess
-                       ? outputs_agree(fast, ref, verify_tolerance(f.generic->f.args[0].dt), agree, why, &worst)
-                       : make_status(SB_STATUS_INTERNAL, "stream synchronize failed");
+    sb_status ce = nullptr;
+    if (cudaStreamSynchronize(s.stream) != cudaSuccess) {
+      ce = make_status(SB_STATUS_INTERNAL, "stream synchronize failed");
+    } else if (f.train) {
+      const size_t first = f.has_key ? 1 : 0;
+      const size_t n = (in.size() - first - 5) / 3;
+      std::vector<double> lr;
+      ce = host_values(in.back(), &lr);
+      if (!ce)
+        ce = train_outputs_agree(fast, ref, first, n, lr.empty() ? 0.0 : std::fabs(lr[0]),
+                                 verify_tolerance(f.generic->f.args[first].dt), agree, why, &worst);
+    } else {
+      ce = outputs_agree(fast, ref, verify_tolerance(f.generic->f.args[0].dt), agree, why, &worst);
+    }
     if (ce) {
       *agree = false;
       *why = sb_status_message(ce);
