@@ -151,9 +151,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
   tc_fence_after();
   pdl_trigger();
   const uint32_t tmem = *tmem_slot;
-  // O_j = P V is accumulated in two halves (even / odd 16-key steps) so that
-  // the two dependent UMMA chains run interleaved; the softmax warps add them
-  const uint32_t tS = tmem, tO = tmem + 128, tO2 = tmem + 192;
+  const uint32_t tS = tmem, tO = tmem + 128;
 
   if (warp == 0) {
     // K_c is reloaded once S_{c-1} has consumed the single K slot, V_c once
@@ -226,8 +224,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
           }
           tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_f16((kk & 1) ? tO2 : tO, kdesc2(p_addr, kk), mndesc(v_addr, kk, 8192), idO, kk > 1);
+          for (int kk = 0; kk < 8; ++kk) umma_f16(tO, kdesc2(p_addr, kk), mndesc(v_addr, kk, 8192), idO, kk > 0);
           umma_commit(o_full);
           umma_commit(v_empty);
         }
@@ -318,16 +315,13 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
         tc_fence_after();
         uint32_t v0[32], v1[32];
         tmem_ld32(tO + lane_base, v0);
-        tmem_ld32(tO2 + lane_base, v1);
+        tmem_ld32(tO + lane_base + 32, v1);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = o[i] * corr + (__uint_as_float(v0[i]) + __uint_as_float(v1[i]));
-        tmem_ld32(tO + lane_base + 32, v0);
-        tmem_ld32(tO2 + lane_base + 32, v1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          o[32 + i] = o[32 + i] * corr + (__uint_as_float(v0[i]) + __uint_as_float(v1[i]));
+        for (int i = 0; i < 32; ++i) {
+          o[i] = o[i] * corr + __uint_as_float(v0[i]);
+          o[32 + i] = o[32 + i] * corr + __uint_as_float(v1[i]);
+        }
         tc_fence_before();
       }
       if (ok) {
@@ -531,13 +525,10 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
           const uint32_t q_addr = smem_u32(sQ + s * kTileBytes), do_addr = smem_u32(sdO + s * kTileBytes);
           // S^T, dP^T overwrite what the softmax warps read for tile g-1
           // (they arrived on p_full(g-1) before this point)
-          // the two independent accumulator chains interleaved, so that one's
-          // UMMA runs while the other's previous one completes
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            umma_f16(tST, kdesc(k_addr, kk), kdesc(q_addr, kk), idS, kk > 0);
-            umma_f16(tdPT, kdesc(v_addr, kk), kdesc(do_addr, kk), idS, kk > 0);
-          }
+          for (int kk = 0; kk < 4; ++kk) umma_f16(tST, kdesc(k_addr, kk), kdesc(q_addr, kk), idS, kk > 0);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) umma_f16(tdPT, kdesc(v_addr, kk), kdesc(do_addr, kk), idS, kk > 0);
           umma_commit(st_full);
           if (!mbar_wait(p_full, g & 1, a.err, abort_flag)) {
             ok = false;
@@ -551,8 +542,12 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
             }
             tc_fence_after();
           }
-          // dQ(g-1) has been read out by now in practice (the softmax warps do
-          // it before they work on tile g); the wait only guards the order
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tdV, kdesc2(pt_addr, kk), mndesc(do_addr, kk, 8192), idKV, (it > 0 || kk > 0));
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tdK, kdesc2(dst_addr, kk), mndesc(q_addr, kk, 8192), idKV, (it > 0 || kk > 0));
           if (g > 0) {
             if (!mbar_wait(dq_empty, (g - 1) & 1, a.err, abort_flag)) {
               ok = false;
@@ -560,13 +555,9 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
             }
             tc_fence_after();
           }
-          // dV, dK and dQ: three independent accumulator chains, interleaved
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            umma_f16(tdV, kdesc2(pt_addr, kk), mndesc(do_addr, kk, 8192), idKV, (it > 0 || kk > 0));
-            umma_f16(tdK, kdesc2(dst_addr, kk), mndesc(q_addr, kk, 8192), idKV, (it > 0 || kk > 0));
+          for (int kk = 0; kk < 8; ++kk)
             umma_f16(tdQ, mndesc(dst_addr, kk, 16384), mndesc(k_addr, kk, 8192), idQ, kk > 0);
-          }
           umma_commit(dq_full);
           umma_commit(&qd_empty[s]);
         }
