@@ -115,6 +115,8 @@ class GptVagModule : public Module {
   int* step_ctr = nullptr;
   float* step_logits = nullptr;
   size_t gen_tok = 0, gen_ids = 0, gen_keys = 0, gen_logits = 0, gen_bytes = 0;
+  void* sample_ws = nullptr;  // the long-vocabulary sort's scratch
+  size_t sample_ws_bytes = 0;
 
   // one captured graph per function (value_and_grad, train_step, one token
   // of generate), its kernel nodes and the eager runs before the capture
@@ -389,7 +391,8 @@ class GptVagModule : public Module {
     if (smp) {
       SB_RETURN_IF(smp->n_new <= 0 || smp->top_k <= 0 || !(smp->temperature > 0.f), SB_STATUS_INVALID_ARGUMENT,
                    "sampler: n_new and top_k must be positive, temperature > 0");
-      SB_RETURN_IF(V > kSampleMaxVocab, SB_STATUS_UNIMPLEMENTED, "sampler: vocabulary larger than the on-device sort");
+      SB_RETURN_IF(V > kSampleMaxVocab || (V > kSampleSmemVocab && T > 4096), SB_STATUS_UNIMPLEMENTED,
+                   "sampler: vocabulary or window beyond the on-device sort");
       sampler = true;
       n_new = smp->n_new;
       top_k = smp->top_k;
@@ -398,6 +401,8 @@ class GptVagModule : public Module {
       SB_TRY(devt(static_cast<size_t>(B) * n_new, &tokens_buf));
       SB_TRY(devt(64, &step_ctr));
       SB_TRY(devt(static_cast<size_t>(n_new) * B * V, &step_logits));
+      sample_ws_bytes = sample_workspace_bytes(B, V);
+      if (sample_ws_bytes) SB_TRY(dev(sample_ws_bytes, &sample_ws));
       // outputs of generate: tokens | ids | keys | step logits (all f32)
       gen_tok = 0;
       gen_ids = align256(gen_tok + static_cast<size_t>(B) * n_new * 4);
@@ -465,7 +470,7 @@ class GptVagModule : public Module {
     SB_K(gemm(desc(hf, D, false, Pp(0), D, false, N, V, D, logits, ldl, f32), st, err));
     if (mode == kSample) {
       SB_K(sample_step(logits, f32, ldl, B, T, V, top_k, temperature, ids, keys_buf, tokens_buf, n_new, step_ctr,
-                       step_logits, st));
+                       step_logits, sample_ws, sample_ws_bytes, st));
       return nullptr;
     }
     SB_K(cross_entropy_fwd_bwd(logits, f32, ldl, N, V, ids + N, dlogits, ldl, ws, loss_f32, nullptr, st));

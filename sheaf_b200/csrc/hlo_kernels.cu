@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(512) sort_rows_kernel(const void* keys, int ke
       static_cast<__nv_bfloat16*>(out_keys)[dst] = static_cast<const __nv_bfloat16*>(keys)[src];
     else
       static_cast<float*>(out_keys)[dst] = static_cast<const float*>(keys)[src];
-    out_payload[dst] = payload[src];
+    out_payload[dst] = payload ? payload[src] : p;  // no payload: the source positions
   }
 }
 
@@ -535,7 +535,7 @@ __global__ void sort_gather_kernel(const uint64_t* sorted, int npad, const void*
        e += static_cast<long>(gridDim.x) * blockDim.x) {
     const long row = e / n, i = e % n;
     const long src = row * n + static_cast<uint32_t>(sorted[row * npad + i]);
-    out_payload[e] = payload[src];
+    out_payload[e] = payload ? payload[src] : static_cast<int32_t>(src - row * n);
     const char* kp = static_cast<const char*>(keys) + src * es;
     char* op = static_cast<char*>(out_keys) + e * es;
     for (int b = 0; b < es; ++b) op[b] = kp[b];

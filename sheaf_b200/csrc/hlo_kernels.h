@@ -70,6 +70,10 @@ int dynamic_update(void* out, const void* upd, int dt, const DynSlice& d, cudaSt
 // Stable sort of `rows` rows of n keys (f32 or bf16) along the last axis,
 // carrying an i32 payload: descending for a GT comparator, ascending for LT;
 // equal keys keep their input order.
+// Stable sort of each of `rows` rows of n keys (descending or ascending),
+// the payload permuted alike (payload null: out_payload receives the source
+// positions). Rows longer than kSortSmemRow need sort_rows_workspace_bytes
+// of scratch in `ws`.
 size_t sort_rows_workspace_bytes(long rows, int n);
 int sort_rows(const void* keys, int key_dt, const int32_t* payload, void* out_keys, int32_t* out_payload, long rows,
               int n, bool descending, void* ws, size_t ws_bytes, cudaStream_t s);

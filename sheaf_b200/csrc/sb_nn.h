@@ -75,10 +75,15 @@ int random_split(const float* key, int n, float* out, cudaStream_t s);
 // (row b*T + T-1, row stride ld), writes tokens[b * n_new + *step], advances
 // each sequence's key [B, 4] and its id window [B, T] in place, records the
 // raw last-position logits in step_logits [n_new, B, V] (optional) and
-// increments *step.
-constexpr int kSampleMaxVocab = 4096;
+// increments *step. Vocabularies up to kSampleSmemVocab sort in one CTA's
+// shared memory and need no workspace; larger ones (window T <= 4096) take
+// sample_workspace_bytes(B, V) of scratch.
+constexpr int kSampleSmemVocab = 4096;
+constexpr int kSampleMaxVocab = 1 << 24;
+size_t sample_workspace_bytes(int B, int V);
 int sample_step(const void* logits, bool logits_f32, long ld, int B, int T, int V, int top_k, float temperature,
-                float* ids, float* keys, float* tokens, int n_new, int* step, float* step_logits, cudaStream_t s);
+                float* ids, float* keys, float* tokens, int n_new, int* step, float* step_logits, void* ws,
+                size_t ws_bytes, cudaStream_t s);
 
 // Global gradient norm, and with `params` the clip-by-global-norm + AdamW
 // step of nanoGPT's train-step over n_leaves tensors of one element type
