@@ -521,6 +521,62 @@ def sweep_ops(only: str | None = None, reps: int = 10):
             tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
             emit({"op": name, "ms": ms, "achieved": tf, "unit": "TFLOP/s", "bound": "tensor + output bytes",
                   "frac_of_bf16_peak": tf / tc_burst, "out_bytes": 2 * M * N * g.element_size()})
+        name = f"gemm_{kind}_step_dw_fc"  # the step's fc weight gradient: dU^T [1536, 16384] x h2 [16384, 384]
+        if want(name):
+            M, N, K = 4 * CFG["n_embd"], CFG["n_embd"], CFG["batch"] * CFG["seq"]
+            du = torch.randn(K, M, device=dev).to(dt)
+            h2 = torch.randn(K, N, device=dev).to(dt)
+            c = torch.empty(M, N, device=dev, dtype=dt)
+            wsb = L.sb_op_matmul_workspace_size(elem, 1, 0, M, N, K)
+            ws = torch.empty(max(wsb // 4, 1), device=dev)
+            fn = lambda: L.sb_op_matmul(elem, du.data_ptr(), M, 1, h2.data_ptr(), N, 0, M, N, K, c.data_ptr(), N,  # noqa
+                                        elem, ws.data_ptr(), wsb, st())
+            ms = _time_op(fn, reps, flush)
+            tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+            emit({"op": name, "ms": ms, "achieved": tf, "unit": "TFLOP/s", "bound": "tensor" if kind == "bf16" else
+                  "fp32 FFMA", "frac_of_bf16_peak": tf / tc_burst})
+        es_ = 2 if kind == "bf16" else 4
+        for R, V in ((CFG["batch"] * CFG["seq"], CFG["vocab_size"]), (8192, 50304)):
+            name = f"cross_entropy_{kind}_{R}x{V}"
+            if not want(name):
+                continue
+            ldv = (V + 7) // 8 * 8
+            lg = torch.randn(R, ldv, device=dev).to(dt)
+            dl = torch.empty(R, ldv, device=dev, dtype=dt)
+            tg = torch.randint(0, V, (R,), device=dev).float()
+            loss = torch.zeros(1, device=dev)
+            wsb = L.sb_op_cross_entropy_workspace_size(R)
+            ws = torch.empty(wsb // 4 + 1, device=dev)
+            ms = _time_op(lambda: L.sb_op_cross_entropy(elem, lg.data_ptr(), ldv, R, V, tg.data_ptr(), dl.data_ptr(),  # noqa
+                                                        ldv, ws.data_ptr(), wsb, loss.data_ptr(), st()), reps, flush)
+            b = 2 * R * V * es_ + 4 * R
+            emit({"op": name, "ms": ms, "achieved": b / (ms / 1e3) / 1e9, "unit": "GB/s", "bound": "hbm", "peak": hbm,
+                  "frac": b / (ms / 1e3) / 1e9 / hbm})
+        for Bt, T, P, V, D in ((CFG["batch"], CFG["seq"], CFG["block_size"], CFG["vocab_size"], CFG["n_embd"]),
+                               (8, 1024, 1024, 50304, 768)):
+            name = f"embedding_{kind}_{Bt * T}x{V}x{D}"
+            if not want(name):
+                continue
+            ids = torch.randint(0, V, (Bt * T,), device=dev).float()
+            wte = torch.randn(V, D, device=dev).to(dt)
+            wpe = torch.randn(P, D, device=dev).to(dt)
+            x = torch.empty(Bt * T, D, device=dev)
+            dx = torch.randn(Bt * T, D, device=dev)
+            dwte = torch.empty(V, D, device=dev, dtype=dt)
+            dwpe = torch.empty(P, D, device=dev, dtype=dt)
+            wsb = L.sb_op_embedding_bwd_workspace_size(V, D)
+            ws = torch.empty(wsb // 4 + 1, device=dev)
+            mf = _time_op(lambda: L.sb_op_embedding_fwd(elem, ids.data_ptr(), wte.data_ptr(), wpe.data_ptr(),  # noqa
+                                                        x.data_ptr(), Bt * T, T, V, D, st()), reps, flush)
+            mb = _time_op(lambda: L.sb_op_embedding_bwd(elem, ids.data_ptr(), dx.data_ptr(), Bt, T, P, V, D,  # noqa
+                                                        dwte.data_ptr(), dwpe.data_ptr(), ws.data_ptr(), wsb, st()),
+                          reps, flush)
+            # gather: ids + rows read (wte, wpe) + f32 rows written; VJP: f32 rows read + both tables written
+            bf_ = Bt * T * (4 + 2 * D * es_ + 4 * D)
+            bb_ = Bt * T * (4 + 4 * D) + (V + P) * D * es_
+            emit({"op": name, "fwd_ms": mf, "vjp_ms": mb, "achieved_fwd": bf_ / (mf / 1e3) / 1e9,
+                  "achieved_vjp": bb_ / (mb / 1e3) / 1e9, "unit": "GB/s", "bound": "hbm", "peak": hbm,
+                  "frac_fwd": bf_ / (mf / 1e3) / 1e9 / hbm, "frac_vjp": bb_ / (mb / 1e3) / 1e9 / hbm})
         for B, T, H, Hd in ((16, 1024, 12, 64), (CFG["batch"], CFG["seq"], CFG["n_head"], CFG["n_embd"] // CFG["n_head"])):
             name = f"attention_{kind}_{B}x{H}x{T}x{Hd}"
             if not want(name):
