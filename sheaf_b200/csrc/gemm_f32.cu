@@ -196,12 +196,15 @@ F32Plan f32_plan(const GemmDesc& d) {
 
 size_t gemm_f32_workspace_bytes(const GemmDesc& d) {
   F32Plan p = f32_plan(d);
-  if (p.splits <= 1) return 0;
-  return static_cast<size_t>(p.splits) * d.M * d.N * sizeof(float);
+  const size_t ffma = p.splits <= 1 ? 0 : static_cast<size_t>(p.splits) * d.M * d.N * sizeof(float);
+  // enough for either path: the choice also depends on the output's alignment
+  return gemm_f32_use_emulation(d) ? std::max(ffma, gemm_f32_emulated_workspace_bytes(d)) : ffma;
 }
 
-int gemm_f32(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* /*err*/) {
+int gemm_f32(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* err) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0) return 1;
+  if (gemm_f32_use_emulation(d) && workspace && workspace_bytes >= gemm_f32_emulated_workspace_bytes(d))
+    return gemm_f32_emulated(d, workspace, workspace_bytes, s, err);
   F32Plan p = f32_plan(d);
   F32Args a{};
   a.A = static_cast<const float*>(d.A);

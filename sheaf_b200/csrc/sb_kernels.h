@@ -44,8 +44,13 @@ struct GemmDesc {
 // bf16 operands on tcgen05 tensor cores (fp32 accumulation in TMEM).
 // `workspace` (fp32) is used for split-K partial sums; returns 0 on success.
 int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* err);
-// fp32 operands on the CUDA cores (exact fp32 FFMA accumulation).
+// fp32 operands: on the tensor cores by the bf16x6 split (one bf16 GEMM over
+// K' = 6K with f32 accumulation, gemm_emul.cu) when the problem is large and
+// the workspace holds the split copies, else on the CUDA cores (FFMA).
 int gemm_f32(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* err);
+bool gemm_f32_use_emulation(const GemmDesc& d);
+size_t gemm_f32_emulated_workspace_bytes(const GemmDesc& d);
+int gemm_f32_emulated(const GemmDesc& d, void* workspace, size_t workspace_bytes, cudaStream_t s, int* err);
 // Bytes of split-K workspace gemm_* would use for this problem (0 if none).
 size_t gemm_workspace_bytes(const GemmDesc& d, bool bf16);
 size_t gemm_f32_workspace_bytes(const GemmDesc& d);
