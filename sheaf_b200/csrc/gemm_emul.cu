@@ -12,10 +12,20 @@
 // accumulation of the 6 K exact terms -- the 1e-5 parity bar of the fp32
 // path holds, as for the CUDA-core FFMA GEMM it replaces on large shapes.
 //
+// The tensor cores' own accumulation of a long chain loses low-order bits
+// (measured on this part: 7e-7 of the largest output at K' = 2304, 1.8e-5 at
+// K' = 9216-12288, against 2e-6 for the FFMA kernel); as Ootomo and Yokota
+// ("Recovering single precision accuracy from Tensor Cores while surpassing
+// the FP32 theoretical peak performance", IJHPCA 2022) do, the chains are kept
+// short and their partial sums added in round-to-nearest f32 on the CUDA
+// cores: the product always runs split-K with at most kSplitK terms of K' per
+// split, the splits summed by the split-K reduction.
+//
 // The split copies keep the operand's storage order (K-major [rows, K] ->
 // [rows, 6K]; MN-major [K, cols] -> [6K, cols]), so the bf16 kernel reads them
-// exactly as it would read the f32 operand. The GELU and multiply epilogues
-// run as one f32 elementwise pass after the product (the bf16 kernel's own
+// exactly as it would read the f32 operand. Epilogues other than a plain store
+// (GELU, multiply, add, accumulate) run as one f32 elementwise pass after the
+// product, which split-K leaves in an f32 temporary (the bf16 kernel's own
 // GELU epilogue rounds u to bf16 first, which the fp32 module does not).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -66,6 +76,8 @@ __global__ void split6_kernel(const float* __restrict__ x, long rows, long cols,
   }
 }
 
+constexpr int kSplitK = 1536;
+
 __device__ __forceinline__ float gelu_f32(float x) {
   const float inner = x + 0.044715f * (x * (x * x));
   return 0.5f * (x * (1.0f + tanhf(0.7978846f * inner)));
@@ -76,7 +88,8 @@ __device__ __forceinline__ float gelu_df32(float x) {
   return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * 0.7978846f * (1.0f + 0.134145f * x2);
 }
 
-// u [M, N] (row stride N) -> out = gelu(u), out2 = gelu'(u); or out = u * aux.
+// u [M, N] (row stride N) -> out = gelu(u), out2 = gelu'(u); out = u * aux;
+// out = u + aux; or out += u.
 __global__ void epilogue_f32_kernel(const float* __restrict__ u, long M, long N, int epi, float* __restrict__ out,
                                     long ldo, float* __restrict__ out2, long ldo2, const float* __restrict__ aux,
                                     long ldaux) {
@@ -88,8 +101,12 @@ __global__ void epilogue_f32_kernel(const float* __restrict__ u, long M, long N,
     if (epi == EPI_GELU) {
       out[r * ldo + c] = gelu_f32(v);
       out2[r * ldo2 + c] = gelu_df32(v);
-    } else {
+    } else if (epi == EPI_MUL) {
       out[r * ldo + c] = v * aux[r * ldaux + c];
+    } else if (epi == EPI_ADD) {
+      out[r * ldo + c] = v + aux[r * ldaux + c];
+    } else {  // EPI_ACCUM
+      out[r * ldo + c] += v;
     }
   }
 }
@@ -102,18 +119,22 @@ int blocks_for(long n) {
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // The bf16 GEMM over the split copies (operands filled in by the caller).
+bool needs_tmp(const GemmDesc& d) { return d.epi != EPI_STORE; }
+
 GemmDesc split_desc(const GemmDesc& d) {
   GemmDesc e = d;
   e.K = 6 * d.K;
   e.lda = d.a_mn ? d.M : 6L * d.K;
   e.ldb = d.b_mn ? d.N : 6L * d.K;
-  if (d.epi == EPI_GELU || d.epi == EPI_MUL) {  // product into an f32 temporary first
+  if (needs_tmp(d)) {  // product into an f32 temporary first
     e.epi = EPI_STORE;
     e.ldo = d.N;
     e.aux = nullptr;
     e.out2 = nullptr;
   }
   e.out_f32 = true;
+  e.splits = std::max(2, (e.K + kSplitK - 1) / kSplitK);
+  e.max_splits = 0;
   return e;
 }
 
@@ -128,10 +149,10 @@ bool gemm_f32_use_emulation(const GemmDesc& d) {
   }();
   if (ffma) return false;
   const double work = static_cast<double>(d.M) * d.N * d.K;
-  const bool gelu_mul = d.epi == EPI_GELU || d.epi == EPI_MUL;
-  // the f32 output (or the temporary) is written by TMA: 16-byte rows
-  const bool tma_out = gelu_mul ? (d.N % 4) == 0
-                                : ((d.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(d.out) & 15) == 0);
+  // split-K partial rows (and the f32 output of a plain store, written by
+  // TMA) must be 16-byte multiples
+  const bool tma_out = (d.N % 4) == 0 && (needs_tmp(d) ||
+                                          ((d.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(d.out) & 15) == 0));
   // the bf16 split copies' rows must be 16-byte multiples too: 6K bf16 for a
   // K-major copy, M (or N) bf16 for an MN-major one
   const bool a_ok = d.a_mn ? (d.M % 8) == 0 : (d.K % 4) == 0;
@@ -142,7 +163,7 @@ bool gemm_f32_use_emulation(const GemmDesc& d) {
 size_t gemm_f32_emulated_workspace_bytes(const GemmDesc& d) {
   const size_t a = up256(6 * static_cast<size_t>(d.M) * d.K * 2);
   const size_t b = up256(6 * static_cast<size_t>(d.N) * d.K * 2);
-  const size_t t = (d.epi == EPI_GELU || d.epi == EPI_MUL) ? up256(static_cast<size_t>(d.M) * d.N * 4) : 0;
+  const size_t t = needs_tmp(d) ? up256(static_cast<size_t>(d.M) * d.N * 4) : 0;
   return a + b + t + gemm_workspace_bytes(split_desc(d), true);
 }
 
@@ -154,7 +175,7 @@ int gemm_f32_emulated(const GemmDesc& d, void* workspace, size_t workspace_bytes
   __nv_bfloat16* b6 = reinterpret_cast<__nv_bfloat16*>(w);
   w += up256(6 * static_cast<size_t>(d.N) * d.K * 2);
   float* tmp = nullptr;
-  if (d.epi == EPI_GELU || d.epi == EPI_MUL) {
+  if (needs_tmp(d)) {
     tmp = reinterpret_cast<float*>(w);
     w += up256(static_cast<size_t>(d.M) * d.N * 4);
   }
