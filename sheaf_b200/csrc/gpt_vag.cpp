@@ -90,6 +90,7 @@ class GptVagModule : public Module {
   void* dres_bf = nullptr;
   void* dh = nullptr;  // dy of the layer-norm VJPs, model element type (as the module materialises it)
   void *du = nullptr, *dout = nullptr, *dqkv = nullptr;
+  __nv_bfloat16* onehot = nullptr;  // bf16 one-hot [N, ldl] of the x ids (small vocabularies, bf16 plan)
   float* ws = nullptr;
   size_t ws_bytes = 0;
 
@@ -337,6 +338,11 @@ class GptVagModule : public Module {
     SB_TRY(dev(4 * nd * es, &du));
     SB_TRY(dev(nd * es, &dout));
     SB_TRY(dev(3 * nd * es, &dqkv));
+    if (bf && V <= 256) {
+      void* oh = nullptr;
+      SB_TRY(dev(static_cast<size_t>(N) * ldl * 2, &oh));
+      onehot = static_cast<__nv_bfloat16*>(oh);
+    }
 
     size_t w = 0;
     for (auto& d : all_gemms()) w = std::max(w, gemm_workspace_bytes(d, bf));
@@ -564,7 +570,16 @@ class GptVagModule : public Module {
       SB_CUDA_TRY(cudaEventRecord(e, wst));
       SB_CUDA_TRY(cudaStreamWaitEvent(st, e, 0));
     }
-    SB_K(embedding_bwd(ids, dres, B, T, P, V, D, Gp(iw), Gp(ip), f32, ws, st));
+    if (onehot) {
+      // the reference's one-hot matmul (reverse.rs:1108-1121) on the tensor
+      // cores: dwte = one_hot(x)^T [V, N] x dres (bf16 copy) [N, D], the
+      // shape of the head's weight gradient
+      SB_K(embedding_onehot(ids, N, V, ldl, onehot, st));
+      SB_K(gemm(desc(onehot, ldl, true, r0, D, true, V, D, N, Gp(iw), D, false), st, err));
+      SB_K(embedding_pos_bwd(dres, B, T, P, D, Gp(ip), false, st));
+    } else {
+      SB_K(embedding_bwd(ids, dres, B, T, P, V, D, Gp(iw), Gp(ip), f32, ws, st));
+    }
     SB_TRY(launch_bucket(offs[ip], grads_bytes, nullptr));
     if (dp) {
       SB_TRY(comm_allreduce_avg(s, loss_f32, 1, SB_ELEM_F32, s.comm_stream));

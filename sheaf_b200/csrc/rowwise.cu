@@ -746,6 +746,22 @@ __global__ void embed_bwd_atomic_kernel(const float* __restrict__ ids, const flo
   }
 }
 
+// one_hot(ids, V) as the reference's embedding VJP builds it (compare of the
+// f32 id with an f32 iota, tensor_ops.rs:163-217), bf16 [ntok, Vp]; columns
+// V..Vp-1 are zero. Its transpose times the token gradients is dwte
+// (reverse.rs:1108-1121).
+__global__ void onehot_kernel(const float* __restrict__ ids, int ntok, int V, int Vp, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const long total = static_cast<long>(ntok) * Vp;
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const long n = i / Vp;
+    const int v = static_cast<int>(i % Vp);
+    out[i] = __float2bfloat16_rn(one_hot_class(ids[n], V) == v ? 1.f : 0.f);
+  }
+}
+
 // dwpe[t, :] = sum_b dx[b*T + t, :] for t < T; rows T..P-1 are zero (pad).
 __global__ void embed_bwd_pos_kernel(const float* __restrict__ dx, int B, int T, int P, int D, void* dwpe,
                                      int out_f32) {
@@ -756,8 +772,18 @@ __global__ void embed_bwd_pos_kernel(const float* __restrict__ dx, int B, int T,
        i += static_cast<long>(gridDim.x) * blockDim.x) {
     const long t = i / D, c = i % D;
     float acc = 0.f;
-    if (t < T)
-      for (int b = 0; b < B; ++b) acc += dx[(static_cast<long>(b) * T + t) * D + c];
+    if (t < T) {
+      // eight rows' loads in flight, summed in batch order
+      int b = 0;
+      for (; b + 8 <= B; b += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = dx[(static_cast<long>(b + u) * T + t) * D + c];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc += v[u];
+      }
+      for (; b < B; ++b) acc += dx[(static_cast<long>(b) * T + t) * D + c];
+    }
     if (out_f32)
       static_cast<float*>(dwpe)[i] = acc;
     else
@@ -1092,6 +1118,19 @@ int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V,
     }
   }
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
+  const long total = static_cast<long>(P) * D;
+  launch_pdl(embed_bwd_pos_kernel, dim3(grid_for(total, 256)), dim3(256), 0, s, dx, B, T, P, D, dwpe, out_f32);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+int embedding_onehot(const float* ids, int ntok, int V, int Vp, __nv_bfloat16* out, cudaStream_t s) {
+  if (ntok <= 0 || V <= 0 || Vp < V) return 1;
+  const long n = static_cast<long>(ntok) * Vp;
+  launch_pdl(onehot_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, ids, ntok, V, Vp, out);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+
+int embedding_pos_bwd(const float* dx, int B, int T, int P, int D, void* dwpe, bool out_f32, cudaStream_t s) {
   const long total = static_cast<long>(P) * D;
   launch_pdl(embed_bwd_pos_kernel, dim3(grid_for(total, 256)), dim3(256), 0, s, dx, B, T, P, D, dwpe, out_f32);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;

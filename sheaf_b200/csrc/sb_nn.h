@@ -46,6 +46,13 @@ size_t embedding_bwd_workspace_bytes(int V, int D);
 int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V, int D, void* dwte, void* dwpe,
                   bool out_f32, float* ws, cudaStream_t s);
 
+// The embedding VJP in two parts, for a plan that computes dwte itself as
+// one_hot(ids)^T dx on the tensor cores: the bf16 one-hot [ntok, Vp] (columns
+// >= V zero; an id that is not exactly an integer in [0, V) has no class)
+// and dwpe alone.
+int embedding_onehot(const float* ids, int ntok, int V, int Vp, __nv_bfloat16* out, cudaStream_t s);
+int embedding_pos_bwd(const float* dx, int B, int T, int P, int D, void* dwpe, bool out_f32, cudaStream_t s);
+
 int convert_f32_to_bf16(const float* in, __nv_bfloat16* out, long n, cudaStream_t s);
 // y = gelu(x) or, with bwd, y = g * gelu'(x), elementwise over n values.
 int gelu(const void* x, const void* g, void* y, bool f32, bool bwd, long n, cudaStream_t s);
