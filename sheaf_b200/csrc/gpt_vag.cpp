@@ -171,7 +171,30 @@ class GptVagModule : public Module {
     return fn == "value_and_grad" || (train && fn == "train_step") || (sampler && fn == "generate");
   }
 
-  void* Pp(int i) const { return params + offs[i]; }
+  // Parameter pointers the kernels read: the plan-owned slots, or (for
+  // value_and_grad on resident, 256-byte-aligned parameter buffers) the input
+  // buffers themselves, read in place as the reference's DeviceBuffer inputs
+  // are (iree_session.rs:505-519). A captured graph records the pointer set it
+  // was captured with and is recaptured when a call brings another one.
+  std::vector<void*> pin;
+  std::vector<void*> exec_pin[kModes];
+  void* Pp(int i) const { return pin[i]; }
+  void* slot(int i) const { return params + offs[i]; }
+  // Points the plan at `ptrs` for the next run of `mode`.
+  sb_status use_params(const std::vector<void*>& ptrs, Mode mode, cudaStream_t st) {
+    pin = ptrs;
+    if (exec[mode] && exec_pin[mode] != pin) {
+      SB_CUDA_TRY(cudaStreamSynchronize(st));
+      cudaGraphExecDestroy(exec[mode]);
+      exec[mode] = nullptr;
+    }
+    return nullptr;
+  }
+  std::vector<void*> slots() const {
+    std::vector<void*> v(shapes.size());
+    for (size_t i = 0; i < shapes.size(); ++i) v[i] = slot(static_cast<int>(i));
+    return v;
+  }
   void* Gp(int i) const { return grads + offs[i]; }
 
   sb_status dev(size_t bytes, void** p) {
@@ -290,6 +313,7 @@ class GptVagModule : public Module {
     void* v;
     SB_TRY(dev(grads_bytes, &v));
     params = static_cast<char*>(v);
+    pin = slots();
     SB_TRY(dev(out_bytes, &v));
     grads = static_cast<char*>(v);
     cudaMemset(grads, 0, out_bytes);
@@ -698,8 +722,16 @@ class GptVagModule : public Module {
   }
 
   sb_status copy_in(Session& s, const std::vector<Buffer*>& in, cudaStream_t st) {
+    std::vector<void*> direct(shapes.size());
+    bool aligned = true;
+    for (size_t i = 0; i < shapes.size(); ++i) {
+      direct[i] = in[i]->data();
+      aligned = aligned && (reinterpret_cast<uintptr_t>(direct[i]) & 255) == 0;
+    }
+    SB_TRY(use_params(aligned ? direct : slots(), kVag, st));
     std::vector<Seg> segs;
-    for (size_t i = 0; i < shapes.size(); ++i) segs.push_back({in[i]->data(), {Pp(static_cast<int>(i)), in[i]->bytes()}});
+    if (!aligned)
+      for (size_t i = 0; i < shapes.size(); ++i) segs.push_back({in[i]->data(), {slot(static_cast<int>(i)), in[i]->bytes()}});
     segs.push_back({in[shapes.size()]->data(), {ids, static_cast<size_t>(N) * 4}});
     segs.push_back({in[shapes.size() + 1]->data(), {ids + N, static_cast<size_t>(N) * 4}});
     return copy_segs(s, segs, st);
@@ -707,10 +739,11 @@ class GptVagModule : public Module {
 
   sb_status copy_in_train(Session& s, const std::vector<Buffer*>& in, cudaStream_t st) {
     const size_t n = shapes.size();
+    SB_TRY(use_params(slots(), kTrain, st));
     std::vector<Seg> segs;
     for (size_t i = 0; i < n; ++i) {
       segs.push_back({in[1 + i]->data(), {mbuf + offs[i], in[1 + i]->bytes()}});
-      segs.push_back({in[1 + n + i]->data(), {Pp(static_cast<int>(i)), in[1 + n + i]->bytes()}});
+      segs.push_back({in[1 + n + i]->data(), {slot(static_cast<int>(i)), in[1 + n + i]->bytes()}});
       segs.push_back({in[2 + 2 * n + i]->data(), {vbuf + offs[i], in[2 + 2 * n + i]->bytes()}});
     }
     segs.push_back({in[1 + 2 * n]->data(), {tl, 4}});
@@ -722,8 +755,9 @@ class GptVagModule : public Module {
 
   sb_status copy_in_gen(Session& s, const std::vector<Buffer*>& in, cudaStream_t st) {
     const size_t n = shapes.size();
+    SB_TRY(use_params(slots(), kSample, st));
     std::vector<Seg> segs;
-    for (size_t i = 0; i < n; ++i) segs.push_back({in[i]->data(), {Pp(static_cast<int>(i)), in[i]->bytes()}});
+    for (size_t i = 0; i < n; ++i) segs.push_back({in[i]->data(), {slot(static_cast<int>(i)), in[i]->bytes()}});
     segs.push_back({in[n]->data(), {ids, static_cast<size_t>(N) * 4}});
     segs.push_back({in[n + 1]->data(), {keys_buf, static_cast<size_t>(B) * 16}});
     SB_TRY(copy_segs(s, segs, st));
@@ -749,6 +783,7 @@ class GptVagModule : public Module {
     }
     if (!ex) {
       exec_dp[mode] = dp;
+      exec_pin[mode] = pin;
       cudaGraph_t graph = nullptr;
       SB_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
       sb_status e = enqueue(s, st, mode);

@@ -165,6 +165,44 @@ def test_gpt2_small_shape_at_full_context_matches_oracle(cuda):
         assert_close(g, r, TOL_BF16, nm)
 
 
+def test_vag_reads_resident_parameters_in_place(cuda):
+    """Parameters passed as resident device buffers are read where they lie:
+    alternating two parameter sets (eager call, graph capture, recaptures on
+    every change of addresses), and rewriting one set's contents in place
+    between calls, every call returns exactly what a fresh session computes
+    for the parameters it was given."""
+    from sheaf_b200.runtime import Session
+
+    cfg = CFGS["tiny"]
+    la, x, y = models.gpt_inputs(cfg, seed_params=0)
+    lb, _, _ = models.gpt_inputs(cfg, seed_params=5)
+    la = [odt.round_bf16(l) for l in la]
+    lb = [odt.round_bf16(l) for l in lb]
+    lc = [odt.round_bf16(l * 0.5) for l in la]  # set A rewritten in place
+
+    def fresh(leaves):
+        (out,) = run_vag(cfg, "bf16", leaves, x, y)
+        return out
+
+    ref = {"a": fresh(la), "b": fresh(lb), "c": fresh(lc)}
+    s = Session(0)
+    s.create_gpt_vag("gpt", n_layer=cfg.n_layer, n_head=cfg.n_head, n_embd=cfg.n_embd, block_size=cfg.block_size,
+                     vocab_size=cfg.vocab_size, batch=cfg.batch, seq=cfg.seq, elem=BF16)
+    ba = [s.upload(l, BF16) for l in la]
+    bb = [s.upload(l, BF16) for l in lb]
+    ids = [s.upload(x, F32), s.upload(y, F32)]
+    rewritten = False
+    for which in ("a", "b", "a", "a", "b", "c", "c", "b"):
+        if which == "c" and not rewritten:  # same buffers (addresses), new contents
+            for buf, l in zip(ba, lc):
+                buf.write(odt.f32_to_bf16_bits(l))
+            rewritten = True
+        bufs = (bb if which == "b" else ba) + ids
+        got = [o.to_host() for o in s.call("gpt.value_and_grad", bufs)]
+        for g, r in zip(got, ref[which]):
+            assert np.array_equal(g, r), which
+
+
 def test_vag_rejects_bad_inputs(cuda):
     from sheaf_b200.runtime import SheafB200Error, Session
 
