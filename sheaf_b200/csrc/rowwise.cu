@@ -265,28 +265,6 @@ __device__ __forceinline__ float block_sum_ordered(float v, float* red) {
   return t;
 }
 
-// Column of float4 chunk j of thread tid (nt threads a row) in the wide
-// layer-norm kernels: with two or more chunks a thread owns pairs of
-// consecutive chunks (8 columns), so that bf16 rows are written 16 bytes at a
-// time.
-template <int CPT>
-__device__ __forceinline__ int wide_col(int j, int nt, int tid) {
-  if constexpr (CPT >= 2)
-    return ((j >> 1) * nt + tid) * 8 + (j & 1) * 4;
-  else
-    return (j * nt + tid) * 4;
-}
-
-__device__ __forceinline__ void store8(float* p, float4 a, float4 b) {
-  reinterpret_cast<float4*>(p)[0] = a;
-  reinterpret_cast<float4*>(p)[1] = b;
-}
-__device__ __forceinline__ void store8(__nv_bfloat16* p, float4 a, float4 b) {
-  __nv_bfloat162 h[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
-                         __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
-  *reinterpret_cast<uint4*>(p) = *reinterpret_cast<uint4*>(h);
-}
-
 template <int CPT, typename TO>
 __global__ void __launch_bounds__(256) ln_fwd_wide_kernel(const float* __restrict__ x, const void* __restrict__ gamma,
                                                           int gamma_f32, TO* __restrict__ y,
@@ -299,7 +277,7 @@ __global__ void __launch_bounds__(256) ln_fwd_wide_kernel(const float* __restric
   float4 g[CPT];
 #pragma unroll
   for (int j = 0; j < CPT; ++j) {
-    const int c = wide_col<CPT>(j, nt, tid);
+    const int c = (j * nt + tid) * 4;
     g[j] = c < D ? (gamma_f32 ? load4(static_cast<const float*>(gamma) + c)
                               : load4(static_cast<const __nv_bfloat16*>(gamma) + c))
                  : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -310,14 +288,14 @@ __global__ void __launch_bounds__(256) ln_fwd_wide_kernel(const float* __restric
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < CPT; ++j) {
-      const int c = wide_col<CPT>(j, nt, tid);
+      const int c = (j * nt + tid) * 4;
       v[j] = c < D ? load4(x + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
       s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
     }
     if (x_copy) {
 #pragma unroll
       for (int j = 0; j < CPT; ++j) {
-        const int c = wide_col<CPT>(j, nt, tid);
+        const int c = (j * nt + tid) * 4;
         if (c < D) store4(x_copy + off + c, v[j]);
       }
     }
@@ -325,7 +303,7 @@ __global__ void __launch_bounds__(256) ln_fwd_wide_kernel(const float* __restric
     float q = 0.f;
 #pragma unroll
     for (int j = 0; j < CPT; ++j) {
-      const int c = wide_col<CPT>(j, nt, tid);
+      const int c = (j * nt + tid) * 4;
       if (c < D) {
         const float a = v[j].x - mean, b = v[j].y - mean, cc = v[j].z - mean, d = v[j].w - mean;
         q += (a * a + b * b) + (cc * cc + d * d);
@@ -333,30 +311,12 @@ __global__ void __launch_bounds__(256) ln_fwd_wide_kernel(const float* __restric
     }
     const float var = block_sum_ordered(q, red2) / static_cast<float>(D);
     const float rstd = 1.0f / sqrtf(var + 1e-5f);
-    float4 o[CPT];
 #pragma unroll
-    for (int j = 0; j < CPT; ++j)
-      o[j] = make_float4(((v[j].x - mean) * rstd) * g[j].x, ((v[j].y - mean) * rstd) * g[j].y,
-                         ((v[j].z - mean) * rstd) * g[j].z, ((v[j].w - mean) * rstd) * g[j].w);
-    if constexpr (CPT >= 2) {
-      // a thread's chunks come in pairs of 8 consecutive columns: one 16-byte
-      // store per pair for bf16 rows
-#pragma unroll
-      for (int j = 0; j < CPT; j += 2) {
-        const int c = wide_col<CPT>(j, nt, tid);
-        if ((D & 7) == 0 && c + 8 <= D) {  // 16-byte aligned: rows are multiples of 8 values
-          store8(y + off + c, o[j], o[j + 1]);
-        } else {
-          if (c < D) store4(y + off + c, o[j]);
-          if (c + 4 < D) store4(y + off + c + 4, o[j + 1]);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < CPT; ++j) {
-        const int c = wide_col<CPT>(j, nt, tid);
-        if (c < D) store4(y + off + c, o[j]);
-      }
+    for (int j = 0; j < CPT; ++j) {
+      const int c = (j * nt + tid) * 4;
+      if (c < D)
+        store4(y + off + c, make_float4(((v[j].x - mean) * rstd) * g[j].x, ((v[j].y - mean) * rstd) * g[j].y,
+                                        ((v[j].z - mean) * rstd) * g[j].z, ((v[j].w - mean) * rstd) * g[j].w));
     }
     if (tid == 0) {
       mean_out[row] = mean;
