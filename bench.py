@@ -545,6 +545,25 @@ def sweep_ops(only: str | None = None, reps: int = 10):
             tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
             emit({"op": name, "ms": ms, "achieved": tf, "unit": "TFLOP/s", "bound": "tensor" if kind == "bf16" else
                   "tensor, bf16x6", "frac_of_bf16_peak": tf / tc_burst})
+        # GPT-2-small's GEMMs (8192 tokens, d 768): forward qkv / fc / fc2 / head,
+        # a dX (B MN-major) and a weight gradient (both MN-major), plain stores
+        for nm, M, N, K, ta, tb in (("qkv", 8192, 2304, 768, 0, 1), ("fc", 8192, 3072, 768, 0, 1),
+                                    ("fc2", 8192, 768, 3072, 0, 1), ("head", 8192, 50304, 768, 0, 1),
+                                    ("dx_fc", 8192, 768, 3072, 0, 0), ("dw_fc", 3072, 768, 8192, 1, 0)):
+            name = f"gemm_{kind}_gpt2_{nm}"
+            if kind != "bf16" or not want(name):
+                continue
+            a = torch.randn(*((K, M) if ta else (M, K)), device=dev).to(dt)
+            b = torch.randn(*((N, K) if tb else (K, N)), device=dev).to(dt)
+            c = torch.empty(M, N, device=dev, dtype=dt)
+            wsb = L.sb_op_matmul_workspace_size(elem, ta, tb, M, N, K)
+            ws = torch.empty(max(wsb // 4, 1), device=dev)
+            fn = lambda: L.sb_op_matmul(elem, a.data_ptr(), a.shape[1], ta, b.data_ptr(), b.shape[1], tb, M, N, K,  # noqa
+                                        c.data_ptr(), N, elem, ws.data_ptr(), wsb, st())
+            ms = _time_op(fn, reps, flush)
+            tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+            emit({"op": name, "ms": ms, "achieved": tf, "unit": "TFLOP/s", "bound": "tensor",
+                  "frac_of_bf16_peak": tf / tc_burst})
         es_ = 2 if kind == "bf16" else 4
         for R, V in ((CFG["batch"] * CFG["seq"], CFG["vocab_size"]), (8192, 50304)):
             name = f"cross_entropy_{kind}_{R}x{V}"
