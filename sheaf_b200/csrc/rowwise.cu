@@ -569,20 +569,19 @@ __global__ void __launch_bounds__(kCeWideThreads, 3) ce_wide_kernel(const T* __r
           for (int e = 0; e < E; ++e) v[u][e] = -INFINITY;
         }
       }
+      // the max over raw values (log2 e > 0 keeps the order), then one FMA
+      // per value into log2 units inside the exponential
       float cm = -INFINITY;
 #pragma unroll
       for (int u = 0; u < U; ++u)
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          v[u][e] *= kL2e;
-          cm = fmaxf(cm, v[u][e]);
-        }
-      const float nm = fmaxf(m, cm);
+        for (int e = 0; e < E; ++e) cm = fmaxf(cm, v[u][e]);
+      const float nm = fmaxf(m, cm * kL2e);
       float acc = m == -INFINITY ? 0.f : sum * ex2_fast(m - nm);
 #pragma unroll
       for (int u = 0; u < U; ++u)
 #pragma unroll
-        for (int e = 0; e < E; ++e) acc += ex2_fast(v[u][e] - nm);
+        for (int e = 0; e < E; ++e) acc += ex2_fast(fmaf(v[u][e], kL2e, -nm));
       sum = acc;
       m = nm;
     }
@@ -623,6 +622,9 @@ __global__ void __launch_bounds__(kCeWideThreads, 3) ce_wide_kernel(const T* __r
     const float lse2 = sm_row[0];
     const int y = static_cast<int>(sm_row[1]);
     const float hit = y >= 0 ? inv_rows : 0.f;
+    // softmax / rows = 2^(x log2 e - lse2 + log2(1 / rows)); a row without a
+    // class gets 2^-inf = 0
+    const float off = y >= 0 ? lse2 - log2f(inv_rows) : INFINITY;
     T* dr = dlogits + static_cast<long>(row) * ldd;
     for (int i0 = threadIdx.x; i0 < nvec; i0 += U * kCeWideThreads) {
       float v[U][E];
@@ -636,9 +638,12 @@ __global__ void __launch_bounds__(kCeWideThreads, 3) ce_wide_kernel(const T* __r
         const int i = i0 + u * kCeWideThreads;
         if (i < nvec) {
 #pragma unroll
-          for (int e = 0; e < E; ++e) {
-            const int c = i * E + e;
-            v[u][e] = ex2_fast(fmaf(v[u][e], kL2e, -lse2)) * hit - (c == y ? inv_rows : 0.f);
+          for (int e = 0; e < E; ++e) v[u][e] = ex2_fast(fmaf(v[u][e], kL2e, -off));
+          const int rel = y - i * E;  // the one-hot's column, if it lies in this chunk
+          if (rel >= 0 && rel < E) {
+#pragma unroll
+            for (int e = 0; e < E; ++e)
+              if (e == rel) v[u][e] -= inv_rows;
           }
           store_vec16(dr + static_cast<long>(i) * E, v[u]);
         }
