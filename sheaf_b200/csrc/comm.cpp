@@ -22,6 +22,7 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <thread>
@@ -114,6 +115,20 @@ sb_status comm_init(Session& s, const void* unique_id, size_t id_bytes, int rank
   std::memcpy(&id, unique_id, sizeof(id));
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
+  // The all-reduces run beside the step's persistent kernels (one CTA per
+  // SM): every SM an all-reduce holds pushes CTAs of those kernels into a
+  // second wave. At most kNcclMaxCtas CTAs per collective (measured on two
+  // B200s: nanoGPT-char 2.564 -> 2.44 ms/step with 8 or 16, GPT-2-small 9.98
+  // -> 10.11 ms at 16 and worse below, its 248 MB of gradients needing the
+  // bandwidth). SHEAF_B200_NCCL_MAX_CTAS overrides it; 0 leaves NCCL's choice.
+  constexpr int kNcclMaxCtas = 16;
+  int max_ctas = kNcclMaxCtas;
+  if (const char* e = std::getenv("SHEAF_B200_NCCL_MAX_CTAS")) max_ctas = std::atoi(e);
+  if (max_ctas > 0) {
+    cfg.minCTAs = 1;
+    cfg.maxCTAs = max_ctas;
+    cfg.nvlsCTAs = max_ctas;
+  }
   auto* c = new Comm();
   cudaSetDevice(s.device);
   ncclResult_t r = a.initRankConfig(&c->comm, world, id, rank, &cfg);
