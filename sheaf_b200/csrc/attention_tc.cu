@@ -360,9 +360,10 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_tc(const __grid_constant__ CU
 // backward
 // ---------------------------------------------------------------------------
 
+constexpr int kBwdSoftmaxWarps = 8;
+constexpr int kBwdThreads = 32 * (2 + kBwdSoftmaxWarps);
 constexpr size_t kBwdSmem = 1024 + 4 * kTileBytes /*K,V x2*/ + 4 * kTileBytes /*Q,dO x2*/ +
-                            4 * kTileBytes /*P^T, dS^T*/ + kTileBytes /*dQ staging, 4 KB per warp*/ +
-                            4 * kT * 4 /*lse, delta x2*/ + 24 * 8 + 16;
+                            4 * kTileBytes /*P^T, dS^T*/ + 4 * kT * 4 /*lse, delta x2*/ + 24 * 8 + 16;
 
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t smem_src, int x, int y) {
   asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
@@ -392,7 +393,16 @@ __device__ __forceinline__ BwdItem bwd_item(const AttnArgs& a, int u) {
 // buffered and the Q/dO ring runs across items, so the next item's loads
 // land while the current one computes; lse/delta of the next query tile are
 // loaded one tile ahead; dK/dV leave through swizzled staging and TMA stores.
-__global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CUtensorMap tm_qkv,
+// Warp 0 loads, warp 1 issues the UMMAs, warps 2-9 compute P^T / dS^T and
+// drain dQ / dK / dV: two warps per TMEM lane quarter (the warp's index mod
+// 4), each owning one 64-column half of its 32 rows -- query chunks 2h and
+// 2h+1 of P^T and dS^T (SW128 atom h), dQ columns 32h..32h+31, and dK (h = 0)
+// or dV (h = 1) -- so each sub-partition runs two of these warps and one's
+// TMEM loads and exponentials overlap the other's. A warp stages its dQ
+// reduce-adds and its dK / dV stores in its own rows of atom h of dS^T and
+// P^T, which no UMMA reads between the commit it waited for and the next
+// tile's softmax.
+__global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_tc(const __grid_constant__ CUtensorMap tm_qkv,
                                                       const __grid_constant__ CUtensorMap tm_do,
                                                       const __grid_constant__ CUtensorMap tm_dq,
                                                       const __grid_constant__ CUtensorMap tm_dkv, AttnArgs a) {
@@ -403,9 +413,8 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
   uint8_t* sQ = sV + 2 * kTileBytes;      // [2]
   uint8_t* sdO = sQ + 2 * kTileBytes;     // [2]
   uint8_t* sPT = sdO + 2 * kTileBytes;    // 32 KB; also dK (first atom) / dV (second atom) staging
-  uint8_t* sdST = sPT + 2 * kTileBytes;   // 32 KB
-  uint8_t* sStg = sdST + 2 * kTileBytes;  // 4 warps x 4 KB dQ staging
-  float* sLse = reinterpret_cast<float*>(sStg + kTileBytes);  // [2][128]
+  uint8_t* sdST = sPT + 2 * kTileBytes;   // 32 KB; also dQ staging
+  float* sLse = reinterpret_cast<float*>(sdST + 2 * kTileBytes);  // [2][128]
   float* sDel = sLse + 2 * kT;                                // [2][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 2 * kT);
   uint64_t* kv_full = bars + 0;     // [2]
@@ -418,7 +427,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
   uint64_t* dq_empty = bars + 11;
   uint64_t* acc_full = bars + 12;
   uint64_t* acc_empty = bars + 13;
-  uint64_t* stats_full = bars + 14;  // [2]: the 4 softmax warps wrote lse / delta of a query tile
+  uint64_t* stats_full = bars + 14;  // [2]: the softmax warps wrote lse / delta of a query tile
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -431,14 +440,14 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
       mbar_init(&kv_empty[i], 1);
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
-      mbar_init(&stats_full[i], 4);
+      mbar_init(&stats_full[i], kBwdSoftmaxWarps);
     }
     mbar_init(st_full, 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, kBwdSoftmaxWarps);
     mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 4);
+    mbar_init(dq_empty, kBwdSoftmaxWarps);
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 4);
+    mbar_init(acc_empty, kBwdSoftmaxWarps);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -567,27 +576,31 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
       }
     }
   } else {
-    const int quarter = warp & 3;
+    const int quarter = warp & 3;        // TMEM lanes 32*quarter .. +31
+    const int half = (warp - 2) >> 2;    // 64-column half of those rows
     const int tid = quarter * 32 + lane;  // 0..127: key row (S^T, dK, dV) / query row (dQ)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl = a.scale * kLog2e;
     const float2 sl2 = make_float2(sl, sl), sc2 = make_float2(a.scale, a.scale);
     const uint32_t pt_addr = smem_u32(sPT), dst_addr = smem_u32(sdST);
-    const uint32_t stg = smem_u32(sStg) + (warp - 2) * 4096;
+    // this warp's 32 rows of atom `half` of P^T and of dS^T (4 KB each)
+    const uint32_t own_pt = pt_addr + half * 16384 + quarter * 4096;
+    const uint32_t own_dst = dst_addr + half * 16384 + quarter * 4096;
     // Per query row of tile i of head bh into buffer s: lse (log2 units) and
     // delta * scale, delta = rowsum(dO * O). Issued one tile ahead so that
     // the global loads overlap the previous tile's UMMAs.
-    // delta of the warp's 32 rows with coalesced loads: instruction k reads
-    // rows 4k .. 4k+3 (eight lanes a row, 16 bytes each; all sixteen loads
-    // in flight first), the eight partial dot products of a row are summed
-    // by shuffles.
+    // delta of the quarter's 32 rows with coalesced loads, half of them per
+    // warp: instruction k reads rows 16h + 4k .. +3 (eight lanes a row, 16
+    // bytes each; all eight loads in flight first), the eight partial dot
+    // products of a row are summed by shuffles.
     auto load_row_stats = [&](const BwdItem& w, int i, int s) {
       const int q = i * kT + tid;
       const int ch = lane & 7;
-      uint4 ov[8], dv[8];
+      const int r0 = quarter * 32 + half * 16;
+      uint4 ov[4], dv[4];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int qk = i * kT + quarter * 32 + 4 * k + (lane >> 3);
+      for (int k = 0; k < 4; ++k) {
+        const int qk = i * kT + r0 + 4 * k + (lane >> 3);
         ov[k] = dv[k] = make_uint4(0u, 0u, 0u, 0u);
         if (qk < a.T) {
           const long off = static_cast<long>(w.row0 + qk) * a.D + w.h * kHd + ch * 8;
@@ -596,7 +609,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
         }
       }
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < 4; ++k) {
         const uint32_t ow[4] = {ov[k].x, ov[k].y, ov[k].z, ov[k].w}, dw[4] = {dv[k].x, dv[k].y, dv[k].z, dv[k].w};
         float dl = 0.f;
 #pragma unroll
@@ -608,9 +621,9 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
         dl += __shfl_xor_sync(0xffffffffu, dl, 4);
         dl += __shfl_xor_sync(0xffffffffu, dl, 2);
         dl += __shfl_xor_sync(0xffffffffu, dl, 1);
-        if (ch == 0) sDel[s * kT + quarter * 32 + 4 * k + (lane >> 3)] = dl * a.scale;
+        if (ch == 0) sDel[s * kT + r0 + 4 * k + (lane >> 3)] = dl * a.scale;
       }
-      sLse[s * kT + tid] = (q < a.T) ? a.lse[static_cast<long>(w.bh) * a.T + q] * kLog2e : INFINITY;
+      if (half == 0) sLse[s * kT + tid] = (q < a.T) ? a.lse[static_cast<long>(w.bh) * a.T + q] * kLog2e : INFINITY;
       __syncwarp();
       if (lane == 0) mbar_arrive(&stats_full[s]);
     };
@@ -635,7 +648,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
           break;
         }
         tc_fence_after();
-        // this warp's rows of sPT held the previous item's dK / dV staging
+        // this warp's rows of P^T / dS^T held its previous dQ / dK / dV staging
         if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
         const float* lse2 = sLse + s * kT;
@@ -646,7 +659,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
         // c < quarter (P = dS = 0), and for t >= lane when c == quarter.
         const int cfirst = (i == w.kt) ? quarter : 0;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 2 * half; c < 2 * half + 2; ++c) {
           uint32_t pp[16], pd[16];
           if (c < cfirst) {
 #pragma unroll
@@ -705,65 +718,52 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_tc(const __grid_constant__ CU
           break;
         }
         tc_fence_after();
-        uint32_t q0[32], q1[32];
-        tmem_ld32(tdQ + lane_base, q0);
-        tmem_ld32(tdQ + lane_base + 32, q1);
+        uint32_t qv[32];
+        tmem_ld32(tdQ + lane_base + half * 32, qv);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(dq_empty);
-        // This warp's 32 query rows x 64 columns of dQ are added into the fp32
-        // accumulator with two bulk tensor reduce-adds (32 columns each)
-        // through one 4 KB slot. Rows past T hold exact zeros (their P and dS
-        // are zero).
-        const int y = w.row0 + i * kT + quarter * 32;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          if (lane == 0) bulk_wait_read<0>();
-          __syncwarp();
-          st_row128_sw(stg, lane, half ? q1 : q0);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_reduce_add_2d(&tm_dq, stg, w.h * kHd + half * 32, y);
-            bulk_commit();
-          }
+        // This warp's 32 query rows x 32 columns of dQ are added into the fp32
+        // accumulator with one bulk tensor reduce-add staged in the warp's own
+        // dS^T rows (the dK and dQ UMMAs that read them have completed). Rows
+        // past T hold exact zeros (their P and dS are zero).
+        st_row128_sw(own_dst, lane, qv);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tm_dq, own_dst, w.h * kHd + half * 32, w.row0 + i * kT + quarter * 32);
+          bulk_commit();
         }
       }
       if (!ok) break;
-      // dK / dV of this item: TMEM -> bf16 -> this warp's rows of sPT (dK in
-      // the first 16 KB atom, dV in the second) -> TMA stores clipped at T
+      // dK (half 0) or dV (half 1) of this item: TMEM -> bf16 -> the warp's
+      // own rows of P^T (no bulk copy reads them: the dQ staging is in dS^T)
+      // -> TMA store clipped at T
       if (!mbar_wait(acc_full, j & 1, a.err, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t k0[32], k1[32], v0[32], v1[32];
-      tmem_ld32(tdK + lane_base, k0);
-      tmem_ld32(tdK + lane_base + 32, k1);
-      tmem_ld32(tdV + lane_base, v0);
-      tmem_ld32(tdV + lane_base + 32, v1);
+      const uint32_t tacc = half ? tdV : tdK;
+      uint32_t x0[32], x1[32];
+      tmem_ld32(tacc + lane_base, x0);
+      tmem_ld32(tacc + lane_base + 32, x1);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
-      uint32_t wk[32], wv[32];
+      uint32_t wx[32];
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
-        wk[t] = pack_bf16x2(__uint_as_float(k0[2 * t]), __uint_as_float(k0[2 * t + 1]));
-        wk[16 + t] = pack_bf16x2(__uint_as_float(k1[2 * t]), __uint_as_float(k1[2 * t + 1]));
-        wv[t] = pack_bf16x2(__uint_as_float(v0[2 * t]), __uint_as_float(v0[2 * t + 1]));
-        wv[16 + t] = pack_bf16x2(__uint_as_float(v1[2 * t]), __uint_as_float(v1[2 * t + 1]));
+        wx[t] = pack_bf16x2(__uint_as_float(x0[2 * t]), __uint_as_float(x0[2 * t + 1]));
+        wx[16 + t] = pack_bf16x2(__uint_as_float(x1[2 * t]), __uint_as_float(x1[2 * t + 1]));
       }
-      const uint32_t sk = pt_addr + quarter * 4096, sv = pt_addr + 16384 + quarter * 4096;
-      st_row128_sw(sk, lane, wk);
-      st_row128_sw(sv, lane, wv);
+      st_row128_sw(own_pt, lane, wx);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        const int t0 = w.kt * kT + quarter * 32;
-        tma_store_3d(&tm_dkv, sk, a.D + w.h * kHd, t0, w.b);
-        tma_store_3d(&tm_dkv, sv, 2 * a.D + w.h * kHd, t0, w.b);
+        tma_store_3d(&tm_dkv, own_pt, (1 + half) * a.D + w.h * kHd, w.kt * kT + quarter * 32, w.b);
         bulk_commit();
       }
     }
@@ -864,7 +864,7 @@ int attention_bwd_tc(const void* qkv, const void* o, const void* dout, const flo
     attr = true;
   }
   const int items = sh.B * sh.H * a.ntiles;
-  launch_pdl(attn_bwd_tc, dim3(std::min(items, num_sms())), dim3(192), kBwdSmem, s, tq, td, tdq, tdkv, a);
+  launch_pdl(attn_bwd_tc, dim3(std::min(items, num_sms())), dim3(kBwdThreads), kBwdSmem, s, tq, td, tdq, tdkv, a);
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
   const int tx = std::min(D / 8, 128), ty = std::max(1, 384 / tx);
   launch_pdl(dq_convert_kernel, dim3((N + ty - 1) / ty), dim3(tx, ty), 0, s, dq_acc, static_cast<__nv_bfloat16*>(dqkv),
