@@ -135,6 +135,8 @@ GemmDesc split_desc(const GemmDesc& d) {
   e.out_f32 = true;
   e.splits = std::max(2, (e.K + kSplitK - 1) / kSplitK);
   e.max_splits = 0;
+  e.max_ctas = 0;
+  e.max_pair_splits = 0;
   return e;
 }
 

@@ -789,6 +789,8 @@ Plan plan_for(const GemmDesc& d) {
     if (d.epi == EPI_STORE && d.N % 4 == 0 && tiles * 2 <= slots && p.kb_total >= 8)
       splits = std::min(slots / tiles, p.kb_total / 4);
     if (d.max_splits > 0) splits = std::min(splits, d.max_splits);
+    if (d.max_ctas > 0) splits = std::min(splits, std::max(1, d.max_ctas / (tiles * (p.pair ? 2 : 1))));
+    if (d.max_pair_splits > 0 && p.pair) splits = std::min(splits, d.max_pair_splits);
   }
   if (d.epi != EPI_STORE || d.N % 4 != 0) splits = 1;  // partial rows of N floats must be 16-byte multiples
   splits = std::max(1, std::min(splits, p.kb_total));

@@ -229,15 +229,25 @@ class GptVagModule : public Module {
     return d;
   }
 
-  // Weight-gradient GEMMs beside the critical path use at most 6 splits of
-  // their token dimension: they then occupy about three quarters of the SMs
-  // and leave the rest to the critical path's kernels (measured fastest
-  // among 2..12 splits: 2.47 ms/step at 6, 2.51 at the full-GPU choice).
-  static constexpr int kSideSplits = 6;
+  // Weight-gradient GEMMs beside the critical path split their token
+  // dimension over at most 108 CTAs, and CTA-pair tiles at most 6 ways: they
+  // then occupy about three quarters of the SMs and leave the rest to the
+  // critical path's kernels. Measured on nanoGPT-char (ms/step): at most 6
+  // splits for every GEMM 2.304; the same with the 384 x 384 proj weight
+  // gradient on 6 tiles x 18 splits (the CTA cap) 2.266-2.274, x 24 splits
+  // 2.281; the CTA cap alone (pair tiles at 9-10 splits) 2.305; the
+  // full-GPU choice for every GEMM slower still. On GPT-2-small the CTA cap
+  // puts the fc and fc2 weight gradients (36 pair tiles each) on one split
+  // instead of two: 9.26-9.30 -> 9.00-9.08 ms/step.
+  static constexpr int kSideCtas = 108;
+  static constexpr int kSidePairSplits = 6;
 
   int gemm(const GemmDesc& d0, cudaStream_t st, int* err, bool side = false) const {
     GemmDesc d = d0;
-    if (side) d.max_splits = kSideSplits;
+    if (side) {
+      d.max_ctas = kSideCtas;
+      d.max_pair_splits = kSidePairSplits;
+    }
     float* w = side ? ws_w : ws;
     const size_t wb = side ? ws_w_bytes : ws_bytes;
     return bf ? gemm_bf16(d, w, wb, st, err) : gemm_f32(d, w, wb, st, err);

@@ -39,6 +39,8 @@ struct GemmDesc {
   int bn = 0;      // 0 = choose tile width (64, 128, 192, 256; 384 runs on CTA pairs)
   int pair = -1;   // 256-row tiles on CTA pairs: -1 = when the tile allows, 0 = never
   int max_splits = 0;  // cap on the chosen split-K factor (0 = none)
+  int max_ctas = 0;    // cap on the CTAs the chosen split-K factor occupies (0 = none)
+  int max_pair_splits = 0;  // cap on the chosen split-K factor of CTA-pair tiles (0 = none)
 };
 
 // bf16 operands on tcgen05 tensor cores (fp32 accumulation in TMEM).
