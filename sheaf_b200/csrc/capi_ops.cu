@@ -103,7 +103,7 @@ int sb_op_layernorm_fwd(uint32_t elem, const void* x, const void* gamma, void* y
                         int32_t rows, int32_t d, void* stream) {
   if (!float_elem(elem) || !x || !gamma || !y || !mean || !rstd) return SB_OPERR_ARGS;
   const bool f = elem == SB_ELEM_F32;
-  return sb::layernorm_fwd(static_cast<const float*>(x), gamma, f, y, f, static_cast<float*>(mean),
+  return sb::layernorm_fwd(x, true, gamma, f, y, f, static_cast<float*>(mean),
                            static_cast<float*>(rstd), rows, d, static_cast<cudaStream_t>(stream));
 }
 
@@ -115,7 +115,7 @@ int sb_op_layernorm_bwd(uint32_t elem, const void* dy, const void* x, const void
   if (!float_elem(elem) || !dy || !x || !mean || !rstd || !gamma || !dres || !dgamma) return SB_OPERR_ARGS;
   if (workspace_bytes < sb::layernorm_bwd_workspace_bytes(rows, d) || !workspace) return SB_OPERR_WORKSPACE;
   const bool f = elem == SB_ELEM_F32;
-  return sb::layernorm_bwd(dy, true, static_cast<const float*>(x), static_cast<const float*>(mean),
+  return sb::layernorm_bwd(dy, true, x, true, static_cast<const float*>(mean),
                            static_cast<const float*>(rstd), gamma, f, static_cast<float*>(dres), nullptr, dgamma, f,
                            static_cast<float*>(workspace), rows, d, static_cast<cudaStream_t>(stream));
 }
@@ -145,7 +145,7 @@ int sb_op_gelu_bwd(uint32_t elem, const void* x, const void* g, void* dx, int64_
 int sb_op_embedding_fwd(uint32_t elem, const void* ids, const void* wte, const void* wpe, void* x, int32_t ntok,
                         int32_t t, int32_t v, int32_t d, void* stream) {
   if (!float_elem(elem) || !ids || !wte || !wpe || !x || t <= 0 || v <= 0) return SB_OPERR_ARGS;
-  return sb::embedding_fwd(static_cast<const float*>(ids), wte, wpe, elem == SB_ELEM_F32, static_cast<float*>(x),
+  return sb::embedding_fwd(static_cast<const float*>(ids), wte, wpe, elem == SB_ELEM_F32, x, true,
                            ntok, t, v, d, static_cast<cudaStream_t>(stream));
 }
 

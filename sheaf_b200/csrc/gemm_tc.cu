@@ -434,7 +434,9 @@ __global__ void __launch_bounds__(384, 1)
           stage(v, &tmC, col0, store_y, a.epi == EPI_ACCUM);
         }
       } else {
-        // 64 bf16 columns (128 B) per block: STORE, GELU (two outputs), MUL
+        // 64 bf16 columns (128 B) per block: STORE, ACCUM (bf16 reduce-add
+        // into the residual stream: x + bf16(acc) rounded to bf16, as the
+        // module's bf16 add), GELU (two outputs), MUL
 #pragma unroll 1
         for (int c = cb16; c < ce16; ++c) {
           const int col0 = nt * BN + c * 64;
@@ -444,13 +446,13 @@ __global__ void __launch_bounds__(384, 1)
           tmem_ld32(t_row + c * 64 + 32, v1);
           tmem_wait_ld();
           uint32_t w[32];
-          if (a.epi == EPI_STORE) {
+          if (a.epi == EPI_STORE || a.epi == EPI_ACCUM) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               w[j] = pack_bf16x2(__uint_as_float(v0[2 * j]), __uint_as_float(v0[2 * j + 1]));
               w[16 + j] = pack_bf16x2(__uint_as_float(v1[2 * j]), __uint_as_float(v1[2 * j + 1]));
             }
-            stage(w, &tmC, col0, store_y, false);
+            stage(w, &tmC, col0, store_y, a.epi == EPI_ACCUM);
           } else if (a.epi == EPI_GELU) {
             // u is the bf16-rounded product, as the module's dot_general
             // result (rounded in pairs: the paired conversion keeps the
@@ -848,10 +850,8 @@ size_t gemm_workspace_bytes(const GemmDesc& d, bool bf16) {
 
 int gemm_bf16(const GemmDesc& d, float* workspace, size_t workspace_bytes, cudaStream_t s, int* err) {
   if (d.M <= 0 || d.N <= 0 || d.K <= 0) return 1;
-  const bool f32_epi = d.epi == EPI_ADD || d.epi == EPI_ACCUM || (d.epi == EPI_STORE && d.out_f32);
-  if (((d.epi == EPI_ADD || d.epi == EPI_ACCUM) && !d.out_f32) ||
-      ((d.epi == EPI_GELU || d.epi == EPI_MUL) && d.out_f32))
-    return 1;
+  const bool f32_epi = d.epi == EPI_ADD || ((d.epi == EPI_STORE || d.epi == EPI_ACCUM) && d.out_f32);
+  if ((d.epi == EPI_ADD && !d.out_f32) || ((d.epi == EPI_GELU || d.epi == EPI_MUL) && d.out_f32)) return 1;
   Plan p = plan_for(d);
   GemmArgs a{};
   a.M = d.M;

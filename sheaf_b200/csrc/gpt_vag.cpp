@@ -8,7 +8,9 @@
 //             fused causal attention -> proj GEMM (+residual) -> LN ->
 //             fc GEMM (+GELU epilogue) -> fc2 GEMM (+residual); each LN also
 //             copies its input to the next residual buffer, into which the
-//             residual GEMM accumulates with bulk tensor reduce-adds;
+//             residual GEMM accumulates with bulk tensor reduce-adds (the
+//             residual stream in the module's element type: a bf16 module
+//             adds and rounds in bf16, as its compiled graph does);
 //             final LN -> head GEMM -> fused cross-entropy fwd+VJP
 //   backward: the `@` VJP GEMMs (dX with K-major / N-major operands, dW
 //             contracted over all tokens with split-K), GELU-VJP fused in the
@@ -82,7 +84,8 @@ class GptVagModule : public Module {
   char* grads = nullptr;  // gradients followed by the loss (output element type)
   float* ids = nullptr;   // x ids [N] then y ids [N]
   float* loss_f32 = nullptr;
-  std::vector<float*> xs, xmid, mean1, rstd1, mean2, rstd2, lse;
+  std::vector<void*> xs, xmid;  // residual stream, model element type
+  std::vector<float*> mean1, rstd1, mean2, rstd2, lse;
   float *meanf = nullptr, *rstdf = nullptr;
   std::vector<void*> h1, h2, qkv, att, gder, gact;  // gder = gelu'(u) saved for the VJP
   void *hf = nullptr, *logits = nullptr, *dlogits = nullptr;
@@ -331,21 +334,21 @@ class GptVagModule : public Module {
     SB_TRY(devt(4, &loss_f32));
     const size_t nd = static_cast<size_t>(N) * D;
     for (int l = 0; l <= L; ++l) {
-      float* p;
-      SB_TRY(devt(nd, &p));
-      xs.push_back(p);
+      void* q;
+      SB_TRY(dev(nd * es, &q));
+      xs.push_back(q);
     }
     for (int l = 0; l < L; ++l) {
       float* p;
-      SB_TRY(devt(nd, &p));
-      xmid.push_back(p);
+      void* q;
+      SB_TRY(dev(nd * es, &q));
+      xmid.push_back(q);
       for (auto* vec : {&mean1, &rstd1, &mean2, &rstd2}) {
         SB_TRY(devt(N, &p));
         vec->push_back(p);
       }
       SB_TRY(devt(static_cast<size_t>(B) * H * T, &p));
       lse.push_back(p);
-      void* q;
       SB_TRY(dev(nd * es, &q));
       h1.push_back(q);
       SB_TRY(dev(nd * es, &q));
@@ -480,19 +483,19 @@ class GptVagModule : public Module {
     const int iw = 3 + 6 * L, ip = 2 + 6 * L, ilnf = 1 + 6 * L;
 
     // ---- forward
-    SB_K(embedding_fwd(ids, Pp(iw), Pp(ip), f32, xs[0], N, T, V, D, st));
+    SB_K(embedding_fwd(ids, Pp(iw), Pp(ip), f32, xs[0], f32, N, T, V, D, st));
     for (int l = 0; l < L; ++l) {
       const int b0 = 1 + 6 * l;
       // LN1 also copies x into xmid, which the proj GEMM then accumulates into
-      SB_K(layernorm_fwd(xs[l], Pp(b0 + 2), f32, h1[l], f32, mean1[l], rstd1[l], N, D, st, xmid[l]));
+      SB_K(layernorm_fwd(xs[l], f32, Pp(b0 + 2), f32, h1[l], f32, mean1[l], rstd1[l], N, D, st, xmid[l]));
       SB_K(gemm(desc(h1[l], D, false, Pp(b0 + 0), D, false, N, 3 * D, D, qkv[l], 3 * D, f32), st, err));
       SB_K(attention_fwd(qkv[l], f32, att[l], lse[l], ash, st));
       {
-        GemmDesc d = desc(att[l], D, false, Pp(b0 + 1), D, false, N, D, D, xmid[l], D, true);
+        GemmDesc d = desc(att[l], D, false, Pp(b0 + 1), D, false, N, D, D, xmid[l], D, f32);
         d.epi = EPI_ACCUM;  // xmid = x + att @ Wproj^T
         SB_K(gemm(d, st, err));
       }
-      SB_K(layernorm_fwd(xmid[l], Pp(b0 + 3), f32, h2[l], f32, mean2[l], rstd2[l], N, D, st, xs[l + 1]));
+      SB_K(layernorm_fwd(xmid[l], f32, Pp(b0 + 3), f32, h2[l], f32, mean2[l], rstd2[l], N, D, st, xs[l + 1]));
       {
         GemmDesc d = desc(h2[l], D, false, Pp(b0 + 4), D, false, N, 4 * D, D, gact[l], 4 * D, f32);
         d.epi = EPI_GELU;
@@ -501,12 +504,12 @@ class GptVagModule : public Module {
         SB_K(gemm(d, st, err));
       }
       {
-        GemmDesc d = desc(gact[l], 4 * D, false, Pp(b0 + 5), 4 * D, false, N, D, 4 * D, xs[l + 1], D, true);
+        GemmDesc d = desc(gact[l], 4 * D, false, Pp(b0 + 5), 4 * D, false, N, D, 4 * D, xs[l + 1], D, f32);
         d.epi = EPI_ACCUM;  // x' = xmid + gelu(...) @ Wfc2^T
         SB_K(gemm(d, st, err));
       }
     }
-    SB_K(layernorm_fwd(xs[L], Pp(ilnf), f32, hf, f32, meanf, rstdf, N, D, st));
+    SB_K(layernorm_fwd(xs[L], f32, Pp(ilnf), f32, hf, f32, meanf, rstdf, N, D, st));
     SB_K(gemm(desc(hf, D, false, Pp(0), D, false, N, V, D, logits, ldl, f32), st, err));
     if (mode == kSample) {
       SB_K(sample_step(logits, f32, ldl, B, T, V, top_k, temperature, ids, keys_buf, tokens_buf, n_new, step_ctr,
@@ -520,7 +523,7 @@ class GptVagModule : public Module {
     SB_K(gemm(desc(dlogits, ldl, true, hf, D, true, V, D, N, Gp(0), D, f32), st, err));
     if (cudaMemsetAsync(dres, 0, static_cast<size_t>(N) * D * sizeof(float), st) != cudaSuccess)
       return make_status(SB_STATUS_INTERNAL, "memset failed");
-    SB_K(layernorm_bwd(dh, f32, xs[L], meanf, rstdf, Pp(ilnf), f32, dres, static_cast<__nv_bfloat16*>(dres_bf),
+    SB_K(layernorm_bwd(dh, f32, xs[L], f32, meanf, rstdf, Pp(ilnf), f32, dres, static_cast<__nv_bfloat16*>(dres_bf),
                        Gp(ilnf), f32, ws, N, D, st));
     int bucket = 0;
     // the all-reduce of a bucket waits for the main stream and, when given,
@@ -581,7 +584,7 @@ class GptVagModule : public Module {
       SB_TRY(mark(ev_fc[l]));
       SB_K(gemm(desc(dul, 4 * D, false, Pp(b0 + 4), D, true, N, D, 4 * D, dh, D, f32), st, err));
       if (l + 1 < L) SB_TRY(wait(ev_proj[l + 1]));  // r1 last read by dW_proj one layer up
-      SB_K(layernorm_bwd(dh, f32, xmid[l], mean2[l], rstd2[l], Pp(b0 + 3), f32, dres, bf_out(r1), Gp(b0 + 3), f32,
+      SB_K(layernorm_bwd(dh, f32, xmid[l], f32, mean2[l], rstd2[l], Pp(b0 + 3), f32, dres, bf_out(r1), Gp(b0 + 3), f32,
                          ws, N, D, st));
       SB_TRY(fork());
       SB_K(gemm(desc(r1, D, true, att[l], D, true, D, D, N, Gp(b0 + 1), D, f32), sst, err, dw_side));
@@ -594,7 +597,7 @@ class GptVagModule : public Module {
       SB_TRY(mark(ev_qkv[l]));
       SB_K(gemm(desc(dql, 3 * D, false, Pp(b0 + 0), D, true, N, D, 3 * D, dh, D, f32), st, err));
       SB_TRY(wait(ev_fc2[l]));  // r0 last read by dW_fc2 of this layer
-      SB_K(layernorm_bwd(dh, f32, xs[l], mean1[l], rstd1[l], Pp(b0 + 2), f32, dres, bf_out(r0), Gp(b0 + 2), f32, ws,
+      SB_K(layernorm_bwd(dh, f32, xs[l], f32, mean1[l], rstd1[l], Pp(b0 + 2), f32, dres, bf_out(r0), Gp(b0 + 2), f32, ws,
                          N, D, st));
       // layer l's six gradients (plus ln_f after the last layer) are final
       SB_TRY(launch_bucket(offs[b0], l == L - 1 ? offs[ip] : offs[b0 + 6], ev_qkv[l]));

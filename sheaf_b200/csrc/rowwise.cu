@@ -91,9 +91,9 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float4 v
 
 // y = (x - mean) * rstd * gamma, rstd = 1 / sqrt(var + 1e-5); one warp per
 // row, two rows per iteration so that both rows' loads are in flight.
-template <int VPT, typename TO>
+template <int VPT, typename TO, typename TX>
 __device__ __forceinline__ void ln_fwd_row(const float4 (&v)[VPT], int lane, int D, const void* gamma, int gamma_f32,
-                                           TO* yr, float* mean_out, float* rstd_out, int row, float* xc) {
+                                           TO* yr, float* mean_out, float* rstd_out, int row, TX* xc) {
   if (xc) {
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
@@ -132,11 +132,13 @@ __device__ __forceinline__ void ln_fwd_row(const float4 (&v)[VPT], int lane, int
   }
 }
 
-template <int VPT, typename TO>
-__global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x, const void* __restrict__ gamma,
+// x (and its optional copy) is the residual stream: f32, or bf16 in a bf16
+// module, as the module computes it.
+template <int VPT, typename TX, typename TO>
+__global__ void __launch_bounds__(256) ln_fwd_kernel(const TX* __restrict__ x, const void* __restrict__ gamma,
                                                      int gamma_f32, TO* __restrict__ y, float* __restrict__ mean_out,
                                                      float* __restrict__ rstd_out, int rows, int D,
-                                                     float* __restrict__ x_copy) {
+                                                     TX* __restrict__ x_copy) {
   pdl_wait();
   pdl_trigger();
   const int warps = blockDim.x / 32;
@@ -152,11 +154,11 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
       v[j] = (c < D) ? load4(x + static_cast<long>(row) * D + c) : make_float4(0.f, 0.f, 0.f, 0.f);
       w[j] = (c < D && two) ? load4(x + static_cast<long>(row2) * D + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    ln_fwd_row<VPT, TO>(v, lane, D, gamma, gamma_f32, y + static_cast<long>(row) * D, mean_out, rstd_out, row,
-                        x_copy ? x_copy + static_cast<long>(row) * D : nullptr);
+    ln_fwd_row<VPT, TO, TX>(v, lane, D, gamma, gamma_f32, y + static_cast<long>(row) * D, mean_out, rstd_out, row,
+                            x_copy ? x_copy + static_cast<long>(row) * D : nullptr);
     if (two)
-      ln_fwd_row<VPT, TO>(w, lane, D, gamma, gamma_f32, y + static_cast<long>(row2) * D, mean_out, rstd_out, row2,
-                          x_copy ? x_copy + static_cast<long>(row2) * D : nullptr);
+      ln_fwd_row<VPT, TO, TX>(w, lane, D, gamma, gamma_f32, y + static_cast<long>(row2) * D, mean_out, rstd_out, row2,
+                              x_copy ? x_copy + static_cast<long>(row2) * D : nullptr);
   }
 }
 
@@ -170,8 +172,8 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
 template <int VPT>
 constexpr int ln_bwd_warps() { return VPT <= 3 ? 24 : 8; }
 
-template <int VPT, typename TI>
-__global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(const TI* __restrict__ dy, const float* __restrict__ x,
+template <int VPT, typename TI, typename TX>
+__global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(const TI* __restrict__ dy, const TX* __restrict__ x,
                                                         const float* __restrict__ mean_in,
                                                         const float* __restrict__ rstd_in,
                                                         const void* __restrict__ gamma, int gamma_f32,
@@ -265,11 +267,11 @@ __device__ __forceinline__ float block_sum_ordered(float v, float* red) {
   return t;
 }
 
-template <int CPT, typename TO>
-__global__ void __launch_bounds__(256) ln_fwd_wide_kernel(const float* __restrict__ x, const void* __restrict__ gamma,
+template <int CPT, typename TX, typename TO>
+__global__ void __launch_bounds__(256) ln_fwd_wide_kernel(const TX* __restrict__ x, const void* __restrict__ gamma,
                                                           int gamma_f32, TO* __restrict__ y,
                                                           float* __restrict__ mean_out, float* __restrict__ rstd_out,
-                                                          int rows, int D, float* __restrict__ x_copy) {
+                                                          int rows, int D, TX* __restrict__ x_copy) {
   pdl_wait();
   pdl_trigger();
   __shared__ float red1[32], red2[32];
@@ -325,8 +327,8 @@ __global__ void __launch_bounds__(256) ln_fwd_wide_kernel(const float* __restric
   }
 }
 
-template <int CPT, typename TI>
-__global__ void __launch_bounds__(256) ln_bwd_wide_kernel(const TI* __restrict__ dy, const float* __restrict__ x,
+template <int CPT, typename TI, typename TX>
+__global__ void __launch_bounds__(256) ln_bwd_wide_kernel(const TI* __restrict__ dy, const TX* __restrict__ x,
                                                           const float* __restrict__ mean_in,
                                                           const float* __restrict__ rstd_in,
                                                           const void* __restrict__ gamma, int gamma_f32,
@@ -678,12 +680,13 @@ __global__ void ce_finish_kernel(const float* __restrict__ part, int nparts, flo
 }
 
 // ---------------------------------------------------------------------------
-// Embedding: x[b*T+t, :] = wte[clamp(id)] + wpe[t]   (f32 residual stream)
+// Embedding: x[b*T+t, :] = wte[clamp(id)] + wpe[t]   (residual stream: f32,
+// or the bf16 sum a bf16 module computes)
 // ---------------------------------------------------------------------------
 
-template <typename TW>
+template <typename TW, typename TX>
 __global__ void embed_fwd_kernel(const float* __restrict__ ids, const TW* __restrict__ wte,
-                                 const TW* __restrict__ wpe, float* __restrict__ x, int ntok, int T, int V, int D) {
+                                 const TW* __restrict__ wpe, TX* __restrict__ x, int ntok, int T, int V, int D) {
   pdl_wait();
   pdl_trigger();
   const int warps = blockDim.x / 32;
@@ -693,7 +696,7 @@ __global__ void embed_fwd_kernel(const float* __restrict__ ids, const TW* __rest
     id = min(max(id, 0), V - 1);
     const TW* a = wte + static_cast<long>(id) * D;
     const TW* p = wpe + static_cast<long>(n % T) * D;
-    float* o = x + static_cast<long>(n) * D;
+    TX* o = x + static_cast<long>(n) * D;
     for (int c = lane * 4; c < D; c += 128) {
       const float4 u = load4(a + c), w = load4(p + c);
       store4(o + c, make_float4(u.x + w.x, u.y + w.y, u.z + w.z, u.w + w.w));
@@ -940,32 +943,37 @@ int ln_wide_grid(int rows) { return std::max(1, std::min(rows, 4 * num_sms_cache
     else return 1;                                         \
   } while (0)
 
-int layernorm_fwd(const float* x, const void* gamma, bool gamma_f32, void* y, bool y_f32, float* mean, float* rstd,
-                  int rows, int D, cudaStream_t s, float* x_copy) {
-  if (rows <= 0 || D <= 0 || (D & 3)) return 1;
+namespace {
+template <typename TX, typename TO>
+int layernorm_fwd_t(const TX* x, const void* gamma, bool gamma_f32, TO* y, float* mean, float* rstd, int rows, int D,
+                    cudaStream_t s, TX* x_copy) {
   if (D >= kLnWideMin) {
     const int nt = ln_wide_threads(D), grid = ln_wide_grid(rows);
-    if (y_f32)
-      SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_fwd_wide_kernel<C, float>), dim3(grid), dim3(nt), 0, s, x,
-                                                      gamma, gamma_f32, static_cast<float*>(y), mean, rstd, rows, D,
-                                                      x_copy)));
-    else
-      SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_fwd_wide_kernel<C, __nv_bfloat16>), dim3(grid), dim3(nt), 0,
-                                                      s, x, gamma, gamma_f32, static_cast<__nv_bfloat16*>(y), mean,
-                                                      rstd, rows, D, x_copy)));
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+    SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_fwd_wide_kernel<C, TX, TO>), dim3(grid), dim3(nt), 0, s, x,
+                                                    gamma, gamma_f32, y, mean, rstd, rows, D, x_copy)));
+  } else {
+    const int warps = 8;
+    const int grid = std::min((rows + 2 * warps - 1) / (2 * warps), 4 * num_sms_cached());
+    SB_LN_DISPATCH((D + 127) / 128, (launch_pdl((ln_fwd_kernel<V, TX, TO>), dim3(grid), dim3(warps * 32), 0, s, x,
+                                                gamma, gamma_f32, y, mean, rstd, rows, D, x_copy)));
   }
-  const int warps = 8;
-  const int grid = std::min((rows + 2 * warps - 1) / (2 * warps), 4 * num_sms_cached());
-  if (y_f32)
-    SB_LN_DISPATCH((D + 127) / 128, (launch_pdl((ln_fwd_kernel<V, float>), dim3(grid), dim3(warps * 32), 0, s, x,
-                                                gamma, gamma_f32, static_cast<float*>(y), mean, rstd, rows, D,
-                                                x_copy)));
-  else
-    SB_LN_DISPATCH((D + 127) / 128, (launch_pdl((ln_fwd_kernel<V, __nv_bfloat16>), dim3(grid), dim3(warps * 32), 0, s,
-                                                x, gamma, gamma_f32, static_cast<__nv_bfloat16*>(y), mean, rstd, rows,
-                                                D, x_copy)));
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+}  // namespace
+
+int layernorm_fwd(const void* x, bool x_f32, const void* gamma, bool gamma_f32, void* y, bool y_f32, float* mean,
+                  float* rstd, int rows, int D, cudaStream_t s, void* x_copy) {
+  if (rows <= 0 || D <= 0 || (D & 3)) return 1;
+  using bf = __nv_bfloat16;
+  if (x_f32) {
+    const float* xf = static_cast<const float*>(x);
+    float* cf = static_cast<float*>(x_copy);
+    return y_f32 ? layernorm_fwd_t(xf, gamma, gamma_f32, static_cast<float*>(y), mean, rstd, rows, D, s, cf)
+                 : layernorm_fwd_t(xf, gamma, gamma_f32, static_cast<bf*>(y), mean, rstd, rows, D, s, cf);
+  }
+  if (y_f32) return 1;  // a bf16 residual stream feeds bf16 outputs only
+  return layernorm_fwd_t(static_cast<const bf*>(x), gamma, gamma_f32, static_cast<bf*>(y), mean, rstd, rows, D, s,
+                         static_cast<bf*>(x_copy));
 }
 
 namespace {
@@ -979,20 +987,15 @@ size_t layernorm_bwd_workspace_bytes(int rows, int D) {
   return static_cast<size_t>(ln_bwd_grid(rows, ln_bwd_warps_for(D))) * D * sizeof(float);
 }
 
-int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean, const float* rstd, const void* gamma,
-                  bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma, bool dgamma_f32, float* ws,
-                  int rows, int D, cudaStream_t s) {
-  if (rows <= 0 || D <= 0 || (D & 3)) return 1;
+namespace {
+template <typename TI, typename TX>
+int layernorm_bwd_t(const TI* dy, const TX* x, const float* mean, const float* rstd, const void* gamma,
+                    bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma, bool dgamma_f32, float* ws,
+                    int rows, int D, cudaStream_t s) {
   if (D >= kLnWideMin) {
     const int nt = ln_wide_threads(D), grid = ln_wide_grid(rows);
-    if (dy_f32)
-      SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, float>), dim3(grid), dim3(nt), 0, s,
-                                                      static_cast<const float*>(dy), x, mean, rstd, gamma, gamma_f32,
-                                                      dres, dres_bf, ws, rows, D)));
-    else
-      SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, __nv_bfloat16>), dim3(grid), dim3(nt), 0,
-                                                      s, static_cast<const __nv_bfloat16*>(dy), x, mean, rstd, gamma,
-                                                      gamma_f32, dres, dres_bf, ws, rows, D)));
+    SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, TI, TX>), dim3(grid), dim3(nt), 0, s, dy,
+                                                    x, mean, rstd, gamma, gamma_f32, dres, dres_bf, ws, rows, D)));
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
     return column_sum(ws, grid, D, dgamma, dgamma_f32, s);
   }
@@ -1000,22 +1003,32 @@ int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean
   const int grid = ln_bwd_grid(rows, warps);
   const size_t smem = static_cast<size_t>(warps) * D * sizeof(float);
   if (smem > 200 * 1024) return 1;
-  if (dy_f32)
-    SB_LN_DISPATCH((D + 127) / 128, ({
-      auto k = ln_bwd_kernel<V, float>;
-      if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, static_cast<const float*>(dy), x, mean, rstd, gamma,
-                 gamma_f32, dres, dres_bf, ws, rows, D);
-    }));
-  else
-    SB_LN_DISPATCH((D + 127) / 128, ({
-      auto k = ln_bwd_kernel<V, __nv_bfloat16>;
-      if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, static_cast<const __nv_bfloat16*>(dy), x, mean, rstd,
-                 gamma, gamma_f32, dres, dres_bf, ws, rows, D);
-    }));
+  SB_LN_DISPATCH((D + 127) / 128, ({
+    auto k = ln_bwd_kernel<V, TI, TX>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, dy, x, mean, rstd, gamma, gamma_f32, dres, dres_bf, ws, rows,
+               D);
+  }));
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
   return column_sum(ws, grid, D, dgamma, dgamma_f32, s);
+}
+}  // namespace
+
+int layernorm_bwd(const void* dy, bool dy_f32, const void* x, bool x_f32, const float* mean, const float* rstd,
+                  const void* gamma, bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma,
+                  bool dgamma_f32, float* ws, int rows, int D, cudaStream_t s) {
+  if (rows <= 0 || D <= 0 || (D & 3)) return 1;
+  using bf = __nv_bfloat16;
+  if (x_f32) {
+    const float* xf = static_cast<const float*>(x);
+    return dy_f32 ? layernorm_bwd_t(static_cast<const float*>(dy), xf, mean, rstd, gamma, gamma_f32, dres, dres_bf,
+                                    dgamma, dgamma_f32, ws, rows, D, s)
+                  : layernorm_bwd_t(static_cast<const bf*>(dy), xf, mean, rstd, gamma, gamma_f32, dres, dres_bf, dgamma,
+                                    dgamma_f32, ws, rows, D, s);
+  }
+  if (dy_f32) return 1;  // a bf16 residual stream comes with bf16 gradients
+  return layernorm_bwd_t(static_cast<const bf*>(dy), static_cast<const bf*>(x), mean, rstd, gamma, gamma_f32, dres,
+                         dres_bf, dgamma, dgamma_f32, ws, rows, D, s);
 }
 
 // Same VJP with the number of blocks capped at `max_blocks`, so that the
@@ -1026,7 +1039,7 @@ int layernorm_bwd_capped(const float* dy, const float* x, const float* mean, con
   if (rows <= 0 || D <= 0 || (D & 3) || max_blocks <= 0) return 1;
   if (D >= kLnWideMin) {  // the kernel layernorm_bwd uses at this width, on fewer blocks
     const int nt = ln_wide_threads(D), grid = std::min(ln_wide_grid(rows), max_blocks);
-    SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, float>), dim3(grid), dim3(nt), 0, s, dy, x,
+    SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, float, float>), dim3(grid), dim3(nt), 0, s, dy, x,
                                                     mean, rstd, gamma, gamma_f32, dres, nullptr, scratch, rows, D)));
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
     return column_sum(scratch, grid, D, dgamma, dgamma_f32, s);
@@ -1036,7 +1049,7 @@ int layernorm_bwd_capped(const float* dy, const float* x, const float* mean, con
   const size_t smem = static_cast<size_t>(warps) * D * sizeof(float);
   if (smem > 200 * 1024) return 1;
   SB_LN_DISPATCH((D + 127) / 128, ({
-    auto k = ln_bwd_kernel<V, float>;
+    auto k = ln_bwd_kernel<V, float, float>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, dy, x, mean, rstd, gamma, gamma_f32, dres, nullptr, scratch,
                rows, D);
@@ -1078,16 +1091,22 @@ int cross_entropy_fwd_bwd(const void* logits, bool f32, long ld, int rows, int V
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
-int embedding_fwd(const float* ids, const void* wte, const void* wpe, bool f32, float* x, int ntok, int T, int V,
-                  int D, cudaStream_t s) {
+int embedding_fwd(const float* ids, const void* wte, const void* wpe, bool f32, void* x, bool x_f32, int ntok, int T,
+                  int V, int D, cudaStream_t s) {
   if (ntok <= 0 || (D & 3)) return 1;
+  using bf = __nv_bfloat16;
   const int grid = std::min((ntok + 7) / 8, 8 * num_sms_cached());
-  if (f32)
-    launch_pdl((embed_fwd_kernel<float>), dim3(grid), dim3(256), 0, s, ids, static_cast<const float*>(wte),
-               static_cast<const float*>(wpe), x, ntok, T, V, D);
+  if (f32 && x_f32)
+    launch_pdl((embed_fwd_kernel<float, float>), dim3(grid), dim3(256), 0, s, ids, static_cast<const float*>(wte),
+               static_cast<const float*>(wpe), static_cast<float*>(x), ntok, T, V, D);
+  else if (!f32 && x_f32)
+    launch_pdl((embed_fwd_kernel<bf, float>), dim3(grid), dim3(256), 0, s, ids, static_cast<const bf*>(wte),
+               static_cast<const bf*>(wpe), static_cast<float*>(x), ntok, T, V, D);
+  else if (!f32)
+    launch_pdl((embed_fwd_kernel<bf, bf>), dim3(grid), dim3(256), 0, s, ids, static_cast<const bf*>(wte),
+               static_cast<const bf*>(wpe), static_cast<bf*>(x), ntok, T, V, D);
   else
-    launch_pdl((embed_fwd_kernel<__nv_bfloat16>), dim3(grid), dim3(256), 0, s, ids,
-               static_cast<const __nv_bfloat16*>(wte), static_cast<const __nv_bfloat16*>(wpe), x, ntok, T, V, D);
+    return 1;  // f32 tables feed an f32 residual stream
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 

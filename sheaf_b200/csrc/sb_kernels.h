@@ -13,7 +13,7 @@ enum EpiKind : int {
   EPI_ADD = 1,       // out = acc + aux            (aux may alias out; f32 only)
   EPI_GELU = 2,      // u = acc; out = gelu(u); out2 = gelu'(u)  (out2 feeds EPI_MUL in the VJP)
   EPI_MUL = 3,       // out = acc * aux            (aux = gelu'(u) saved by EPI_GELU)
-  EPI_ACCUM = 4,     // out += acc                 (f32 out; no split-K)
+  EPI_ACCUM = 4,     // out += acc                 (f32 or bf16 out; no split-K)
 };
 
 // C[M,N] = A[M,K] * B[N,K]^T with either operand stored K-major (rows of K)

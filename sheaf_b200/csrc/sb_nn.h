@@ -16,16 +16,18 @@ constexpr int kEmbedSmallVocab = 4096;
 int num_sms_cached();
 int* device_error_word();
 
-// y = (x - mean) / sqrt(var + 1e-5) * gamma over the last dim (rows x D, f32 in).
-// x_copy (optional, f32 [rows, D]) receives a copy of x: the base that a
-// following residual GEMM accumulates into (EPI_ACCUM).
-int layernorm_fwd(const float* x, const void* gamma, bool gamma_f32, void* y, bool y_f32, float* mean, float* rstd,
-                  int rows, int D, cudaStream_t s, float* x_copy = nullptr);
+// y = (x - mean) / sqrt(var + 1e-5) * gamma over the last dim (rows x D).
+// x is the residual stream, f32 (x_f32) or bf16; a bf16 x takes a bf16 y.
+// x_copy (optional, x's type, [rows, D]) receives a copy of x: the base that
+// a following residual GEMM accumulates into (EPI_ACCUM).
+int layernorm_fwd(const void* x, bool x_f32, const void* gamma, bool gamma_f32, void* y, bool y_f32, float* mean,
+                  float* rstd, int rows, int D, cudaStream_t s, void* x_copy = nullptr);
 // dres += LN-VJP(dy); dres_bf (optional) = bf16(dres); dgamma = sum_rows dy * xhat.
+// x f32 (x_f32) or bf16; a bf16 x takes a bf16 dy.
 size_t layernorm_bwd_workspace_bytes(int rows, int D);
-int layernorm_bwd(const void* dy, bool dy_f32, const float* x, const float* mean, const float* rstd, const void* gamma,
-                  bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma, bool dgamma_f32, float* ws,
-                  int rows, int D, cudaStream_t s);
+int layernorm_bwd(const void* dy, bool dy_f32, const void* x, bool x_f32, const float* mean, const float* rstd,
+                  const void* gamma, bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma,
+                  bool dgamma_f32, float* ws, int rows, int D, cudaStream_t s);
 
 // layernorm_bwd (f32 dy) with at most `max_blocks` blocks; `scratch` holds
 // max_blocks * D floats of dgamma partials.
@@ -38,9 +40,10 @@ size_t cross_entropy_workspace_bytes(int rows);
 int cross_entropy_fwd_bwd(const void* logits, bool f32, long ld, int rows, int V, const float* targets, void* dlogits,
                           long ldd, float* ws, float* loss_f32, __nv_bfloat16* loss_bf16, cudaStream_t s);
 
-// x[b*T+t] = wte[clamp(ids)] + wpe[t] (f32 out).
-int embedding_fwd(const float* ids, const void* wte, const void* wpe, bool f32, float* x, int ntok, int T, int V, int D,
-                  cudaStream_t s);
+// x[b*T+t] = wte[clamp(ids)] + wpe[t]: tables f32 (f32) or bf16; x f32
+// (x_f32) or, from bf16 tables, the bf16-rounded sum.
+int embedding_fwd(const float* ids, const void* wte, const void* wpe, bool f32, void* x, bool x_f32, int ntok, int T,
+                  int V, int D, cudaStream_t s);
 // dwte = scatter-add of dx rows by id; dwpe[t] = sum_b dx[b,t] (rows >= T zero).
 size_t embedding_bwd_workspace_bytes(int V, int D);
 int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V, int D, void* dwte, void* dwpe,
