@@ -116,7 +116,7 @@ int sb_op_layernorm_bwd(uint32_t elem, const void* dy, const void* x, const void
   if (workspace_bytes < sb::layernorm_bwd_workspace_bytes(rows, d) || !workspace) return SB_OPERR_WORKSPACE;
   const bool f = elem == SB_ELEM_F32;
   return sb::layernorm_bwd(dy, true, x, true, static_cast<const float*>(mean),
-                           static_cast<const float*>(rstd), gamma, f, static_cast<float*>(dres), nullptr, dgamma, f,
+                           static_cast<const float*>(rstd), gamma, f, dres, dres, dgamma, f,
                            static_cast<float*>(workspace), rows, d, static_cast<cudaStream_t>(stream));
 }
 
@@ -155,7 +155,7 @@ int sb_op_embedding_bwd(uint32_t elem, const void* ids, const void* dx, int32_t 
                         int32_t d, void* dwte, void* dwpe, void* workspace, size_t workspace_bytes, void* stream) {
   if (!float_elem(elem) || !ids || !dx || !dwte || !dwpe || p < t) return SB_OPERR_ARGS;
   if (workspace_bytes < sb::embedding_bwd_workspace_bytes(v, d)) return SB_OPERR_WORKSPACE;
-  return sb::embedding_bwd(static_cast<const float*>(ids), static_cast<const float*>(dx), b, t, p, v, d, dwte, dwpe,
+  return sb::embedding_bwd(static_cast<const float*>(ids), dx, true, b, t, p, v, d, dwte, dwpe,
                            elem == SB_ELEM_F32, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream));
 }
 

@@ -89,6 +89,8 @@ class GptVagModule : public Module {
   float *meanf = nullptr, *rstdf = nullptr;
   std::vector<void*> h1, h2, qkv, att, gder, gact;  // gder = gelu'(u) saved for the VJP
   void *hf = nullptr, *logits = nullptr, *dlogits = nullptr;
+  // gradient of the residual stream: f32, updated in place (f32 module), or
+  // two bf16 buffers the layer-norm VJPs read and write in turn (bf16)
   float* dres = nullptr;
   void* dres_bf = nullptr;
   void* dh = nullptr;  // dy of the layer-norm VJPs, model element type (as the module materialises it)
@@ -136,7 +138,7 @@ class GptVagModule : public Module {
   // bf16 backward: the weight-gradient GEMMs run on a low-priority side
   // stream beside the critical path (dX GEMMs, layer-norm and attention
   // VJPs), filling the SMs its tails leave idle. The operands they read are
-  // double-buffered (dres copy by writer, dU and dqkv by layer parity) so the
+  // double-buffered (residual gradient by writer, dU and dqkv by layer parity) so the
   // critical path only waits for a dW GEMM before overwriting its operand.
   bool dw_side = false;
   cudaStream_t wst = nullptr;
@@ -369,8 +371,12 @@ class GptVagModule : public Module {
     SB_TRY(dev(static_cast<size_t>(N) * ldl * es, &dlogits));
     cudaMemset(logits, 0, static_cast<size_t>(N) * ldl * es);
     cudaMemset(dlogits, 0, static_cast<size_t>(N) * ldl * es);
-    SB_TRY(devt(nd, &dres));
-    if (bf) SB_TRY(dev(nd * 2, &dres_bf));
+    if (bf) {
+      SB_TRY(dev(nd * 2, &dres_bf));
+      SB_TRY(dev(nd * 2, &dres_bf2));
+    } else {
+      SB_TRY(devt(nd, &dres));
+    }
     SB_TRY(dev(nd * es, &dh));
     SB_TRY(dev(4 * nd * es, &du));
     SB_TRY(dev(nd * es, &dout));
@@ -401,7 +407,6 @@ class GptVagModule : public Module {
         if (d.K == N) w2 = std::max(w2, gemm_workspace_bytes(d, bf));  // the dW GEMMs contract over tokens
       ws_w_bytes = align256(w2);
       SB_TRY(devt(ws_w_bytes / 4 + 64, &ws_w));
-      SB_TRY(dev(nd * 2, &dres_bf2));
       SB_TRY(dev(4 * nd * es, &du2));
       SB_TRY(dev(3 * nd * es, &dqkv2));
       for (int i = 0; i < 8 * L + 8; ++i) {
@@ -521,10 +526,11 @@ class GptVagModule : public Module {
     // ---- backward
     SB_K(gemm(desc(dlogits, ldl, false, Pp(0), D, true, N, D, V, dh, D, f32), st, err));
     SB_K(gemm(desc(dlogits, ldl, true, hf, D, true, V, D, N, Gp(0), D, f32), st, err));
-    if (cudaMemsetAsync(dres, 0, static_cast<size_t>(N) * D * sizeof(float), st) != cudaSuccess)
-      return make_status(SB_STATUS_INTERNAL, "memset failed");
-    SB_K(layernorm_bwd(dh, f32, xs[L], f32, meanf, rstdf, Pp(ilnf), f32, dres, static_cast<__nv_bfloat16*>(dres_bf),
-                       Gp(ilnf), f32, ws, N, D, st));
+    // residual-stream gradient buffers: r0 is written by the LN_f and LN1
+    // VJPs, r1 by LN2's (the same f32 buffer in an f32 module)
+    void* r0 = bf ? dres_bf : static_cast<void*>(dres);
+    void* r1 = bf ? dres_bf2 : r0;
+    SB_K(layernorm_bwd(dh, f32, xs[L], f32, meanf, rstdf, Pp(ilnf), f32, nullptr, r0, Gp(ilnf), f32, ws, N, D, st));
     int bucket = 0;
     // the all-reduce of a bucket waits for the main stream and, when given,
     // a side-stream mark
@@ -558,10 +564,6 @@ class GptVagModule : public Module {
       if (dw_side && e) SB_CUDA_TRY(cudaStreamWaitEvent(st, e, 0));
       return nullptr;
     };
-    // dres operand of the GEMMs: r0 is written by LN_f / LN1 VJPs, r1 by LN2's
-    const void* r0 = bf ? dres_bf : static_cast<void*>(dres);
-    const void* r1 = dw_side ? dres_bf2 : r0;
-    auto bf_out = [&](const void* p) { return bf ? static_cast<__nv_bfloat16*>(const_cast<void*>(p)) : nullptr; };
     std::vector<cudaEvent_t> ev_fc2(L, nullptr), ev_fc(L, nullptr), ev_proj(L, nullptr), ev_qkv(L, nullptr);
     for (int l = L - 1; l >= 0; --l) {
       const int b0 = 1 + 6 * l;
@@ -584,7 +586,7 @@ class GptVagModule : public Module {
       SB_TRY(mark(ev_fc[l]));
       SB_K(gemm(desc(dul, 4 * D, false, Pp(b0 + 4), D, true, N, D, 4 * D, dh, D, f32), st, err));
       if (l + 1 < L) SB_TRY(wait(ev_proj[l + 1]));  // r1 last read by dW_proj one layer up
-      SB_K(layernorm_bwd(dh, f32, xmid[l], f32, mean2[l], rstd2[l], Pp(b0 + 3), f32, dres, bf_out(r1), Gp(b0 + 3), f32,
+      SB_K(layernorm_bwd(dh, f32, xmid[l], f32, mean2[l], rstd2[l], Pp(b0 + 3), f32, r0, r1, Gp(b0 + 3), f32,
                          ws, N, D, st));
       SB_TRY(fork());
       SB_K(gemm(desc(r1, D, true, att[l], D, true, D, D, N, Gp(b0 + 1), D, f32), sst, err, dw_side));
@@ -597,7 +599,7 @@ class GptVagModule : public Module {
       SB_TRY(mark(ev_qkv[l]));
       SB_K(gemm(desc(dql, 3 * D, false, Pp(b0 + 0), D, true, N, D, 3 * D, dh, D, f32), st, err));
       SB_TRY(wait(ev_fc2[l]));  // r0 last read by dW_fc2 of this layer
-      SB_K(layernorm_bwd(dh, f32, xs[l], f32, mean1[l], rstd1[l], Pp(b0 + 2), f32, dres, bf_out(r0), Gp(b0 + 2), f32, ws,
+      SB_K(layernorm_bwd(dh, f32, xs[l], f32, mean1[l], rstd1[l], Pp(b0 + 2), f32, r1, r0, Gp(b0 + 2), f32, ws,
                          N, D, st));
       // layer l's six gradients (plus ln_f after the last layer) are final
       SB_TRY(launch_bucket(offs[b0], l == L - 1 ? offs[ip] : offs[b0 + 6], ev_qkv[l]));
@@ -609,13 +611,13 @@ class GptVagModule : public Module {
     }
     if (onehot) {
       // the reference's one-hot matmul (reverse.rs:1108-1121) on the tensor
-      // cores: dwte = one_hot(x)^T [V, N] x dres (bf16 copy) [N, D], the
-      // shape of the head's weight gradient
+      // cores: dwte = one_hot(x)^T [V, N] x dres (bf16) [N, D], the shape
+      // of the head's weight gradient
       SB_K(embedding_onehot(ids, N, V, ldl, onehot, st));
       SB_K(gemm(desc(onehot, ldl, true, r0, D, true, V, D, N, Gp(iw), D, false), st, err));
-      SB_K(embedding_pos_bwd(dres, B, T, P, D, Gp(ip), false, st));
+      SB_K(embedding_pos_bwd(r0, f32, B, T, P, D, Gp(ip), false, st));
     } else {
-      SB_K(embedding_bwd(ids, dres, B, T, P, V, D, Gp(iw), Gp(ip), f32, ws, st));
+      SB_K(embedding_bwd(ids, r0, f32, B, T, P, V, D, Gp(iw), Gp(ip), f32, ws, st));
     }
     SB_TRY(launch_bucket(offs[ip], grads_bytes, nullptr));
     if (dp) {

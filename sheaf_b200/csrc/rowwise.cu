@@ -163,8 +163,10 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const TX* __restrict__ x, c
 }
 
 // dx = rstd * (dxh - mean(dxh) - xhat * mean(dxh * xhat)), dxh = dy * gamma.
-// dres (f32) += dx; optional bf16 copy of the updated dres; per-block partial
-// sums of dgamma = sum_rows dy * xhat into dgamma_part[blockIdx.x][D].
+// dres_out = dres_in + dx (the residual stream's gradient, in the type of x:
+// f32, or bf16 rounded once per add in a bf16 module; dres_in may be null
+// for zero, or alias dres_out); per-block partial sums of
+// dgamma = sum_rows dy * xhat into dgamma_part[blockIdx.x][D].
 // x, dy and dres of a row are loaded together (the dres read does not wait
 // for the row reductions); gamma is re-read from L1 per row to keep the
 // register count low. Rows up to 384 wide run 24 warps per block, one block
@@ -177,7 +179,7 @@ __global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(con
                                                         const float* __restrict__ mean_in,
                                                         const float* __restrict__ rstd_in,
                                                         const void* __restrict__ gamma, int gamma_f32,
-                                                        float* __restrict__ dres, __nv_bfloat16* __restrict__ dres_bf,
+                                                        const TX* dres_in, TX* dres_out,
                                                         float* __restrict__ dgamma_part, int rows, int D) {
   pdl_wait();
   pdl_trigger();
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(con
       const bool in = c < D;
       xh[j] = in ? load4(x + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
       dxh[j] = in ? load4(dy + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      r[j] = in ? load4(dres + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      r[j] = (in && dres_in) ? load4(dres_in + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
@@ -228,8 +230,7 @@ __global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(con
         r[j].y += rstd * (dxh[j].y - c1 - xh[j].y * c2);
         r[j].z += rstd * (dxh[j].z - c1 - xh[j].z * c2);
         r[j].w += rstd * (dxh[j].w - c1 - xh[j].w * c2);
-        store4(dres + off + c, r[j]);
-        if (dres_bf) store4(dres_bf + off + c, r[j]);
+        store4(dres_out + off + c, r[j]);
       }
     }
   }
@@ -332,7 +333,7 @@ __global__ void __launch_bounds__(256) ln_bwd_wide_kernel(const TI* __restrict__
                                                           const float* __restrict__ mean_in,
                                                           const float* __restrict__ rstd_in,
                                                           const void* __restrict__ gamma, int gamma_f32,
-                                                          float* __restrict__ dres, __nv_bfloat16* __restrict__ dres_bf,
+                                                          const TX* dres_in, TX* dres_out,
                                                           float* __restrict__ dgamma_part, int rows, int D) {
   pdl_wait();
   pdl_trigger();
@@ -357,7 +358,7 @@ __global__ void __launch_bounds__(256) ln_bwd_wide_kernel(const TI* __restrict__
       const bool in = c < D;
       xh[j] = in ? load4(x + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
       dxh[j] = in ? load4(dy + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      r[j] = in ? load4(dres + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      r[j] = (in && dres_in) ? load4(dres_in + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
@@ -385,8 +386,7 @@ __global__ void __launch_bounds__(256) ln_bwd_wide_kernel(const TI* __restrict__
         r[j].y += rstd * (dxh[j].y - c1 - xh[j].y * c2);
         r[j].z += rstd * (dxh[j].z - c1 - xh[j].z * c2);
         r[j].w += rstd * (dxh[j].w - c1 - xh[j].w * c2);
-        store4(dres + off + c, r[j]);
-        if (dres_bf) store4(dres_bf + off + c, r[j]);
+        store4(dres_out + off + c, r[j]);
       }
     }
   }
@@ -708,7 +708,8 @@ __global__ void embed_fwd_kernel(const float* __restrict__ ids, const TW* __rest
 // [b*chunk, (b+1)*chunk) in order into a private [V, D] copy in shared memory
 // (thread = column, so no two threads touch one word), then writes it to
 // part[b]; the partials are summed in block order by column_sum.
-__global__ void embed_bwd_priv_kernel(const float* __restrict__ ids, const float* __restrict__ dx, int ntok, int V,
+template <typename TD>
+__global__ void embed_bwd_priv_kernel(const float* __restrict__ ids, const TD* __restrict__ dx, int ntok, int V,
                                       int D, int chunk, float* __restrict__ part) {
   pdl_wait();
   pdl_trigger();
@@ -725,7 +726,7 @@ __global__ void embed_bwd_priv_kernel(const float* __restrict__ ids, const float
     for (int u = 0; u < 8; ++u) {
       const int tt = t + u;
       id[u] = (tt < t1) ? one_hot_class(ids[tt], V) : -1;
-      g[u] = (tt < t1 && c < D) ? dx[static_cast<long>(tt) * D + c] : 0.f;
+      g[u] = (tt < t1 && c < D) ? load1(dx + static_cast<long>(tt) * D + c) : 0.f;
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u)
@@ -739,7 +740,8 @@ __global__ void embed_bwd_priv_kernel(const float* __restrict__ ids, const float
 constexpr int kEmbedPrivBlocks = 148;
 
 // dwte for a large vocabulary: fp32 atomics into a zeroed f32 accumulator.
-__global__ void embed_bwd_atomic_kernel(const float* __restrict__ ids, const float* __restrict__ dx, int ntok, int V,
+template <typename TD>
+__global__ void embed_bwd_atomic_kernel(const float* __restrict__ ids, const TD* __restrict__ dx, int ntok, int V,
                                         int D, float* __restrict__ acc) {
   pdl_wait();
   pdl_trigger();
@@ -748,9 +750,9 @@ __global__ void embed_bwd_atomic_kernel(const float* __restrict__ ids, const flo
   for (int n = blockIdx.x * warps + threadIdx.x / 32; n < ntok; n += gridDim.x * warps) {
     const int id = one_hot_class(ids[n], V);
     if (id < 0) continue;
-    const float* g = dx + static_cast<long>(n) * D;
+    const TD* g = dx + static_cast<long>(n) * D;
     float* o = acc + static_cast<long>(id) * D;
-    for (int c = lane; c < D; c += 32) atomicAdd(o + c, g[c]);
+    for (int c = lane; c < D; c += 32) atomicAdd(o + c, load1(g + c));
   }
 }
 
@@ -771,7 +773,8 @@ __global__ void onehot_kernel(const float* __restrict__ ids, int ntok, int V, in
 }
 
 // dwpe[t, :] = sum_b dx[b*T + t, :] for t < T; rows T..P-1 are zero (pad).
-__global__ void embed_bwd_pos_kernel(const float* __restrict__ dx, int B, int T, int P, int D, void* dwpe,
+template <typename TD>
+__global__ void embed_bwd_pos_kernel(const TD* __restrict__ dx, int B, int T, int P, int D, void* dwpe,
                                      int out_f32) {
   pdl_wait();
   pdl_trigger();
@@ -786,11 +789,11 @@ __global__ void embed_bwd_pos_kernel(const float* __restrict__ dx, int B, int T,
       for (; b + 8 <= B; b += 8) {
         float v[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = dx[(static_cast<long>(b + u) * T + t) * D + c];
+        for (int u = 0; u < 8; ++u) v[u] = load1(dx + (static_cast<long>(b + u) * T + t) * D + c);
 #pragma unroll
         for (int u = 0; u < 8; ++u) acc += v[u];
       }
-      for (; b < B; ++b) acc += dx[(static_cast<long>(b) * T + t) * D + c];
+      for (; b < B; ++b) acc += load1(dx + (static_cast<long>(b) * T + t) * D + c);
     }
     if (out_f32)
       static_cast<float*>(dwpe)[i] = acc;
@@ -990,12 +993,12 @@ size_t layernorm_bwd_workspace_bytes(int rows, int D) {
 namespace {
 template <typename TI, typename TX>
 int layernorm_bwd_t(const TI* dy, const TX* x, const float* mean, const float* rstd, const void* gamma,
-                    bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma, bool dgamma_f32, float* ws,
+                    bool gamma_f32, const TX* dres_in, TX* dres_out, void* dgamma, bool dgamma_f32, float* ws,
                     int rows, int D, cudaStream_t s) {
   if (D >= kLnWideMin) {
     const int nt = ln_wide_threads(D), grid = ln_wide_grid(rows);
     SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, TI, TX>), dim3(grid), dim3(nt), 0, s, dy,
-                                                    x, mean, rstd, gamma, gamma_f32, dres, dres_bf, ws, rows, D)));
+                                                    x, mean, rstd, gamma, gamma_f32, dres_in, dres_out, ws, rows, D)));
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
     return column_sum(ws, grid, D, dgamma, dgamma_f32, s);
   }
@@ -1006,8 +1009,8 @@ int layernorm_bwd_t(const TI* dy, const TX* x, const float* mean, const float* r
   SB_LN_DISPATCH((D + 127) / 128, ({
     auto k = ln_bwd_kernel<V, TI, TX>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, dy, x, mean, rstd, gamma, gamma_f32, dres, dres_bf, ws, rows,
-               D);
+    launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, dy, x, mean, rstd, gamma, gamma_f32, dres_in, dres_out, ws,
+               rows, D);
   }));
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
   return column_sum(ws, grid, D, dgamma, dgamma_f32, s);
@@ -1015,20 +1018,23 @@ int layernorm_bwd_t(const TI* dy, const TX* x, const float* mean, const float* r
 }  // namespace
 
 int layernorm_bwd(const void* dy, bool dy_f32, const void* x, bool x_f32, const float* mean, const float* rstd,
-                  const void* gamma, bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma,
+                  const void* gamma, bool gamma_f32, const void* dres_in, void* dres_out, void* dgamma,
                   bool dgamma_f32, float* ws, int rows, int D, cudaStream_t s) {
-  if (rows <= 0 || D <= 0 || (D & 3)) return 1;
+  if (rows <= 0 || D <= 0 || (D & 3) || !dres_out) return 1;
   using bf = __nv_bfloat16;
   if (x_f32) {
     const float* xf = static_cast<const float*>(x);
-    return dy_f32 ? layernorm_bwd_t(static_cast<const float*>(dy), xf, mean, rstd, gamma, gamma_f32, dres, dres_bf,
-                                    dgamma, dgamma_f32, ws, rows, D, s)
-                  : layernorm_bwd_t(static_cast<const bf*>(dy), xf, mean, rstd, gamma, gamma_f32, dres, dres_bf, dgamma,
+    const float* ri = static_cast<const float*>(dres_in);
+    float* ro = static_cast<float*>(dres_out);
+    return dy_f32 ? layernorm_bwd_t(static_cast<const float*>(dy), xf, mean, rstd, gamma, gamma_f32, ri, ro, dgamma,
+                                    dgamma_f32, ws, rows, D, s)
+                  : layernorm_bwd_t(static_cast<const bf*>(dy), xf, mean, rstd, gamma, gamma_f32, ri, ro, dgamma,
                                     dgamma_f32, ws, rows, D, s);
   }
   if (dy_f32) return 1;  // a bf16 residual stream comes with bf16 gradients
-  return layernorm_bwd_t(static_cast<const bf*>(dy), static_cast<const bf*>(x), mean, rstd, gamma, gamma_f32, dres,
-                         dres_bf, dgamma, dgamma_f32, ws, rows, D, s);
+  return layernorm_bwd_t(static_cast<const bf*>(dy), static_cast<const bf*>(x), mean, rstd, gamma, gamma_f32,
+                         static_cast<const bf*>(dres_in), static_cast<bf*>(dres_out), dgamma, dgamma_f32, ws, rows, D,
+                         s);
 }
 
 // Same VJP with the number of blocks capped at `max_blocks`, so that the
@@ -1040,7 +1046,7 @@ int layernorm_bwd_capped(const float* dy, const float* x, const float* mean, con
   if (D >= kLnWideMin) {  // the kernel layernorm_bwd uses at this width, on fewer blocks
     const int nt = ln_wide_threads(D), grid = std::min(ln_wide_grid(rows), max_blocks);
     SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, float, float>), dim3(grid), dim3(nt), 0, s, dy, x,
-                                                    mean, rstd, gamma, gamma_f32, dres, nullptr, scratch, rows, D)));
+                                                    mean, rstd, gamma, gamma_f32, dres, dres, scratch, rows, D)));
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
     return column_sum(scratch, grid, D, dgamma, dgamma_f32, s);
   }
@@ -1051,7 +1057,7 @@ int layernorm_bwd_capped(const float* dy, const float* x, const float* mean, con
   SB_LN_DISPATCH((D + 127) / 128, ({
     auto k = ln_bwd_kernel<V, float, float>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, dy, x, mean, rstd, gamma, gamma_f32, dres, nullptr, scratch,
+    launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, dy, x, mean, rstd, gamma, gamma_f32, dres, dres, scratch,
                rows, D);
   }));
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
@@ -1117,25 +1123,28 @@ size_t embedding_bwd_workspace_bytes(int V, int D) {
                            : static_cast<size_t>(V) * D * sizeof(float);
 }
 
-int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V, int D, void* dwte, void* dwpe,
-                  bool out_f32, float* ws, cudaStream_t s) {
+namespace {
+template <typename TD>
+int embedding_bwd_t(const float* ids, const TD* dx, int B, int T, int P, int V, int D, void* dwte, void* dwpe,
+                    bool out_f32, float* ws, cudaStream_t s) {
   const int ntok = B * T;
   if (embed_small(V, D)) {
     if (!ws) return 5;
     const int chunk = (ntok + kEmbedPrivBlocks - 1) / kEmbedPrivBlocks;
     const size_t smem = static_cast<size_t>(V) * D * sizeof(float);
     if (smem > 48 * 1024)
-      cudaFuncSetAttribute(embed_bwd_priv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    launch_pdl(embed_bwd_priv_kernel, dim3(kEmbedPrivBlocks), dim3((D + 31) / 32 * 32), smem, s, ids, dx, ntok, V, D,
-               chunk, ws);
+      cudaFuncSetAttribute(embed_bwd_priv_kernel<TD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem));
+    launch_pdl(embed_bwd_priv_kernel<TD>, dim3(kEmbedPrivBlocks), dim3((D + 31) / 32 * 32), smem, s, ids, dx, ntok, V,
+               D, chunk, ws);
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
     if (column_sum(ws, kEmbedPrivBlocks, static_cast<long>(V) * D, dwte, out_f32, s)) return 4;
   } else {
     float* acc = out_f32 ? static_cast<float*>(dwte) : ws;
     if (!acc) return 5;
     cudaMemsetAsync(acc, 0, static_cast<size_t>(V) * D * sizeof(float), s);
-    launch_pdl(embed_bwd_atomic_kernel, dim3(std::min((ntok + 7) / 8, 8 * num_sms_cached())), dim3(256), 0, s, ids,
-               dx, ntok, V, D, acc);
+    launch_pdl(embed_bwd_atomic_kernel<TD>, dim3(std::min((ntok + 7) / 8, 8 * num_sms_cached())), dim3(256), 0, s,
+               ids, dx, ntok, V, D, acc);
     if (!out_f32) {
       const long n = static_cast<long>(V) * D;
       launch_pdl(convert_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, acc, static_cast<__nv_bfloat16*>(dwte), n);
@@ -1143,8 +1152,17 @@ int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V,
   }
   if (cudaPeekAtLastError() != cudaSuccess) return 4;
   const long total = static_cast<long>(P) * D;
-  launch_pdl(embed_bwd_pos_kernel, dim3(grid_for(total, 256)), dim3(256), 0, s, dx, B, T, P, D, dwpe, out_f32);
+  launch_pdl(embed_bwd_pos_kernel<TD>, dim3(grid_for(total, 256)), dim3(256), 0, s, dx, B, T, P, D, dwpe,
+             static_cast<int>(out_f32));
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
+}
+}  // namespace
+
+int embedding_bwd(const float* ids, const void* dx, bool dx_f32, int B, int T, int P, int V, int D, void* dwte,
+                  void* dwpe, bool out_f32, float* ws, cudaStream_t s) {
+  return dx_f32 ? embedding_bwd_t(ids, static_cast<const float*>(dx), B, T, P, V, D, dwte, dwpe, out_f32, ws, s)
+                : embedding_bwd_t(ids, static_cast<const __nv_bfloat16*>(dx), B, T, P, V, D, dwte, dwpe, out_f32, ws,
+                                  s);
 }
 
 int embedding_onehot(const float* ids, int ntok, int V, int Vp, __nv_bfloat16* out, cudaStream_t s) {
@@ -1154,9 +1172,15 @@ int embedding_onehot(const float* ids, int ntok, int V, int Vp, __nv_bfloat16* o
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 
-int embedding_pos_bwd(const float* dx, int B, int T, int P, int D, void* dwpe, bool out_f32, cudaStream_t s) {
+int embedding_pos_bwd(const void* dx, bool dx_f32, int B, int T, int P, int D, void* dwpe, bool out_f32,
+                      cudaStream_t s) {
   const long total = static_cast<long>(P) * D;
-  launch_pdl(embed_bwd_pos_kernel, dim3(grid_for(total, 256)), dim3(256), 0, s, dx, B, T, P, D, dwpe, out_f32);
+  if (dx_f32)
+    launch_pdl(embed_bwd_pos_kernel<float>, dim3(grid_for(total, 256)), dim3(256), 0, s,
+               static_cast<const float*>(dx), B, T, P, D, dwpe, static_cast<int>(out_f32));
+  else
+    launch_pdl(embed_bwd_pos_kernel<__nv_bfloat16>, dim3(grid_for(total, 256)), dim3(256), 0, s,
+               static_cast<const __nv_bfloat16*>(dx), B, T, P, D, dwpe, static_cast<int>(out_f32));
   return cudaPeekAtLastError() == cudaSuccess ? 0 : 4;
 }
 

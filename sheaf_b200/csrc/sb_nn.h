@@ -22,11 +22,12 @@ int* device_error_word();
 // a following residual GEMM accumulates into (EPI_ACCUM).
 int layernorm_fwd(const void* x, bool x_f32, const void* gamma, bool gamma_f32, void* y, bool y_f32, float* mean,
                   float* rstd, int rows, int D, cudaStream_t s, void* x_copy = nullptr);
-// dres += LN-VJP(dy); dres_bf (optional) = bf16(dres); dgamma = sum_rows dy * xhat.
-// x f32 (x_f32) or bf16; a bf16 x takes a bf16 dy.
+// dres_out = dres_in + LN-VJP(dy) (dres_in null: zero; it may alias
+// dres_out); dgamma = sum_rows dy * xhat. x and the residual gradients are
+// f32 (x_f32) or bf16; a bf16 x takes a bf16 dy.
 size_t layernorm_bwd_workspace_bytes(int rows, int D);
 int layernorm_bwd(const void* dy, bool dy_f32, const void* x, bool x_f32, const float* mean, const float* rstd,
-                  const void* gamma, bool gamma_f32, float* dres, __nv_bfloat16* dres_bf, void* dgamma,
+                  const void* gamma, bool gamma_f32, const void* dres_in, void* dres_out, void* dgamma,
                   bool dgamma_f32, float* ws, int rows, int D, cudaStream_t s);
 
 // layernorm_bwd (f32 dy) with at most `max_blocks` blocks; `scratch` holds
@@ -46,7 +47,7 @@ int embedding_fwd(const float* ids, const void* wte, const void* wpe, bool f32, 
                   int V, int D, cudaStream_t s);
 // dwte = scatter-add of dx rows by id; dwpe[t] = sum_b dx[b,t] (rows >= T zero).
 size_t embedding_bwd_workspace_bytes(int V, int D);
-int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V, int D, void* dwte, void* dwpe,
+int embedding_bwd(const float* ids, const void* dx, bool dx_f32, int B, int T, int P, int V, int D, void* dwte, void* dwpe,
                   bool out_f32, float* ws, cudaStream_t s);
 
 // The embedding VJP in two parts, for a plan that computes dwte itself as
@@ -54,7 +55,8 @@ int embedding_bwd(const float* ids, const float* dx, int B, int T, int P, int V,
 // >= V zero; an id that is not exactly an integer in [0, V) has no class)
 // and dwpe alone.
 int embedding_onehot(const float* ids, int ntok, int V, int Vp, __nv_bfloat16* out, cudaStream_t s);
-int embedding_pos_bwd(const float* dx, int B, int T, int P, int D, void* dwpe, bool out_f32, cudaStream_t s);
+int embedding_pos_bwd(const void* dx, bool dx_f32, int B, int T, int P, int D, void* dwpe, bool out_f32,
+                      cudaStream_t s);
 
 int convert_f32_to_bf16(const float* in, __nv_bfloat16* out, long n, cudaStream_t s);
 // y = gelu(x) or, with bwd, y = g * gelu'(x), elementwise over n values.
