@@ -245,6 +245,9 @@ def cpu_sample(name: str, c, dtype: str, target_s: float = 15.0):
                         f"tokens, same model; BLAS on {cores} threads of {cpu_model()}")
 
 
+REF_BUDGET_S = 200.0  # host seconds the reference arm's timed steps may take
+
+
 def run_reference(args, world, rank):
     """Reference arm: the reference's own math on the host cores (the oracle
     port; the reference's IREE llvm-cpu path cannot be built here). Rank 0
@@ -258,8 +261,18 @@ def run_reference(args, world, rank):
     cc = dict(c, batch=batch)
     cfg = _oracle_cfg(cc)
     leaves, x, y = synthetic_inputs(0, cc)
-    for _ in range(min(args.warmup, 1)):
+    t0 = time.perf_counter()
+    for _ in range(max(1, min(args.warmup, 1))):
         models.gpt_value_and_grad(leaves, x, y, cfg, dtype=np.float32)
+    per_seq = (time.perf_counter() - t0) / batch
+    # Each step is the whole batch unless K such steps would take longer than
+    # REF_BUDGET_S: then the largest halving of it whose K steps fit.
+    while batch > 1 and batch % 2 == 0 and args.steps * per_seq * batch > REF_BUDGET_S:
+        batch //= 2
+    if batch != cc["batch"]:
+        cc = dict(c, batch=batch)
+        cfg = _oracle_cfg(cc)
+        x, y = x[:batch], y[:batch]
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()

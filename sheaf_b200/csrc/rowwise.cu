@@ -165,7 +165,9 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const TX* __restrict__ x, c
 // dx = rstd * (dxh - mean(dxh) - xhat * mean(dxh * xhat)), dxh = dy * gamma.
 // dres_out = dres_in + dx (the residual stream's gradient, in the type of x:
 // f32, or bf16 rounded once per add in a bf16 module; dres_in may be null
-// for zero, or alias dres_out); per-block partial sums of
+// for zero, or alias dres_out: every element is read once, by the thread
+// that then writes it, so the no-alias qualifiers only let loads of later
+// rows move ahead of stores to earlier ones); per-block partial sums of
 // dgamma = sum_rows dy * xhat into dgamma_part[blockIdx.x][D].
 // x, dy and dres of a row are loaded together (the dres read does not wait
 // for the row reductions); gamma is re-read from L1 per row to keep the
@@ -179,7 +181,7 @@ __global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(con
                                                         const float* __restrict__ mean_in,
                                                         const float* __restrict__ rstd_in,
                                                         const void* __restrict__ gamma, int gamma_f32,
-                                                        const TX* dres_in, TX* dres_out,
+                                                        const TX* __restrict__ dres_in, TX* __restrict__ dres_out,
                                                         float* __restrict__ dgamma_part, int rows, int D) {
   pdl_wait();
   pdl_trigger();
@@ -333,7 +335,7 @@ __global__ void __launch_bounds__(256) ln_bwd_wide_kernel(const TI* __restrict__
                                                           const float* __restrict__ mean_in,
                                                           const float* __restrict__ rstd_in,
                                                           const void* __restrict__ gamma, int gamma_f32,
-                                                          const TX* dres_in, TX* dres_out,
+                                                          const TX* __restrict__ dres_in, TX* __restrict__ dres_out,
                                                           float* __restrict__ dgamma_part, int rows, int D) {
   pdl_wait();
   pdl_trigger();
@@ -993,7 +995,7 @@ size_t layernorm_bwd_workspace_bytes(int rows, int D) {
 namespace {
 template <typename TI, typename TX>
 int layernorm_bwd_t(const TI* dy, const TX* x, const float* mean, const float* rstd, const void* gamma,
-                    bool gamma_f32, const TX* dres_in, TX* dres_out, void* dgamma, bool dgamma_f32, float* ws,
+                    bool gamma_f32, const TX* __restrict__ dres_in, TX* __restrict__ dres_out, void* dgamma, bool dgamma_f32, float* ws,
                     int rows, int D, cudaStream_t s) {
   if (D >= kLnWideMin) {
     const int nt = ln_wide_threads(D), grid = ln_wide_grid(rows);
