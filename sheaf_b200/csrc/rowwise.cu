@@ -164,8 +164,8 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const TX* __restrict__ x, c
 
 // dx = rstd * (dxh - mean(dxh) - xhat * mean(dxh * xhat)), dxh = dy * gamma.
 // dres_out = dres_in + dx (the residual stream's gradient, in the type of x:
-// f32, or bf16 rounded once per add in a bf16 module; dres_in may be null
-// for zero, or alias dres_out: every element is read once, by the thread
+// f32, or bf16 rounded once per add in a bf16 module; without ACC dres_in is
+// zero and not read; it may alias dres_out: every element is read once, by the thread
 // that then writes it, so the no-alias qualifiers only let loads of later
 // rows move ahead of stores to earlier ones); per-block partial sums of
 // dgamma = sum_rows dy * xhat into dgamma_part[blockIdx.x][D].
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const TX* __restrict__ x, c
 template <int VPT>
 constexpr int ln_bwd_warps() { return VPT <= 3 ? 24 : 8; }
 
-template <int VPT, typename TI, typename TX>
+template <int VPT, typename TI, typename TX, bool ACC>
 __global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(const TI* __restrict__ dy, const TX* __restrict__ x,
                                                         const float* __restrict__ mean_in,
                                                         const float* __restrict__ rstd_in,
@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(con
       const bool in = c < D;
       xh[j] = in ? load4(x + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
       dxh[j] = in ? load4(dy + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      r[j] = (in && dres_in) ? load4(dres_in + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      r[j] = (ACC && in) ? load4(dres_in + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(256) ln_fwd_wide_kernel(const TX* __restrict__
   }
 }
 
-template <int CPT, typename TI, typename TX>
+template <int CPT, typename TI, typename TX, bool ACC>
 __global__ void __launch_bounds__(256) ln_bwd_wide_kernel(const TI* __restrict__ dy, const TX* __restrict__ x,
                                                           const float* __restrict__ mean_in,
                                                           const float* __restrict__ rstd_in,
@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(256) ln_bwd_wide_kernel(const TI* __restrict__
       const bool in = c < D;
       xh[j] = in ? load4(x + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
       dxh[j] = in ? load4(dy + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      r[j] = (in && dres_in) ? load4(dres_in + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      r[j] = (ACC && in) ? load4(dres_in + off + c) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
@@ -999,8 +999,14 @@ int layernorm_bwd_t(const TI* dy, const TX* x, const float* mean, const float* r
                     int rows, int D, cudaStream_t s) {
   if (D >= kLnWideMin) {
     const int nt = ln_wide_threads(D), grid = ln_wide_grid(rows);
-    SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, TI, TX>), dim3(grid), dim3(nt), 0, s, dy,
-                                                    x, mean, rstd, gamma, gamma_f32, dres_in, dres_out, ws, rows, D)));
+    if (dres_in)
+      SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, TI, TX, true>), dim3(grid), dim3(nt), 0, s,
+                                                      dy, x, mean, rstd, gamma, gamma_f32, dres_in, dres_out, ws, rows,
+                                                      D)));
+    else
+      SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, TI, TX, false>), dim3(grid), dim3(nt), 0,
+                                                      s, dy, x, mean, rstd, gamma, gamma_f32, dres_in, dres_out, ws,
+                                                      rows, D)));
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
     return column_sum(ws, grid, D, dgamma, dgamma_f32, s);
   }
@@ -1009,7 +1015,7 @@ int layernorm_bwd_t(const TI* dy, const TX* x, const float* mean, const float* r
   const size_t smem = static_cast<size_t>(warps) * D * sizeof(float);
   if (smem > 200 * 1024) return 1;
   SB_LN_DISPATCH((D + 127) / 128, ({
-    auto k = ln_bwd_kernel<V, TI, TX>;
+    auto k = dres_in ? ln_bwd_kernel<V, TI, TX, true> : ln_bwd_kernel<V, TI, TX, false>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, dy, x, mean, rstd, gamma, gamma_f32, dres_in, dres_out, ws,
                rows, D);
@@ -1047,7 +1053,7 @@ int layernorm_bwd_capped(const float* dy, const float* x, const float* mean, con
   if (rows <= 0 || D <= 0 || (D & 3) || max_blocks <= 0) return 1;
   if (D >= kLnWideMin) {  // the kernel layernorm_bwd uses at this width, on fewer blocks
     const int nt = ln_wide_threads(D), grid = std::min(ln_wide_grid(rows), max_blocks);
-    SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, float, float>), dim3(grid), dim3(nt), 0, s, dy, x,
+    SB_LN_WIDE_DISPATCH(ln_wide_cpt(D), (launch_pdl((ln_bwd_wide_kernel<C, float, float, true>), dim3(grid), dim3(nt), 0, s, dy, x,
                                                     mean, rstd, gamma, gamma_f32, dres, dres, scratch, rows, D)));
     if (cudaPeekAtLastError() != cudaSuccess) return 4;
     return column_sum(scratch, grid, D, dgamma, dgamma_f32, s);
@@ -1057,7 +1063,7 @@ int layernorm_bwd_capped(const float* dy, const float* x, const float* mean, con
   const size_t smem = static_cast<size_t>(warps) * D * sizeof(float);
   if (smem > 200 * 1024) return 1;
   SB_LN_DISPATCH((D + 127) / 128, ({
-    auto k = ln_bwd_kernel<V, float, float>;
+    auto k = ln_bwd_kernel<V, float, float, true>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     launch_pdl(k, dim3(grid), dim3(warps * 32), smem, s, dy, x, mean, rstd, gamma, gamma_f32, dres, dres, scratch,
                rows, D);
