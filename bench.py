@@ -121,14 +121,22 @@ class ClockSampler:
         self.device = device
         self.proc = None
         self.lines: list[str] = []
+        self.start = 0  # samples taken before the timed region
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi takes a moment to start (longer with one per rank):
+            # wait for its first sample so that the timed region, tens of ms
+            # long, is sampled
+            t0 = time.perf_counter()
+            while not self.lines and self.proc.poll() is None and time.perf_counter() - t0 < 5.0:
+                time.sleep(0.005)
+            self.start = len(self.lines)
         except (FileNotFoundError, OSError):
             self.proc = None
         return self
@@ -148,7 +156,9 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        # the samples taken during the region, else the last one before it
+        lines = self.lines[self.start:] or self.lines[-1:]
+        for ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
