@@ -110,6 +110,10 @@ SB_API sb_status sb_buffer_h2d(sb_buffer* buffer, const void* host, size_t bytes
 SB_API sb_status sb_buffer_d2h(sb_buffer* buffer, void* host, size_t bytes, int64_t timeout_ns);
 SB_API void sb_buffer_retain(sb_buffer* buffer);
 SB_API void sb_buffer_release(sb_buffer* buffer);
+/* Releases buffers[0 .. n) (null entries skipped) in one call: for a host
+ * language whose foreign calls are costly, the outputs of a call it does not
+ * keep. No counterpart in the reference (its values are dropped by Rust). */
+SB_API void sb_buffer_release_many(sb_buffer* const* buffers, size_t n);
 SB_API size_t sb_buffer_rank(const sb_buffer* buffer);
 SB_API int64_t sb_buffer_dim(const sb_buffer* buffer, size_t axis);
 SB_API uint32_t sb_buffer_elem_type(const sb_buffer* buffer);

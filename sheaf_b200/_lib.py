@@ -99,6 +99,7 @@ SIGNATURES: dict[str, tuple] = {
     "sb_buffer_d2h": (_P, [_P, _P, C.c_size_t, C.c_int64]),
     "sb_buffer_retain": (None, [_P]),
     "sb_buffer_release": (None, [_P]),
+    "sb_buffer_release_many": (None, [_P, C.c_size_t]),
     "sb_buffer_rank": (C.c_size_t, [_P]),
     "sb_buffer_dim": (C.c_int64, [_P, C.c_size_t]),
     "sb_buffer_elem_type": (C.c_uint32, [_P]),

@@ -274,6 +274,11 @@ void sb_buffer_retain(sb_buffer* b) {
   if (b) b->refs.fetch_add(1);
 }
 void sb_buffer_release(sb_buffer* b) { buffer_release(b); }
+void sb_buffer_release_many(sb_buffer* const* bufs, size_t n) {
+  if (!bufs) return;
+  for (size_t i = 0; i < n; ++i)
+    if (bufs[i]) buffer_release(bufs[i]);
+}
 size_t sb_buffer_rank(const sb_buffer* b) { return b ? b->shape.size() : 0; }
 int64_t sb_buffer_dim(const sb_buffer* b, size_t axis) {
   return (b && axis < b->shape.size()) ? b->shape[axis] : -1;

@@ -220,12 +220,12 @@ class Session:
             raise SheafB200Error(3, f"get_batch failed ({rc})")
         return x, y
 
-    def call(self, qualified_name: str, inputs: Sequence["Buffer"], max_outputs: int = 1024) -> list["Buffer"]:
+    def call(self, qualified_name: str, inputs: Sequence["Buffer"], max_outputs: int = 1024) -> "Outputs":
         arr = (C.c_void_p * max(1, len(inputs)))(*[b._h for b in inputs])
         outs = (C.c_void_p * max_outputs)()
         n = C.c_size_t()
         _check(lib().sb_call(self._h, qualified_name.encode(), arr, len(inputs), outs, max_outputs, C.byref(n)))
-        return [Buffer(C.c_void_p(outs[i])) for i in range(n.value)]
+        return Outputs(outs, n.value)
 
 
 # ---- leaving a data-parallel group between steps -------------------------
@@ -295,16 +295,66 @@ def _nest_keys(flat: dict):
     return lists(root)
 
 
+class Outputs(Sequence):
+    """The buffers a call returned, in order (loss first, then the gradient
+    leaves, for a value_and_grad). An entry becomes a Buffer, which then owns
+    it, when first read; the entries never read are released together (one
+    foreign call) when the sequence is dropped."""
+
+    __slots__ = ("_arr", "_n", "_bufs")
+
+    def __init__(self, arr, n: int):
+        self._arr = arr
+        self._n = n
+        self._bufs: list = [None] * n
+
+    def __len__(self) -> int:
+        return self._n
+
+    def __getitem__(self, i):
+        if isinstance(i, slice):
+            return [self[j] for j in range(*i.indices(self._n))]
+        if i < 0:
+            i += self._n
+        if not 0 <= i < self._n:
+            raise IndexError(i)
+        b = self._bufs[i]
+        if b is None:
+            b = Buffer(C.c_void_p(self._arr[i]))
+            self._arr[i] = None
+            self._bufs[i] = b
+        return b
+
+    def release(self) -> None:
+        if self._arr is not None:
+            lib().sb_buffer_release_many(self._arr, self._n)
+            self._arr = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
 class Buffer:
     """A device buffer view (sb_buffer); released when garbage collected."""
 
     def __init__(self, handle):
         self._h = handle
+        self._meta = None  # (shape, elem, nbytes): fixed for a buffer's life
 
     def release(self) -> None:
         if self._h:
             lib().sb_buffer_release(self._h)
             self._h = None
+
+    def _info(self):
+        if self._meta is None:
+            L = lib()
+            shape = tuple(L.sb_buffer_dim(self._h, i) for i in range(L.sb_buffer_rank(self._h)))
+            self._meta = (shape, L.sb_buffer_elem_type(self._h), L.sb_buffer_byte_length(self._h))
+        return self._meta
 
     def __del__(self):
         try:
@@ -314,16 +364,15 @@ class Buffer:
 
     @property
     def shape(self) -> tuple[int, ...]:
-        L = lib()
-        return tuple(L.sb_buffer_dim(self._h, i) for i in range(L.sb_buffer_rank(self._h)))
+        return self._info()[0]
 
     @property
     def elem(self) -> int:
-        return lib().sb_buffer_elem_type(self._h)
+        return self._info()[1]
 
     @property
     def nbytes(self) -> int:
-        return lib().sb_buffer_byte_length(self._h)
+        return self._info()[2]
 
     @property
     def device_ptr(self) -> int:
