@@ -173,8 +173,10 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const TX* __restrict__ x, c
 // for the row reductions); gamma is re-read from L1 per row to keep the
 // register count low. Rows up to 384 wide run 24 warps per block, one block
 // per SM, so there is one dgamma partial row per SM.
+// Rows up to 768 wide run 12 warps per block (about 150 registers: one block
+// per SM, 12 warps instead of 8), wider ones 8.
 template <int VPT>
-constexpr int ln_bwd_warps() { return VPT <= 3 ? 24 : 8; }
+constexpr int ln_bwd_warps() { return VPT <= 3 ? 24 : VPT <= 6 ? 12 : 8; }
 
 template <int VPT, typename TI, typename TX, bool ACC>
 __global__ void __launch_bounds__(32 * ln_bwd_warps<VPT>(), 1) ln_bwd_kernel(const TI* __restrict__ dy, const TX* __restrict__ x,
@@ -985,7 +987,10 @@ int layernorm_fwd(const void* x, bool x_f32, const void* gamma, bool gamma_f32, 
 namespace {
 // Blocks of the layer-norm VJP: one per SM (fewer for short inputs).
 int ln_bwd_grid(int rows, int warps) { return std::max(1, std::min((rows + warps - 1) / warps, num_sms_cached())); }
-int ln_bwd_warps_for(int D) { return (D + 127) / 128 <= 3 ? 24 : 8; }
+int ln_bwd_warps_for(int D) {
+  const int vpt = (D + 127) / 128;
+  return vpt <= 3 ? 24 : vpt <= 6 ? 12 : 8;
+}
 }  // namespace
 
 size_t layernorm_bwd_workspace_bytes(int rows, int D) {
