@@ -241,7 +241,8 @@ class GptVagModule : public Module {
   // splits for every GEMM 2.304; the same with the 384 x 384 proj weight
   // gradient on 6 tiles x 18 splits (the CTA cap) 2.266-2.274, x 24 splits
   // 2.281; the CTA cap alone (pair tiles at 9-10 splits) 2.305; the
-  // full-GPU choice for every GEMM slower still. On GPT-2-small the CTA cap
+  // full-GPU choice for every GEMM slower still. With the bf16 residual
+  // stream: 2.107-2.109 at 108 CTAs, 2.118-2.119 at 132, 2.161-2.163 at 84. On GPT-2-small the CTA cap
   // puts the fc and fc2 weight gradients (36 pair tiles each) on one split
   // instead of two: 9.26-9.30 -> 9.00-9.08 ms/step.
   static constexpr int kSideCtas = 108;
